@@ -1,0 +1,217 @@
+"""Generate the golden fixtures in this directory from the REFERENCE implementation.
+
+Runs the reference repository's own Triton kernels on the CPU through the Triton interpreter
+(``TRITON_INTERPRET=1``) on small seeded inputs and stores inputs + outputs as ``.npz``.  The
+reference is imported read-only from ``--ref`` (default ``/root/reference``); it is NOT needed
+at test time -- the committed fixtures are.
+
+Intermediate tensors (Kernel A's votes / wvotes / bits, and the selection outputs) are captured
+by wrapping the reference module's host selection function for the duration of one call.
+
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+os.environ.setdefault("TRITON_INTERPRET", "1")
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(REPO, "sparse-thresholded-attention_b200"))
+
+from sta.synth import SynthSpec, make_inputs, rope_inv_freq, yarn_inv_freq  # noqa: E402
+
+
+def _np(x):
+    if isinstance(x, torch.Tensor):
+        if x.dtype == torch.bfloat16:
+            x = x.float()
+        return x.detach().cpu().numpy()
+    return np.asarray(x)
+
+
+class Capture:
+    """Wrap ``module.<name>`` so that its inputs and outputs are recorded."""
+
+    def __init__(self, module, name):
+        self.module, self.name = module, name
+        self.orig = getattr(module, name)
+        self.args = self.kwargs = self.result = None
+
+    def __enter__(self):
+        def wrapped(*args, **kwargs):
+            self.args, self.kwargs = args, kwargs
+            self.result = self.orig(*args, **kwargs)
+            return self.result
+        setattr(self.module, self.name, wrapped)
+        return self
+
+    def __exit__(self, *exc):
+        setattr(self.module, self.name, self.orig)
+
+
+def inputs(H, N, D, seed, dtype, planted=8, Hkv=None):
+    spec = SynthSpec(batch=1, n_heads=H, n_kv_heads=Hkv or H, seq_len=N, head_dim=D,
+                     n_planted=planted, n_planted_queries=16, seed=seed, dtype=dtype)
+    q, k, v = make_inputs(spec)
+    return q, k, v
+
+
+def save(name, meta, arrays):
+    path = os.path.join(HERE, name + ".npz")
+    out = {k: _np(v) for k, v in arrays.items()}
+    for k, v in list(out.items()):
+        if v.dtype == np.int64:
+            out[k] = v.astype(np.int32)
+        if v.dtype == np.bool_:
+            out[k] = v.astype(np.uint8)
+    np.savez_compressed(path, meta=np.array(json.dumps(meta)), **out)
+    print("wrote", path, {k: v.shape for k, v in out.items()})
+
+
+def gen_shared(ref, mod_name, case, H, N, D, T, k_max, seed, dtype, select_score="freq",
+               geom="pi", pos_scale=1.0, tau_val=5.0, pct=30.0, measure=False, block_n=64,
+               block_k=64, n_global=32, n_local=32, planted=8):
+    mod = __import__(mod_name)
+    q, k, v = inputs(H, N, D, seed, dtype, planted=planted)
+    tau = torch.full((H,), float(tau_val))
+    meta = dict(kind="shared", module=mod_name, H=H, N=N, D=D, T=T, k_max=k_max, seed=seed,
+                dtype=str(dtype).replace("torch.", ""), select_score=select_score, geom=geom,
+                pct=pct, measure=measure, block_n=block_n, block_k=block_k,
+                n_global=n_global, n_local=n_local)
+    if geom == "hybrid":
+        invf_a, att = yarn_inv_freq(D, 5e5, 4.0, 256)
+        invf_c = rope_inv_freq(D, 1e4)
+        meta.update(pos_scale_a=1.0, rope_scale_a=att, pos_scale_c=pos_scale, rope_scale_c=1.0)
+        with Capture(mod, "_build_sets") as cap:
+            res = mod.shared_pi_attention(q, k, v, tau, invf_a, 1.0, att, invf_c, pos_scale, 1.0,
+                                          pct=pct, n_global=n_global, n_local=n_local, tile=T,
+                                          k_max=k_max, block_n=block_n, block_k=block_k,
+                                          measure=measure, select_score=select_score)
+    else:
+        if geom == "yarn":
+            invf, att = yarn_inv_freq(D, 5e5, 4.0, 256)
+            rs, ps = att, 1.0
+        else:
+            invf, rs, ps = rope_inv_freq(D, 1e4), 1.0, pos_scale
+        invf_a = invf_c = invf
+        meta.update(pos_scale_a=ps, rope_scale_a=rs, pos_scale_c=ps, rope_scale_c=rs)
+        kw = dict(pos_scale=ps, pct=pct, rope_scale=rs, n_global=n_global, n_local=n_local,
+                  tile=T, k_max=k_max, block_n=block_n, block_k=block_k, measure=measure)
+        if mod_name != "shared_selection_triton_exact":
+            kw["select_score"] = select_score
+        with Capture(mod, "_build_sets") as cap:
+            res = mod.shared_pi_attention(q, k, v, tau, invf, **kw)
+    votes = cap.args[0]
+    wvotes = cap.kwargs.get("wvotes")
+    sets = cap.result
+    arrays = dict(q=q[0], k=k[0], v=v[0], tau=tau, inv_freq_a=invf_a, inv_freq_c=invf_c,
+                  out=res[0][0], shared_size=res[1], kept_size=res[2], kpct=res[3],
+                  overflow=res[4], kpct_meas=res[5], overflow20=res[6], votes=votes,
+                  idx=sets[0], newpos_k=sets[1], newpos_q=sets[2])
+    if wvotes is not None and wvotes.shape[-1] == N:
+        arrays["wvotes"] = wvotes
+    save(case, meta, arrays)
+
+
+def gen_pq(case, H, N, D, k_max, seed, dtype, select_score="expmass", geom="pi",
+           pos_scale=1.0, tau_val=5.0, planted=8):
+    mod = __import__("shared_selection_triton_perquery")
+    q, k, v = inputs(H, N, D, seed, dtype, planted=planted)
+    tau = torch.full((H,), float(tau_val))
+    invf_c = rope_inv_freq(D, 1e4)
+    if geom == "yarn":
+        invf_a, rs = yarn_inv_freq(D, 5e5, 4.0, 256)
+        ps = 1.0
+    else:
+        invf_a, rs, ps = invf_c, 1.0, pos_scale
+    meta = dict(kind="pq", H=H, N=N, D=D, T=32, k_max=k_max, seed=seed,
+                dtype=str(dtype).replace("torch.", ""), select_score=select_score, geom=geom,
+                pos_scale_a=ps, rope_scale_a=rs, n_global=32, n_local=32, block_k=64)
+    with Capture(mod, "_build_sets_pq") as cap:
+        res = mod.shared_pq_attention(q, k, v, tau, invf_a, invf_c, pos_scale_a=ps,
+                                      rope_scale_a=rs, k_max=k_max, select_score=select_score)
+    golden = mod.pq_attention_torch(q, k, v, tau, invf_a, invf_c, pos_scale_a=ps,
+                                    rope_scale_a=rs, k_max=k_max, select_score=select_score)
+    votes, bits, wvotes = cap.args[0], cap.args[1], cap.args[2]
+    sets = cap.result
+    arrays = dict(q=q[0], k=k[0], v=v[0], tau=tau, inv_freq_a=invf_a, inv_freq_c=invf_c,
+                  out=res[0][0], out_torch_golden=golden[0], usize=res[1], kept_size=res[2],
+                  overflow=res[3], votes=votes, bits=bits.view(torch.int32), idx=sets[0],
+                  newpos_k=sets[1], newpos_q=sets[2], mask=sets[3])
+    if wvotes.shape[-1] == N:
+        arrays["wvotes"] = wvotes
+    save(case, meta, arrays)
+
+
+def gen_pqstream(case, H, N, D, seed, dtype, block_n=32, pos_advance="max", use_skip=True,
+                 geom="pi", pos_scale=1.0, tau_val=5.0, planted=8):
+    mod = __import__("pqstream_kernel")
+    q, k, v = inputs(H, N, D, seed, dtype, planted=planted)
+    tau = torch.full((H,), float(tau_val))
+    invf_c = rope_inv_freq(D, 1e4)
+    if geom == "yarn":
+        invf_a, rs = yarn_inv_freq(D, 5e5, 4.0, 256)
+        ps = 1.0
+    else:
+        invf_a, rs, ps = invf_c, 1.0, pos_scale
+    meta = dict(kind="pqstream", H=H, N=N, D=D, T=32, seed=seed,
+                dtype=str(dtype).replace("torch.", ""), geom=geom, pos_scale_a=ps,
+                rope_scale_a=rs, n_global=32, n_local=32, block_n=block_n,
+                pos_advance=pos_advance, use_skip=use_skip, tau=tau_val)
+    out, span, kept, blocks, skipped = mod.pqstream_attention(
+        q, k, v, tau, invf_a, invf_c, pos_scale_a=ps, rope_scale_a=rs, block_n=block_n,
+        pos_advance=pos_advance, use_skip=use_skip)
+    golden = mod.pqstream_attention_torch(q, k, v, tau, invf_a, invf_c, pos_scale_a=ps,
+                                          rope_scale_a=rs, block_n=block_n,
+                                          pos_advance=pos_advance)
+    save(case, meta, dict(q=q[0], k=k[0], v=v[0], tau=tau, inv_freq_a=invf_a,
+                          inv_freq_c=invf_c, out=out[0], out_torch_golden=golden[0], span=span,
+                          kept=kept, blocks=blocks, skipped=skipped))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    args = ap.parse_args()
+    sys.path.insert(0, args.ref)
+    torch.set_num_threads(os.cpu_count() or 1)
+    # fp32 only: the Triton interpreter does not evaluate bf16 arithmetic faithfully (numpy has
+    # no bf16; its bf16 outputs come back as ~1e10 garbage), so bf16 parity is anchored on the
+    # fp32-pinned oracle instead.
+    f32 = torch.float32
+    # shared path: PI freq, ragged N, small k_max to drive the 30->25->20 fallback + truncation
+    gen_shared(None, "shared_selection_triton_exact_2", "shared_pi_freq_f32", 2, 300, 64, 64, 160,
+               11, f32, pos_scale=0.5, measure=True)
+    gen_shared(None, "shared_selection_triton_exact", "shared_exact_sort_f32", 2, 256, 64, 32, 96,
+               12, f32, pos_scale=0.75)
+    gen_shared(None, "shared_selection_triton_exact_2", "shared_pi_margin_f32", 2, 320, 64, 64,
+               200, 13, f32, select_score="margin", pos_scale=0.5)
+    gen_shared(None, "shared_selection_triton_exact_2", "shared_pi_expmass_f32", 2, 320, 64, 64,
+               200, 14, f32, select_score="expmass", pos_scale=0.5)
+    gen_shared(None, "shared_selection_triton_YaRN_exact", "shared_yarn_freq_f32", 2, 288, 64, 32,
+               128, 15, f32, geom="yarn")
+    gen_shared(None, "shared_selection_triton_hybrid_exact", "shared_hybrid_expmass_f32", 2, 288,
+               64, 32, 128, 16, f32, geom="hybrid", pos_scale=0.5, select_score="expmass")
+    gen_shared(None, "shared_selection_triton_exact_2", "shared_pi_freq_tau1_f32", 2, 256, 64, 64,
+               2048, 18, f32, tau_val=1.0)
+    # PQ-Union: overflow-forcing k_max, expmass and freq ranking, yarn select geometry
+    gen_pq("pq_union_expmass_f32", 2, 288, 64, 160, 21, f32)
+    gen_pq("pq_union_freq_f32", 2, 256, 64, 4096, 22, f32, select_score="freq")
+    gen_pq("pq_union_yarn_f32", 2, 256, 64, 128, 23, f32, geom="yarn")
+    # PQ-Stream: max / full advance, skip on/off, ragged N, BN 32 and 64
+    gen_pqstream("pqstream_max_f32", 2, 300, 64, 31, f32)
+    gen_pqstream("pqstream_full_f32", 2, 256, 64, 32, f32, pos_advance="full")
+    gen_pqstream("pqstream_bn64_f32", 2, 288, 64, 33, f32, block_n=64, geom="yarn")
+    gen_pqstream("pqstream_noskip_f32", 2, 256, 64, 34, f32, use_skip=False, pos_scale=0.5)
+
+
+if __name__ == "__main__":
+    main()
