@@ -1,0 +1,293 @@
+/*
+ * sta.h -- C ABI of the B200 (sm_100a) thresholded-attention prefill library (libsta.so).
+ *
+ * Plain pointers and sizes only: every pointer is a CUDA device pointer unless stated
+ * otherwise, every stride is in ELEMENTS, the last (head_dim) dimension of every tensor is
+ * contiguous.  `stream` is a cudaStream_t passed as void*.  Every entry point returns an int
+ * status (STA_OK == 0); no C++ exception crosses this boundary.  sta_last_error() returns a
+ * static description of the most recent failure of the calling thread.
+ *
+ * Tensor conventions follow the reference's call surfaces (Vihaan-Thaker/
+ * Sparse-Thresholded-Attention): q (batch*n_heads, n, d), k / v (batch*n_kv_heads, n, d)
+ * (GQA-native: q head h of batch b reads kv head b*n_kv_heads + h / (n_heads / n_kv_heads);
+ * the reference instead receives repeat_kv-expanded k/v, which is n_kv_heads == n_heads).
+ * Batch 1 is the reference's only case (assert Z == 1, shared_selection_triton_exact_2.py:444).
+ *
+ * Per-(head, tile) selection arrays (votes, wvotes, bits) are stored COMPACT: tile t of a
+ * head holds only its causal keys j < hi_t = min((t+1)*tile, n), at offset
+ * tile*t*(t+1)/2 inside the head, heads sta_tri_head_stride(n, tile) apart.
+ */
+#ifndef STA_H_
+#define STA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define STA_OK 0
+#define STA_ERR_ARG 1          /* bad argument (null pointer, inconsistent sizes)           */
+#define STA_ERR_UNSUPPORTED 2  /* shape / option this build does not support                */
+#define STA_ERR_CUDA 3         /* a CUDA runtime call or launch failed                      */
+#define STA_ERR_TIMEOUT 4      /* a bounded device-side wait expired (kernel unwound)       */
+#define STA_ERR_WORKSPACE 5    /* workspace too small                                       */
+
+#define STA_DTYPE_F32 0
+#define STA_DTYPE_BF16 1
+
+#define STA_SCORE_FREQ 0     /* rank by vote frequency                   */
+#define STA_SCORE_MARGIN 1   /* rank by summed margin s - (m - tau)      */
+#define STA_SCORE_EXPMASS 2  /* rank by summed exp(s - m)                */
+
+#define STA_ADV_MAX 0        /* PQ-Stream: d += max_i c_i                 */
+#define STA_ADV_FULL 1       /* PQ-Stream: d += slots the block occupies  */
+
+/* ---------------------------------------------------------------------------------------
+ * Library
+ * ------------------------------------------------------------------------------------- */
+const char* sta_last_error(void);
+int sta_version(void);
+/* Number of elements of one head of a compact selection array. */
+int64_t sta_tri_head_stride(int64_t n, int32_t tile);
+
+/* ---------------------------------------------------------------------------------------
+ * Stage 0 -- RoPE prologue of the selection geometry.
+ * Rotates raw rows (heads, n, d) at position float(i) * pos_scale with (inv_freq, rope_scale)
+ * and writes the fp32 result split into two bf16 tensors hi + lo (heads, n, d), contiguous.
+ * Replaces the per-block rotations inside Kernel A (shared_selection_triton_exact_2.py:79-104).
+ * ------------------------------------------------------------------------------------- */
+int sta_rope_split(const void* x, int32_t dtype, int64_t heads, int64_t n, int32_t d,
+                   int64_t stride_h, int64_t stride_n, const float* inv_freq, float pos_scale,
+                   float rope_scale, void* out_hi, void* out_lo, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Stage 1 -- exact-max two-pass selection on tcgen05 tensor cores (Kernel A).
+ * Replaces _select_vote_kernel (shared_selection_triton_exact_2.py:50-140) and
+ * _select_bits_kernel (shared_selection_triton_perquery.py:119-218).
+ * ------------------------------------------------------------------------------------- */
+typedef struct sta_select_args {
+  const void* q_hi;        /* bf16 (batch*n_heads, n, d) rotated queries, hi part */
+  const void* q_lo;        /*                                           lo part */
+  const void* k_hi;        /* bf16 (batch*n_kv_heads, n, d) rotated keys */
+  const void* k_lo;
+  int64_t batch;
+  int64_t n_heads;
+  int64_t n_kv_heads;
+  int64_t n;
+  int32_t d;               /* 64 or 128 */
+  int32_t tile;            /* 32, 64 or 128 */
+  float sm_scale;
+  int32_t wmode;           /* STA_SCORE_*: 0 = no weighted votes */
+  const float* tau;        /* (n_heads,) threshold per q head */
+  int32_t max_only;        /* 1: pass 1 only (row max), no votes */
+  uint8_t* votes;          /* compact (batch*n_heads heads), or NULL */
+  float* wvotes;           /* compact, required when wmode != 0 */
+  uint32_t* bits;          /* compact per-query keep bits (tile == 32 only), or NULL */
+  float* row_max;          /* (batch*n_heads, n) exact row max, or NULL */
+  int32_t* row_count;      /* (batch*n_heads, n) kept keys per query, or NULL */
+} sta_select_args;
+
+int sta_select(const sta_select_args* a, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Stage 2 -- device selection of the shared path (top pct% of the pooled set with the
+ * 30 -> 25 -> 20 fallback, forced global/local keys, PI repositioning, compaction).
+ * Replaces _build_sets (shared_selection_triton_exact_2.py:277-426; exact.py:253-370).
+ * ------------------------------------------------------------------------------------- */
+typedef struct sta_build_args {
+  const uint8_t* votes;    /* compact */
+  const float* wvotes;     /* compact, used when select_score != FREQ */
+  int64_t heads;           /* batch*n_heads */
+  int64_t n;
+  int32_t tile;
+  int32_t k_max;
+  int32_t n_global;
+  int32_t n_local;
+  float pct;
+  float pos_scale;         /* PI compression of the attend geometry */
+  int32_t select_score;    /* STA_SCORE_* */
+  int32_t measure;         /* 1: refine kpct_meas below the floor percentage */
+  int32_t* idx;            /* (heads, nt, k_max) kept key positions ascending, sentinel n */
+  float* newpos_k;         /* (heads, nt, k_max) */
+  float* newpos_q;         /* (heads, nt, tile) */
+  int32_t* shared_size;    /* (heads, nt) */
+  int32_t* kept_size;      /* (heads, nt) */
+  int32_t* chosen;         /* (heads, nt) percentage that fit, 0 if none */
+  uint8_t* overflow;       /* (heads, nt) top-pct set exceeded k_max */
+  int32_t* kpct_meas;      /* (heads, nt) */
+  uint8_t* overflow20;     /* (heads, nt) still over k_max at the floor percentage */
+} sta_build_args;
+
+int sta_build_sets(const sta_build_args* a, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Stage 2' -- PQ-Union selection: full union + forced, expmass (or freq) truncation of last
+ * resort, dense ranks, per-slot query bitmask.
+ * Replaces _build_sets_pq (shared_selection_triton_perquery.py:363-453).  Ties at the
+ * truncation cut keep the lowest key indices.
+ * ------------------------------------------------------------------------------------- */
+typedef struct sta_build_pq_args {
+  const uint8_t* votes;
+  const float* wvotes;
+  const uint32_t* bits;
+  int64_t heads;
+  int64_t n;
+  int32_t tile;            /* 32 */
+  int32_t k_max;
+  int32_t n_global;
+  int32_t n_local;
+  int32_t select_score;
+  int32_t* idx;
+  float* newpos_k;
+  float* newpos_q;
+  int32_t* mask;           /* (heads, nt, k_max) bit i = query row i attends; forced = -1 */
+  int32_t* usize;
+  int32_t* kept_size;
+  uint8_t* overflow;
+} sta_build_pq_args;
+
+int sta_build_sets_pq(const sta_build_pq_args* a, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Stage 3 -- gather + repositioned attention over the selected slots (Kernel C / C').
+ * Replaces _gather_attn_kernel (shared_selection_triton_exact_2.py:146-225) and
+ * _gather_attn_pq_kernel (shared_selection_triton_perquery.py:226-312).
+ * ------------------------------------------------------------------------------------- */
+typedef struct sta_attend_args {
+  const void* q; int64_t q_stride_h; int64_t q_stride_n;   /* raw (batch*n_heads, n, d) */
+  const void* k; int64_t k_stride_h; int64_t k_stride_n;   /* raw (batch*n_kv_heads, n, d) */
+  const void* v; int64_t v_stride_h; int64_t v_stride_n;
+  void* out;               /* (batch*n_heads, n, d) contiguous, dtype */
+  int32_t dtype;
+  int64_t batch;
+  int64_t n_heads;
+  int64_t n_kv_heads;
+  int64_t n;
+  int32_t d;
+  int32_t tile;            /* 32 or 64 */
+  int32_t k_max;
+  const int32_t* idx;
+  const float* newpos_k;
+  const float* newpos_q;
+  const int32_t* mask;     /* NULL: every query attends every valid slot */
+  const int32_t* kept_size;/* (heads, nt) or NULL: bounds the slot loop (result unchanged) */
+  const float* inv_freq;   /* attend geometry */
+  float rope_scale;
+  float sm_scale;
+} sta_attend_args;
+
+int sta_gather_attend(const sta_attend_args* a, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * PQ-Stream pass 2 (fused select + streamed positions + attend, descending key blocks).
+ * Together with sta_select(max_only=1) this replaces _pqstream_kernel
+ * (pqstream_kernel.py:174-368).
+ * ------------------------------------------------------------------------------------- */
+typedef struct sta_pqstream_args {
+  const void* q; int64_t q_stride_h; int64_t q_stride_n;
+  const void* k; int64_t k_stride_h; int64_t k_stride_n;
+  const void* v; int64_t v_stride_h; int64_t v_stride_n;
+  void* out;
+  int32_t dtype;
+  int64_t batch;
+  int64_t n_heads;
+  int64_t n_kv_heads;
+  int64_t n;
+  int32_t d;
+  int32_t tile;            /* 32 */
+  int32_t block_n;         /* 32 or 64 */
+  const void* q_hi; const void* q_lo; const void* k_hi; const void* k_lo;  /* select geometry */
+  const float* row_max;    /* (batch*n_heads, n) from sta_select(max_only=1) */
+  const float* tau;        /* (n_heads,) */
+  int32_t n_global;
+  int32_t n_local;
+  const float* inv_freq_c; /* attend geometry: base RoPE, rope_scale 1 */
+  float sm_scale;
+  int32_t pos_advance;     /* STA_ADV_* */
+  int32_t use_skip;
+  float* span;             /* (heads, nt) */
+  int32_t* kept;           /* (heads, n) */
+  float* blocks;           /* (heads, nt) */
+  float* skipped;          /* (heads, nt) */
+} sta_pqstream_args;
+
+int sta_pqstream_attend(const sta_pqstream_args* a, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Orchestrators: the whole prefill op in one call (replaces shared_pi_attention of
+ * shared_selection_triton_exact_2.py:432-486 / YaRN:442-496 / hybrid:450-510,
+ * shared_pq_attention of shared_selection_triton_perquery.py:459-525 and
+ * pqstream_attention of pqstream_kernel.py:498-564).  Scratch comes from `workspace`
+ * (device memory, >= the size the matching *_workspace_bytes call reports).
+ * ------------------------------------------------------------------------------------- */
+typedef struct sta_forward_args {
+  /* inputs */
+  const void* q; int64_t q_stride_h; int64_t q_stride_n;
+  const void* k; int64_t k_stride_h; int64_t k_stride_n;
+  const void* v; int64_t v_stride_h; int64_t v_stride_n;
+  void* out;
+  int32_t dtype;
+  int64_t batch;
+  int64_t n_heads;
+  int64_t n_kv_heads;
+  int64_t n;
+  int32_t d;
+  const float* tau;                 /* (n_heads,) */
+  /* selection geometry (Kernel A) */
+  const float* inv_freq_a; float pos_scale_a; float rope_scale_a;
+  /* attend geometry (selection repositioning + Kernel C) */
+  const float* inv_freq_c; float pos_scale_c; float rope_scale_c;
+  float sm_scale;
+  float pct;
+  int32_t n_global;
+  int32_t n_local;
+  int32_t tile;
+  int32_t k_max;
+  int32_t select_score;
+  int32_t measure;
+  int32_t block_n;                  /* PQ-Stream key block */
+  int32_t pos_advance;              /* PQ-Stream */
+  int32_t use_skip;                 /* PQ-Stream */
+  /* per-(head, tile) statistics (shared: shared_size, kept_size, chosen, overflow,
+   * kpct_meas, overflow20; PQ-Union: usize -> shared_size, kept_size, overflow;
+   * PQ-Stream: span, kept, blocks, skipped) */
+  int32_t* shared_size;
+  int32_t* kept_size;
+  int32_t* chosen;
+  uint8_t* overflow;
+  int32_t* kpct_meas;
+  uint8_t* overflow20;
+  float* span;
+  int32_t* kept_rows;
+  float* blocks;
+  float* skipped;
+  /* optional copies of the intermediates (NULL = keep them in the workspace only) */
+  int32_t* idx_out;
+  float* newpos_k_out;
+  float* newpos_q_out;
+  int32_t* mask_out;
+  /* scratch cap: the op runs over groups of kv heads so that its workspace stays below this
+   * many bytes (0 = one group holding every kv head) */
+  int64_t max_workspace_bytes;
+} sta_forward_args;
+
+size_t sta_shared_workspace_bytes(const sta_forward_args* a);
+int sta_shared_forward(const sta_forward_args* a, void* workspace, size_t workspace_bytes,
+                       void* stream);
+size_t sta_pq_union_workspace_bytes(const sta_forward_args* a);
+int sta_pq_union_forward(const sta_forward_args* a, void* workspace, size_t workspace_bytes,
+                         void* stream);
+size_t sta_pq_stream_workspace_bytes(const sta_forward_args* a);
+int sta_pq_stream_forward(const sta_forward_args* a, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* Error flag of the last bounded device wait on this device: 0 = none. */
+int sta_device_error(void* stream, int32_t* code_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STA_H_ */

@@ -1,0 +1,78 @@
+// RoPE prologue of the selection geometry: rotate raw Q or K rows at their (scaled) positions
+// and store the fp32 result as a (hi, lo) pair of bf16 tensors, the operand format of the
+// 3xBF16 tensor-core score products.
+//
+// Reference behaviour (shared_selection_triton_exact_2.py:79-86 for Q, :97-104 for K): the
+// reference re-derives RoPE(K) for every (query tile, key block) pair in both passes, i.e.
+// O(N^2 D) trigonometry.  The selection geometry does not depend on the query tile, so here
+// every row is rotated exactly once (O(N D)) and the passes become plain contractions.
+#include "common.cuh"
+#include "sta_internal.h"
+
+namespace sta {
+
+template <typename T>
+__device__ __forceinline__ float load_f(const T* p);
+template <>
+__device__ __forceinline__ float load_f<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float load_f<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat162float(*p);
+}
+
+// One thread per (row, frequency pair).  x is (rows = heads*N, D) with element strides
+// (stride_h, stride_n); last dim contiguous.  Position of row n is float(n) * pos_scale.
+template <typename T>
+__global__ void rope_split_kernel(const T* __restrict__ x, int64_t heads, int64_t N, int D,
+                                  int64_t stride_h, int64_t stride_n,
+                                  const float* __restrict__ inv_freq, float pos_scale,
+                                  float rope_scale, __nv_bfloat16* __restrict__ hi,
+                                  __nv_bfloat16* __restrict__ lo) {
+  const int half = D >> 1;
+  const int64_t total = heads * N * half;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int f = (int)(i % half);
+    const int64_t row = i / half;
+    const int64_t n = row % N;
+    const int64_t h = row / N;
+    const T* src = x + h * stride_h + n * stride_n;
+    const float x1 = load_f(src + f);
+    const float x2 = load_f(src + f + half);
+    const float ang = __fmul_rn(__fmul_rn((float)n, pos_scale), __ldg(inv_freq + f));
+    float r1, r2;
+    rope_pair(x1, x2, ang, rope_scale, r1, r2);
+    __nv_bfloat16 h1, l1, h2, l2;
+    split_bf16(r1, h1, l1);
+    split_bf16(r2, h2, l2);
+    const int64_t o = row * D;
+    hi[o + f] = h1;
+    lo[o + f] = l1;
+    hi[o + f + half] = h2;
+    lo[o + f + half] = l2;
+  }
+}
+
+int launch_rope_split(const void* x, int dtype, int64_t heads, int64_t N, int D,
+                      int64_t stride_h, int64_t stride_n, const float* inv_freq,
+                      float pos_scale, float rope_scale, void* hi, void* lo,
+                      cudaStream_t stream) {
+  const int64_t total = heads * N * (D / 2);
+  if (total == 0) return 0;
+  const int threads = 256;
+  int64_t blocks = (total + threads - 1) / threads;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (dtype == STA_DTYPE_F32) {
+    rope_split_kernel<float><<<(unsigned)blocks, threads, 0, stream>>>(
+        static_cast<const float*>(x), heads, N, D, stride_h, stride_n, inv_freq, pos_scale,
+        rope_scale, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo));
+  } else {
+    rope_split_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x), heads, N, D, stride_h, stride_n, inv_freq,
+        pos_scale, rope_scale, static_cast<__nv_bfloat16*>(hi),
+        static_cast<__nv_bfloat16*>(lo));
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : STA_ERR_CUDA;
+}
+
+}  // namespace sta

@@ -1,0 +1,429 @@
+// Exact-max two-pass selection (Kernel A) on 5th-generation tensor cores.
+//
+// Reference: _select_vote_kernel, shared_selection_triton_exact_2.py:50-140 (votes, row
+// counts, margin / expmass weighted votes) and _select_bits_kernel,
+// shared_selection_triton_perquery.py:119-218 (packed per-query keep bits, tile 32).
+//
+// Work item: 128 consecutive query rows of one q head (query block qb), against all causal
+// key blocks [0, (qb+1)*128).  Pass 1 sweeps the blocks for the exact row max m_i; pass 2
+// sweeps them again and evaluates keep = s >= m_i - tau_h & causal & row < N per (query, key).
+//
+// Scores are s = (Qr . Kr) * sm_scale with Qr / Kr the fp32 rotated rows, formed as three
+// bf16 tcgen05 products (hi*hi + hi*lo + lo*hi, fp32 accumulation in TMEM); both passes issue
+// the identical instruction sequence, so pass 2 reproduces pass 1's scores bit for bit.
+//
+// Roles (192 threads, one CTA per SM, persistent over a longest-first static schedule):
+//   warps 0-3  epilogue: thread r owns accumulator row r (TMEM lane r); row max in pass 1;
+//              keep / warp-ballot votes / per-query bits / weighted votes in pass 2;
+//   warp 4     TMA producer (Q tile once per item, K blocks through an NSTAGE smem ring);
+//   warp 5     MMA issuer (one thread), 4 TMEM accumulator slots of 128 columns.
+// All waits are bounded; on expiry the kernel records STA_ERR_TIMEOUT and unwinds.
+#include "common.cuh"
+#include "sta_internal.h"
+
+namespace sta {
+
+namespace {
+
+constexpr int BM = 128;       // query rows per item == TMEM lanes
+constexpr int BN = 128;       // keys per block == MMA N
+constexpr int NACC = 4;       // accumulator slots (4 x 128 fp32 columns = all 512 TMEM columns)
+constexpr int kThreads = 192;
+constexpr int kTileBytes = 128 * 128;  // 128 rows x 64 bf16 (one 128-byte swizzle chunk)
+
+template <int D>
+struct Cfg {
+  static constexpr int NC = D / 64;
+  static constexpr int Q_BYTES = 2 * NC * kTileBytes;
+  static constexpr int STAGE_BYTES = 2 * NC * kTileBytes;
+  static constexpr int NSTAGE = (D == 64) ? 4 : 2;
+  static constexpr int RED_WORDS = 2 * 4 * 128;  // [buffer][quadrant][column]
+  static constexpr int SMEM = 1024 + Q_BYTES + NSTAGE * STAGE_BYTES + 3 * RED_WORDS * 4 + 512;
+};
+
+struct Params {
+  int64_t BH;
+  int H, Hkv;
+  int64_t N;
+  int T;
+  int nqb;
+  int npass;
+  int wmode;
+  float sm_scale;
+  const float* tau;
+  uint8_t* votes;
+  float* wvotes;
+  uint32_t* bits;
+  float* row_max;
+  int32_t* row_count;
+  int* err;
+  int64_t head_stride;  // compact per-head stride
+};
+
+// lane l receives sum over the warp's lanes of v[l] (fixed butterfly order, 31 shuffles)
+__device__ __forceinline__ float transpose_reduce32(float (&v)[32]) {
+  const int l = lane_id();
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool up = (l & s) != 0;
+#pragma unroll
+    for (int i = 0; i < s; ++i) {
+      const float send = up ? v[i] : v[i + s];
+      const float keep = up ? v[i + s] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  return v[0];
+}
+
+__device__ __forceinline__ void decode_item(int64_t w, const Params& p, int64_t& bh, int& qb,
+                                            int64_t& kvh) {
+  qb = p.nqb - 1 - (int)(w / p.BH);
+  bh = w % p.BH;
+  const int G = p.H / p.Hkv;
+  kvh = (bh / p.H) * p.Hkv + (bh % p.H) / G;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
+              const __grid_constant__ CUtensorMap tm_khi, const __grid_constant__ CUtensorMap tm_klo,
+              const Params p) {
+  using C = Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sQ = base;
+  uint8_t* sK = base + C::Q_BYTES;
+  uint32_t* s_vote = reinterpret_cast<uint32_t*>(sK + C::NSTAGE * C::STAGE_BYTES);
+  float* s_w = reinterpret_cast<float*>(s_vote + C::RED_WORDS);
+  uint32_t* s_bits = reinterpret_cast<uint32_t*>(s_w + C::RED_WORDS);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_bits + C::RED_WORDS);
+  uint64_t* q_full = bars;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;
+  uint64_t* k_empty = k_full + C::NSTAGE;
+  uint64_t* acc_full = k_empty + C::NSTAGE;
+  uint64_t* acc_empty = acc_full + NACC;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(acc_empty + NACC);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < C::NSTAGE; ++s) {
+      mbar_init(k_full + s, 1);
+      mbar_init(k_empty + s, 1);
+    }
+    for (int a = 0; a < NACC; ++a) {
+      mbar_init(acc_full + a, 1);
+      mbar_init(acc_empty + a, 128);
+    }
+    *s_abort = 0;
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 0) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+
+  const int64_t total = p.BH * (int64_t)p.nqb;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_qhi);
+      prefetch_tmap(&tm_qlo);
+      prefetch_tmap(&tm_khi);
+      prefetch_tmap(&tm_klo);
+      uint32_t kc = 0;
+      int it = 0;
+      bool ok = true;
+      for (int64_t w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
+        int64_t bh, kvh;
+        int qb;
+        decode_item(w, p, bh, qb, kvh);
+        if (it > 0 && !mbar_wait(q_empty, (it - 1) & 1, s_abort, p.err, kErrTimeoutQ)) break;
+        mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+        for (int c = 0; c < C::NC; ++c) {
+          tma_load_3d(sQ + c * kTileBytes, &tm_qhi, q_full, c * 64, qb * BM, (int)bh);
+          tma_load_3d(sQ + (C::NC + c) * kTileBytes, &tm_qlo, q_full, c * 64, qb * BM, (int)bh);
+        }
+        const int nb = qb + 1;
+        for (int pass = 0; pass < p.npass && ok; ++pass) {
+          for (int kb = 0; kb < nb; ++kb, ++kc) {
+            const uint32_t s = kc % C::NSTAGE, r = kc / C::NSTAGE;
+            if (r > 0 && !mbar_wait(k_empty + s, (r - 1) & 1, s_abort, p.err, kErrTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
+            uint8_t* st = sK + s * C::STAGE_BYTES;
+            mbar_arrive_expect_tx(k_full + s, C::STAGE_BYTES);
+            for (int c = 0; c < C::NC; ++c) {
+              tma_load_3d(st + c * kTileBytes, &tm_khi, k_full + s, c * 64, kb * BN, (int)kvh);
+              tma_load_3d(st + (C::NC + c) * kTileBytes, &tm_klo, k_full + s, c * 64, kb * BN,
+                          (int)kvh);
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t k_addr = smem_u32(sK);
+      uint32_t kc = 0, ac = 0;
+      int it = 0;
+      bool ok = true;
+      for (int64_t w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
+        int64_t bh, kvh;
+        int qb;
+        decode_item(w, p, bh, qb, kvh);
+        if (!mbar_wait(q_full, it & 1, s_abort, p.err, kErrTimeoutQ)) break;
+        tc_fence_after();
+        const int nb = qb + 1;
+        for (int pass = 0; pass < p.npass && ok; ++pass) {
+          for (int kb = 0; kb < nb; ++kb, ++kc, ++ac) {
+            const uint32_t slot = ac % NACC, use = ac / NACC;
+            if (use > 0 && !mbar_wait(acc_empty + slot, (use - 1) & 1, s_abort, p.err,
+                                      kErrTimeoutAcc)) {
+              ok = false;
+              break;
+            }
+            const uint32_t s = kc % C::NSTAGE, r = kc / C::NSTAGE;
+            if (!mbar_wait(k_full + s, r & 1, s_abort, p.err, kErrTimeoutK)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + slot * BN;
+            const uint32_t st = k_addr + s * C::STAGE_BYTES;
+            uint32_t acc = 0;
+#pragma unroll
+            for (int c = 0; c < C::NC; ++c) {
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t off = c * kTileBytes + kk * 32;
+                const uint64_t qh = sw128_kmajor_desc(q_addr + off);
+                const uint64_t ql = sw128_kmajor_desc(q_addr + C::NC * kTileBytes + off);
+                const uint64_t kh = sw128_kmajor_desc(st + off);
+                const uint64_t kl = sw128_kmajor_desc(st + C::NC * kTileBytes + off);
+                umma_bf16(d_tmem, qh, kh, idesc, acc);
+                acc = 1;
+                umma_bf16(d_tmem, qh, kl, idesc, 1);
+                umma_bf16(d_tmem, ql, kh, idesc, 1);
+              }
+            }
+            umma_commit(k_empty + s);
+            umma_commit(acc_full + slot);
+          }
+        }
+        if (ok) umma_commit(q_empty);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 0-3)
+    const int quad = warp;                 // TMEM lane quadrant
+    const int row = quad * 32 + lane;
+    const int64_t nt = (p.N + p.T - 1) / p.T;
+    const int tiles_per_item = BM / p.T;
+    const int quads_per_tile = p.T / 32;
+    uint32_t ac = 0;
+    int rb = 0;
+    bool ok = true;
+    for (int64_t w = blockIdx.x; w < total && ok; w += gridDim.x) {
+      int64_t bh, kvh;
+      int qb;
+      decode_item(w, p, bh, qb, kvh);
+      const int64_t q0 = (int64_t)qb * BM;
+      const int64_t qp = q0 + row;
+      const bool row_ok = qp < p.N;
+      const float tau_h = __ldg(p.tau + (bh % p.H));
+      const int nb = qb + 1;
+      float m = -INFINITY, thr = -INFINITY;
+      int cnt = 0;
+      for (int pass = 0; pass < p.npass && ok; ++pass) {
+        if (pass == 1) thr = __fsub_rn(m, tau_h);
+        for (int kb = 0; kb < nb; ++kb, ++ac) {
+          const uint32_t slot = ac % NACC, use = ac / NACC;
+          if (!mbar_wait(acc_full + slot, use & 1, s_abort, p.err, kErrTimeoutAcc)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + slot * BN;
+          if (pass == 0) {
+#pragma unroll 1
+            for (int ch = 0; ch < 4; ++ch) {
+              float v[32];
+              tmem_ld32(taddr + ch * 32, v);
+              tmem_wait_ld();
+              const int64_t kbase = (int64_t)kb * BN + ch * 32;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float sc = __fmul_rn(v[j], p.sm_scale);
+                if (kbase + j <= qp) m = fmaxf(m, sc);
+              }
+            }
+            tc_fence_before();
+            mbar_arrive(acc_empty + slot);
+          } else {
+            const uint32_t* bufv = s_vote + rb * 512;
+#pragma unroll 1
+            for (int ch = 0; ch < 4; ++ch) {
+              float v[32];
+              tmem_ld32(taddr + ch * 32, v);
+              tmem_wait_ld();
+              const int64_t kbase = (int64_t)kb * BN + ch * 32;
+              uint32_t myvote = 0, mybits = 0;
+              float wv[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float sc = __fmul_rn(v[j], p.sm_scale);
+                const bool keep = row_ok && (kbase + j <= qp) && (sc >= thr);
+                cnt += keep ? 1 : 0;
+                const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+                if (lane == j) {
+                  myvote = __popc(bal);
+                  mybits = bal;
+                }
+                if (p.wmode == 1) {
+                  wv[j] = keep ? __fsub_rn(sc, thr) : 0.f;
+                } else if (p.wmode == 2) {
+                  wv[j] = keep ? expf(__fsub_rn(sc, m)) : 0.f;
+                }
+              }
+              float myw = 0.f;
+              if (p.wmode != 0) myw = transpose_reduce32(wv);
+              const int col = ch * 32 + lane;
+              const int o = rb * 512 + quad * 128 + col;
+              s_vote[o] = myvote;
+              s_bits[o] = mybits;
+              s_w[o] = myw;
+            }
+            (void)bufv;
+            tc_fence_before();
+            mbar_arrive(acc_empty + slot);
+            // combine the quadrants of each query tile, store compact votes / bits / wvotes
+            named_bar_sync(1, 128);
+            const int col = threadIdx.x;
+            const int64_t kj = (int64_t)kb * BN + col;
+            for (int tt = 0; tt < tiles_per_item; ++tt) {
+              const int64_t tg = q0 / p.T + tt;
+              if (tg >= nt) break;
+              const int64_t hi_t = min((tg + 1) * (int64_t)p.T, p.N);
+              if (kj >= hi_t) continue;
+              uint32_t vs = 0;
+              float wsum = 0.f;
+              for (int qq = tt * quads_per_tile; qq < (tt + 1) * quads_per_tile; ++qq) {
+                const int o = rb * 512 + qq * 128 + col;
+                vs += s_vote[o];
+                wsum += s_w[o];
+              }
+              const int64_t off = bh * p.head_stride + tri_tile_offset(tg, p.T) + kj;
+              if (p.votes) p.votes[off] = (uint8_t)vs;
+              if (p.wmode != 0 && p.wvotes) p.wvotes[off] = wsum;
+              if (p.bits && p.T == 32) p.bits[off] = s_bits[rb * 512 + tt * 128 + col];
+            }
+            rb ^= 1;
+          }
+        }
+      }
+      if (ok && row_ok) {
+        if (p.row_max) p.row_max[bh * p.N + qp] = m;
+        if (p.row_count && p.npass == 2) p.row_count[bh * p.N + qp] = cnt;
+      }
+    }
+  }
+
+  // ------------------------------------------------------------------ teardown
+  if (*s_abort) {
+    // let in-flight asynchronous copies / MMAs drain before the CTA releases its resources
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 2000000ull) {
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem_base, 512);
+}
+
+}  // namespace
+
+int launch_select(const sta_select_args* a, cudaStream_t stream) {
+  if (!a || !a->q_hi || !a->q_lo || !a->k_hi || !a->k_lo || !a->tau)
+    return fail(STA_ERR_ARG, "sta_select: null pointer");
+  if (a->d != 64 && a->d != 128) return fail(STA_ERR_UNSUPPORTED, "sta_select: d must be 64 or 128");
+  if (a->tile != 32 && a->tile != 64 && a->tile != 128)
+    return fail(STA_ERR_UNSUPPORTED, "sta_select: tile must be 32, 64 or 128");
+  if (a->n_heads <= 0 || a->n_kv_heads <= 0 || a->n_heads % a->n_kv_heads)
+    return fail(STA_ERR_ARG, "sta_select: n_heads must be a positive multiple of n_kv_heads");
+  if (a->bits && a->tile != 32) return fail(STA_ERR_UNSUPPORTED, "sta_select: bits need tile 32");
+  if (a->wmode != 0 && !a->wvotes && !a->max_only)
+    return fail(STA_ERR_ARG, "sta_select: weighted mode needs wvotes");
+  if (a->n <= 0 || a->batch <= 0) return 0;
+  if (a->n > (int64_t)1 << 30) return fail(STA_ERR_UNSUPPORTED, "sta_select: n too large");
+
+  const int64_t BH = a->batch * a->n_heads;
+  const int64_t BHk = a->batch * a->n_kv_heads;
+  CUtensorMap m_qhi, m_qlo, m_khi, m_klo;
+  bool okm = make_tmap_bf16_3d(&m_qhi, a->q_hi, a->d, a->n, BH, 64, 128) &&
+             make_tmap_bf16_3d(&m_qlo, a->q_lo, a->d, a->n, BH, 64, 128) &&
+             make_tmap_bf16_3d(&m_khi, a->k_hi, a->d, a->n, BHk, 64, 128) &&
+             make_tmap_bf16_3d(&m_klo, a->k_lo, a->d, a->n, BHk, 64, 128);
+  if (!okm) return fail(STA_ERR_CUDA, "sta_select: cuTensorMapEncodeTiled failed");
+
+  Params p;
+  p.BH = BH;
+  p.H = (int)a->n_heads;
+  p.Hkv = (int)a->n_kv_heads;
+  p.N = a->n;
+  p.T = a->tile;
+  p.nqb = (int)((a->n + BM - 1) / BM);
+  p.npass = a->max_only ? 1 : 2;
+  p.wmode = a->max_only ? 0 : a->wmode;
+  p.sm_scale = a->sm_scale;
+  p.tau = a->tau;
+  p.votes = a->max_only ? nullptr : a->votes;
+  p.wvotes = a->max_only ? nullptr : a->wvotes;
+  p.bits = a->max_only ? nullptr : a->bits;
+  p.row_max = a->row_max;
+  p.row_count = a->row_count;
+  p.err = device_error_word();
+  p.head_stride = tri_head_stride(a->n, a->tile);
+
+  int dev = 0, nsm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t total = BH * p.nqb;
+  const int grid = (int)(total < nsm ? total : nsm);
+  cudaError_t e;
+  if (a->d == 128) {
+    e = cudaFuncSetAttribute(select_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg<128>::SMEM);
+    if (e == cudaSuccess)
+      select_kernel<128><<<grid, kThreads, Cfg<128>::SMEM, stream>>>(m_qhi, m_qlo, m_khi, m_klo, p);
+  } else {
+    e = cudaFuncSetAttribute(select_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg<64>::SMEM);
+    if (e == cudaSuccess)
+      select_kernel<64><<<grid, kThreads, Cfg<64>::SMEM, stream>>>(m_qhi, m_qlo, m_khi, m_klo, p);
+  }
+  if (e != cudaSuccess) return fail(STA_ERR_CUDA, cudaGetErrorString(e));
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(STA_ERR_CUDA, cudaGetErrorString(e));
+  return STA_OK;
+}
+
+}  // namespace sta

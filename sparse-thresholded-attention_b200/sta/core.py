@@ -1,0 +1,347 @@
+"""Torch-facing plumbing around the C ABI: argument normalisation, output allocation,
+workspace allocation (torch caching allocator) and the launch on torch's current stream.
+
+Everything numeric runs in libsta.so; this module only moves pointers.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib as L
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.float32:
+        return L.STA_DTYPE_F32
+    if dt == torch.bfloat16:
+        return L.STA_DTYPE_BF16
+    raise TypeError(f"unsupported dtype {dt} (float32 or bfloat16)")
+
+
+def _rows(x: torch.Tensor) -> torch.Tensor:
+    """(heads, n, d) view with a contiguous last dim (copy only when needed)."""
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    return x
+
+
+@dataclass
+class Geometry:
+    """RoPE geometry: frequencies, position compression, cos/sin scale (YaRN mscale)."""
+    inv_freq: torch.Tensor
+    pos_scale: float = 1.0
+    rope_scale: float = 1.0
+
+
+def _dev_f32(x, device):
+    return x.to(device=device, dtype=torch.float32).contiguous()
+
+
+def _check_inputs(q, k, v):
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise ValueError("q, k, v must be CUDA tensors (there is no CPU path)")
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError("q, k, v must be (Z, H, N, D)")
+    Z, H, N, D = q.shape
+    if k.shape[0] != Z or v.shape != k.shape or k.shape[2] != N or k.shape[3] != D:
+        raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
+    if H % k.shape[1]:
+        raise ValueError("number of q heads must be a multiple of the number of kv heads")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError("q, k, v must share one dtype")
+    dtype_code(q.dtype)
+    return Z, H, k.shape[1], N, D
+
+
+def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=None,
+            pct=30.0, n_global=32, n_local=32, tile=32, k_max=1024, select_score="freq",
+            measure=False, block_n=32, pos_advance="max", use_skip=True, keep_sets=False,
+            max_workspace_bytes=0):
+    """Run one prefill op.  variant: 'shared' | 'pq_union' | 'pq_stream'.
+    q (Z,H,N,D); k, v (Z,Hkv,N,D) with H % Hkv == 0 (Hkv == H for repeat_kv-expanded input).
+    Returns (out (Z,H,N,D), dict of per-(head, tile) statistics [+ sets when keep_sets])."""
+    Z, H, Hk, N, D = _check_inputs(q, k, v)
+    dev = q.device
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    T = int(tile)
+    nt = (N + T - 1) // T
+    tau_d = _dev_f32(tau, dev).reshape(-1)
+    if tau_d.numel() != H:
+        raise ValueError(f"tau must have one entry per q head ({H}), got {tau_d.numel()}")
+    ia = _dev_f32(ga.inv_freq, dev)
+    ic = _dev_f32(gc.inv_freq, dev)
+    if ia.numel() != D // 2 or ic.numel() != D // 2:
+        raise ValueError("inv_freq must have head_dim/2 entries")
+    out = torch.empty((Z, H, N, D), dtype=q.dtype, device=dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    st = {}
+    if variant == "shared":
+        for name in ("shared_size", "kept_size", "chosen", "kpct_meas"):
+            st[name] = torch.empty((Z, H, nt), **i32)
+        st["overflow"] = torch.empty((Z, H, nt), dtype=torch.uint8, device=dev)
+        st["overflow20"] = torch.empty((Z, H, nt), dtype=torch.uint8, device=dev)
+    elif variant == "pq_union":
+        st["usize"] = torch.empty((Z, H, nt), **i32)
+        st["kept_size"] = torch.empty((Z, H, nt), **i32)
+        st["overflow"] = torch.empty((Z, H, nt), dtype=torch.uint8, device=dev)
+    elif variant == "pq_stream":
+        f32 = dict(dtype=torch.float32, device=dev)
+        st["span"] = torch.empty((Z, H, nt), **f32)
+        st["kept"] = torch.empty((Z, H, N), **i32)
+        st["blocks"] = torch.empty((Z, H, nt), **f32)
+        st["skipped"] = torch.empty((Z, H, nt), **f32)
+    else:
+        raise ValueError(variant)
+    sets = {}
+    if keep_sets and variant != "pq_stream":
+        sets["idx"] = torch.empty((Z, H, nt, k_max), **i32)
+        sets["newpos_k"] = torch.empty((Z, H, nt, k_max), dtype=torch.float32, device=dev)
+        sets["newpos_q"] = torch.empty((Z, H, nt, T), dtype=torch.float32, device=dev)
+        if variant == "pq_union":
+            sets["mask"] = torch.empty((Z, H, nt, k_max), **i32)
+    lib = L.lib()
+    fn_ws = getattr(lib, {"shared": "sta_shared_workspace_bytes",
+                          "pq_union": "sta_pq_union_workspace_bytes",
+                          "pq_stream": "sta_pq_stream_workspace_bytes"}[variant])
+    fn = getattr(lib, {"shared": "sta_shared_forward", "pq_union": "sta_pq_union_forward",
+                       "pq_stream": "sta_pq_stream_forward"}[variant])
+    stream = _stream()
+    ws = None
+    for b in range(Z):
+        qb, kb, vb = _rows(q[b]), _rows(k[b]), _rows(v[b])
+        a = L.ForwardArgs()
+        a.q, a.q_stride_h, a.q_stride_n = qb.data_ptr(), qb.stride(0), qb.stride(1)
+        a.k, a.k_stride_h, a.k_stride_n = kb.data_ptr(), kb.stride(0), kb.stride(1)
+        a.v, a.v_stride_h, a.v_stride_n = vb.data_ptr(), vb.stride(0), vb.stride(1)
+        a.out = out[b].data_ptr()
+        a.dtype = dtype_code(q.dtype)
+        a.batch, a.n_heads, a.n_kv_heads, a.n, a.d = 1, H, Hk, N, D
+        a.tau = tau_d.data_ptr()
+        a.inv_freq_a, a.pos_scale_a, a.rope_scale_a = ia.data_ptr(), float(ga.pos_scale), float(ga.rope_scale)
+        a.inv_freq_c, a.pos_scale_c, a.rope_scale_c = ic.data_ptr(), float(gc.pos_scale), float(gc.rope_scale)
+        a.sm_scale = float(sm_scale)
+        a.pct = float(pct)
+        a.n_global, a.n_local, a.tile, a.k_max = int(n_global), int(n_local), T, int(k_max or 0)
+        a.select_score = L.SCORE[select_score]
+        a.measure = int(bool(measure))
+        a.block_n = int(block_n)
+        a.pos_advance = L.ADV[pos_advance]
+        a.use_skip = int(bool(use_skip))
+        if variant == "shared":
+            a.shared_size = st["shared_size"][b].data_ptr()
+            a.kept_size = st["kept_size"][b].data_ptr()
+            a.chosen = st["chosen"][b].data_ptr()
+            a.overflow = st["overflow"][b].data_ptr()
+            a.kpct_meas = st["kpct_meas"][b].data_ptr()
+            a.overflow20 = st["overflow20"][b].data_ptr()
+        elif variant == "pq_union":
+            a.shared_size = st["usize"][b].data_ptr()
+            a.kept_size = st["kept_size"][b].data_ptr()
+            a.overflow = st["overflow"][b].data_ptr()
+        else:
+            a.span = st["span"][b].data_ptr()
+            a.kept_rows = st["kept"][b].data_ptr()
+            a.blocks = st["blocks"][b].data_ptr()
+            a.skipped = st["skipped"][b].data_ptr()
+        if sets:
+            a.idx_out = sets["idx"][b].data_ptr()
+            a.newpos_k_out = sets["newpos_k"][b].data_ptr()
+            a.newpos_q_out = sets["newpos_q"][b].data_ptr()
+            if "mask" in sets:
+                a.mask_out = sets["mask"][b].data_ptr()
+        a.max_workspace_bytes = int(max_workspace_bytes)
+        nbytes = fn_ws(ctypes.byref(a))
+        if nbytes == 0:
+            L.check(1, f"sta_{variant}_workspace_bytes")
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        L.check(fn(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel()),
+                   stream), f"sta_{variant}_forward")
+    return out, st, sets
+
+
+# -------------------------------------------------------------------------------------------
+# stage-level access (used by the parity tests to compare intermediates with the oracle)
+# -------------------------------------------------------------------------------------------
+def rope_split(x: torch.Tensor, g: Geometry):
+    """x (heads, n, d) -> (hi, lo) bf16 rotated at the selection geometry."""
+    x = _rows(x)
+    Hx, N, D = x.shape
+    hi = torch.empty((Hx, N, D), dtype=torch.bfloat16, device=x.device)
+    lo = torch.empty_like(hi)
+    invf = _dev_f32(g.inv_freq, x.device)
+    L.check(L.lib().sta_rope_split(_p(x), dtype_code(x.dtype), Hx, N, D, x.stride(0),
+                                   x.stride(1), _p(invf), float(g.pos_scale),
+                                   float(g.rope_scale), _p(hi), _p(lo), _stream()),
+            "sta_rope_split")
+    return hi, lo
+
+
+def tri_head_stride(n: int, tile: int) -> int:
+    return int(L.lib().sta_tri_head_stride(n, tile))
+
+
+def select(q: torch.Tensor, k: torch.Tensor, tau, g: Geometry, *, tile, sm_scale=None,
+           wmode=0, bits=False, max_only=False):
+    """Kernel A on raw (H,N,D) q and (Hkv,N,D) k.  Returns dict of compact votes / wvotes /
+    bits, row_max (H,N) and row_count (H,N)."""
+    H, N, D = q.shape
+    Hk = k.shape[0]
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    qh, ql = rope_split(q, g)
+    kh, kl = rope_split(k, g)
+    HS = tri_head_stride(N, tile)
+    dev = q.device
+    res = {"row_max": torch.empty((H, N), dtype=torch.float32, device=dev),
+           "row_count": torch.empty((H, N), dtype=torch.int32, device=dev)}
+    if not max_only:
+        res["votes"] = torch.empty((H * HS,), dtype=torch.uint8, device=dev)
+        if wmode:
+            res["wvotes"] = torch.empty((H * HS,), dtype=torch.float32, device=dev)
+        if bits:
+            res["bits"] = torch.empty((H * HS,), dtype=torch.int32, device=dev)
+    tau_d = _dev_f32(tau, dev)
+    a = L.SelectArgs()
+    a.q_hi, a.q_lo, a.k_hi, a.k_lo = qh.data_ptr(), ql.data_ptr(), kh.data_ptr(), kl.data_ptr()
+    a.batch, a.n_heads, a.n_kv_heads, a.n, a.d, a.tile = 1, H, Hk, N, D, tile
+    a.sm_scale = float(sm_scale)
+    a.wmode = int(wmode)
+    a.tau = tau_d.data_ptr()
+    a.max_only = int(bool(max_only))
+    a.votes = res["votes"].data_ptr() if "votes" in res else None
+    a.wvotes = res["wvotes"].data_ptr() if "wvotes" in res else None
+    a.bits = res["bits"].data_ptr() if "bits" in res else None
+    a.row_max = res["row_max"].data_ptr()
+    a.row_count = res["row_count"].data_ptr()
+    L.check(L.lib().sta_select(ctypes.byref(a), _stream()), "sta_select")
+    return res
+
+
+def expand_compact(flat: torch.Tensor, H: int, N: int, tile: int, fill=0):
+    """compact (H*HS,) per-(head, tile) array -> dense (H, nt, N) (small sizes only)."""
+    HS = tri_head_stride(N, tile)
+    nt = (N + tile - 1) // tile
+    x = flat.reshape(H, HS)
+    out = torch.full((H, nt, N), fill, dtype=flat.dtype, device=flat.device)
+    for t in range(nt):
+        hi = min((t + 1) * tile, N)
+        o = tile * t * (t + 1) // 2
+        out[:, t, :hi] = x[:, o:o + hi]
+    return out
+
+
+def compact_from_dense(dense: torch.Tensor, tile: int):
+    """dense (H, nt, N) -> compact (H*HS,) (inverse of expand_compact)."""
+    H, nt, N = dense.shape
+    parts = []
+    for h in range(H):
+        for t in range(nt):
+            parts.append(dense[h, t, :min((t + 1) * tile, N)])
+    return torch.cat(parts).contiguous()
+
+
+def device_error() -> int:
+    code = L.c_i32(0)
+    L.lib().sta_device_error(_stream(), ctypes.byref(code))
+    return int(code.value)
+
+
+def build_sets(votes_c, wvotes_c, H, N, *, tile, k_max, n_global=32, n_local=32, pct=30.0,
+               pos_scale=1.0, select_score="freq", measure=False):
+    """Stage 2 on compact votes (uint8) / wvotes (f32).  Returns the reference's 9 outputs."""
+    dev = votes_c.device
+    nt = (N + tile - 1) // tile
+    i32 = dict(dtype=torch.int32, device=dev)
+    o = dict(idx=torch.empty((H, nt, k_max), **i32),
+             newpos_k=torch.empty((H, nt, k_max), dtype=torch.float32, device=dev),
+             newpos_q=torch.empty((H, nt, tile), dtype=torch.float32, device=dev),
+             shared_size=torch.empty((H, nt), **i32), kept_size=torch.empty((H, nt), **i32),
+             chosen=torch.empty((H, nt), **i32),
+             overflow=torch.empty((H, nt), dtype=torch.uint8, device=dev),
+             kpct_meas=torch.empty((H, nt), **i32),
+             overflow20=torch.empty((H, nt), dtype=torch.uint8, device=dev))
+    a = L.BuildArgs()
+    a.votes = votes_c.data_ptr()
+    a.wvotes = wvotes_c.data_ptr() if wvotes_c is not None else None
+    a.heads, a.n, a.tile, a.k_max = H, N, tile, k_max
+    a.n_global, a.n_local, a.pct, a.pos_scale = n_global, n_local, float(pct), float(pos_scale)
+    a.select_score = L.SCORE[select_score]
+    a.measure = int(bool(measure))
+    for name in ("idx", "newpos_k", "newpos_q", "shared_size", "kept_size", "chosen",
+                 "overflow", "kpct_meas", "overflow20"):
+        setattr(a, name, o[name].data_ptr())
+    L.check(L.lib().sta_build_sets(ctypes.byref(a), _stream()), "sta_build_sets")
+    return o
+
+
+def build_sets_pq(votes_c, wvotes_c, bits_c, H, N, *, k_max, n_global=32, n_local=32,
+                  select_score="expmass"):
+    dev = votes_c.device
+    T = 32
+    nt = (N + T - 1) // T
+    i32 = dict(dtype=torch.int32, device=dev)
+    o = dict(idx=torch.empty((H, nt, k_max), **i32),
+             newpos_k=torch.empty((H, nt, k_max), dtype=torch.float32, device=dev),
+             newpos_q=torch.empty((H, nt, T), dtype=torch.float32, device=dev),
+             mask=torch.empty((H, nt, k_max), **i32), usize=torch.empty((H, nt), **i32),
+             kept_size=torch.empty((H, nt), **i32),
+             overflow=torch.empty((H, nt), dtype=torch.uint8, device=dev))
+    a = L.BuildPQArgs()
+    a.votes = votes_c.data_ptr()
+    a.wvotes = wvotes_c.data_ptr() if wvotes_c is not None else None
+    a.bits = bits_c.data_ptr()
+    a.heads, a.n, a.tile, a.k_max = H, N, T, k_max
+    a.n_global, a.n_local = n_global, n_local
+    a.select_score = L.SCORE[select_score]
+    for name in ("idx", "newpos_k", "newpos_q", "mask", "usize", "kept_size", "overflow"):
+        setattr(a, name, o[name].data_ptr())
+    L.check(L.lib().sta_build_sets_pq(ctypes.byref(a), _stream()), "sta_build_sets_pq")
+    return o
+
+
+def gather_attend(q, k, v, idx, newpos_k, newpos_q, g: Geometry, *, tile, sm_scale=None,
+                  mask=None, kept_size=None):
+    """Stage 3 on raw (H,N,D) q and (Hkv,N,D) k, v with (H,nt,k_max) slot arrays."""
+    q, k, v = _rows(q), _rows(k), _rows(v)
+    H, N, D = q.shape
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    out = torch.empty((H, N, D), dtype=q.dtype, device=q.device)
+    invf = _dev_f32(g.inv_freq, q.device)
+    a = L.AttendArgs()
+    a.q, a.q_stride_h, a.q_stride_n = q.data_ptr(), q.stride(0), q.stride(1)
+    a.k, a.k_stride_h, a.k_stride_n = k.data_ptr(), k.stride(0), k.stride(1)
+    a.v, a.v_stride_h, a.v_stride_n = v.data_ptr(), v.stride(0), v.stride(1)
+    a.out = out.data_ptr()
+    a.dtype = dtype_code(q.dtype)
+    a.batch, a.n_heads, a.n_kv_heads, a.n, a.d = 1, H, k.shape[0], N, D
+    a.tile, a.k_max = tile, idx.shape[-1]
+    idx = idx.to(torch.int32).contiguous()
+    newpos_k = newpos_k.float().contiguous()
+    newpos_q = newpos_q.float().contiguous()
+    a.idx, a.newpos_k, a.newpos_q = idx.data_ptr(), newpos_k.data_ptr(), newpos_q.data_ptr()
+    if mask is not None:
+        mask = mask.to(torch.int32).contiguous()
+        a.mask = mask.data_ptr()
+    if kept_size is not None:
+        kept_size = kept_size.to(torch.int32).contiguous()
+        a.kept_size = kept_size.data_ptr()
+    a.inv_freq = invf.data_ptr()
+    a.rope_scale = float(g.rope_scale)
+    a.sm_scale = float(sm_scale)
+    L.check(L.lib().sta_gather_attend(ctypes.byref(a), _stream()), "sta_gather_attend")
+    return out

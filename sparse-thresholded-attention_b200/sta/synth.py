@@ -76,9 +76,10 @@ def make_inputs(spec: SynthSpec):
                 n_later = S - 1 - p
                 nq = min(spec.n_planted_queries, n_later)
                 for h in range(kh * G, (kh + 1) * G):
-                    # random later queries (drawn with replacement; duplicates are harmless)
-                    later = torch.randint(p + 1, S, (nq,), generator=g)
-                    w = torch.randn((nq, D), generator=g)
+                    # random later queries (drawn with replacement, then de-duplicated so the
+                    # scatter below is deterministic)
+                    later = torch.unique(torch.randint(p + 1, S, (nq,), generator=g))
+                    w = torch.randn((nq, D), generator=g)[:later.numel()]
                     w = w - (w @ u)[:, None] * u[None, :]
                     w = w / w.norm(dim=-1, keepdim=True).clamp_min(1e-12)
                     qn = q[b, h, later].norm(dim=-1, keepdim=True)

@@ -1,0 +1,100 @@
+"""CPU-side checks of the C ABI library and the host layer (no GPU compute)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from sta import _lib as L
+from sta import core
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+HEADER = os.path.join(os.path.dirname(HERE), "include", "sta.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(sta_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = L.lib()
+    decl = declared_functions()
+    assert len(decl) >= 15
+    for name in decl:
+        assert hasattr(lib, name), name
+    assert sorted(L.EXPORTED) == decl
+
+
+def test_struct_layouts_match_header_order():
+    """ctypes mirrors list the header's fields in order (names compared)."""
+    src = open(HEADER).read()
+    for cname, cls in (("sta_select_args", L.SelectArgs), ("sta_build_args", L.BuildArgs),
+                       ("sta_build_pq_args", L.BuildPQArgs), ("sta_attend_args", L.AttendArgs),
+                       ("sta_pqstream_args", L.PQStreamArgs), ("sta_forward_args", L.ForwardArgs)):
+        body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), src, re.S).group(1)
+        body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+        fields = re.findall(r"\**\s*([a-z_0-9]+)\s*;", body)
+        assert [f for f, _ in cls._fields_] == fields, cname
+
+
+def test_tri_head_stride():
+    lib = L.lib()
+    for n, t in ((300, 64), (1024, 32), (1, 32), (131072, 32), (65536, 64)):
+        nt = (n + t - 1) // t
+        assert lib.sta_tri_head_stride(n, t) == t * (nt - 1) * nt // 2 + n
+
+
+def test_null_arguments_rejected_without_gpu():
+    lib = L.lib()
+    assert lib.sta_select(None, None) == 1
+    assert lib.sta_build_sets(None, None) == 1
+    assert lib.sta_gather_attend(None, None) == 1
+    assert lib.sta_shared_workspace_bytes(None) == 0
+    assert b"null" in lib.sta_last_error()
+
+
+def test_workspace_query_and_grouping():
+    lib = L.lib()
+    a = L.ForwardArgs()
+    for f in ("q", "k", "v", "out", "tau", "inv_freq_a", "inv_freq_c", "shared_size",
+              "kept_size", "chosen", "overflow", "kpct_meas", "overflow20"):
+        setattr(a, f, 256)  # non-null placeholders: the size query reads no memory
+    a.dtype, a.batch, a.n_heads, a.n_kv_heads, a.n, a.d = 1, 1, 32, 8, 32768, 128
+    a.tile, a.k_max, a.select_score = 64, 2048, 0
+    full = lib.sta_shared_workspace_bytes(ctypes.byref(a))
+    assert full > 0
+    a.max_workspace_bytes = full // 4
+    part = lib.sta_shared_workspace_bytes(ctypes.byref(a))
+    assert 0 < part <= full // 4 + 4096
+
+
+def test_cpu_tensors_rejected():
+    from sta import shared_selection_exact_2 as ex2
+    x = torch.zeros((1, 2, 64, 64))
+    with pytest.raises(ValueError):
+        ex2.shared_pi_attention(x, x, x, torch.ones(2), torch.ones(32))
+
+
+def test_compact_layout_roundtrip():
+    H, N, T = 2, 300, 64
+    rng = np.random.default_rng(0)
+    dense = torch.from_numpy(rng.integers(0, 65, size=(H, (N + T - 1) // T, N)).astype(np.int32))
+    nt = dense.shape[1]
+    for t in range(nt):
+        dense[:, t, min((t + 1) * T, N):] = 0
+    flat = core.compact_from_dense(dense, T)
+    assert flat.numel() == H * core.tri_head_stride(N, T)
+    assert torch.equal(core.expand_compact(flat, H, N, T), dense)
+
+
+def test_synth_is_deterministic():
+    from sta.synth import SynthSpec, make_inputs
+    a = make_inputs(SynthSpec(n_heads=2, n_kv_heads=1, seq_len=128, head_dim=64, seed=3))
+    b = make_inputs(SynthSpec(n_heads=2, n_kv_heads=1, seq_len=128, head_dim=64, seed=3))
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+    assert a[0].shape == (1, 2, 128, 64) and a[1].shape == (1, 1, 128, 64)

@@ -1,0 +1,329 @@
+"""CUDA path vs the oracle / the reference's golden outputs (needs a B200).
+
+Parity bar (from the benchmark contract): integer / index outputs of the selection bit-exact
+for identical votes; Kernel A's keep decisions exact except pairs whose score lies within 1e-3
+of the threshold (counted by the oracle); outputs within max-abs 1e-4 (fp32) or max-abs 2e-2 /
+mean-abs 1e-3 (bf16).
+"""
+import glob
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import oracle
+
+import sta  # noqa: F401
+from sta import core
+from sta.core import Geometry
+from sta import shared_selection_exact_2 as ex2
+from sta import shared_selection_exact as ex1
+from sta import shared_selection_hybrid_exact as hyb
+from sta import shared_selection_perquery as pq
+from sta import pqstream_kernel as pqs
+from sta.synth import SynthSpec, make_inputs, rope_inv_freq, yarn_inv_freq
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+FIX = sorted(glob.glob(os.path.join(HERE, "golden", "*.npz")))
+DEV = "cuda"
+BAND = 1e-3
+F32_TOL = 1e-4
+BF16_MAX, BF16_MEAN = 2e-2, 1e-3
+
+
+def load(name):
+    z = np.load(os.path.join(HERE, "golden", name + ".npz"))
+    meta = json.loads(str(z["meta"]))
+    return meta, {k: z[k] for k in z.files if k != "meta"}
+
+
+def cu(x, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(x)).to(DEV)
+    return t.to(dtype) if dtype is not None else t
+
+
+def names(pattern):
+    return [os.path.basename(p)[:-4] for p in FIX if pattern in os.path.basename(p)]
+
+
+def assert_close_out(got, ref, dtype):
+    err = (got.float().cpu().numpy() - np.asarray(ref, np.float32))
+    err = np.abs(err[np.isfinite(err)])
+    if dtype == torch.float32:
+        assert err.max() <= F32_TOL, err.max()
+    else:
+        assert err.max() <= BF16_MAX and err.mean() <= BF16_MEAN, (err.max(), err.mean())
+
+
+# ---------------------------------------------------------------------------------------------
+# Kernel A (tcgen05 select) vs oracle
+# ---------------------------------------------------------------------------------------------
+SELECT_CASES = [
+    # H, Hkv, N, D, T, dtype, wmode, bits, pos_scale, seed
+    (2, 2, 300, 64, 64, torch.float32, 0, False, 0.5, 1),
+    (2, 2, 256, 128, 32, torch.float32, 2, True, 1.0, 2),
+    (4, 2, 384, 128, 64, torch.bfloat16, 1, False, 1.0, 3),
+    (2, 1, 200, 64, 32, torch.bfloat16, 2, True, 0.75, 4),
+    (1, 1, 129, 128, 64, torch.float32, 0, False, 1.0, 5),
+    (2, 2, 1000, 128, 128, torch.bfloat16, 0, False, 1.0, 6),
+]
+
+
+@pytest.mark.parametrize("case", SELECT_CASES, ids=[f"sel{i}" for i in range(len(SELECT_CASES))])
+def test_select_vs_oracle(case):
+    H, Hk, N, D, T, dt, wmode, want_bits, ps, seed = case
+    q, k, v = make_inputs(SynthSpec(n_heads=H, n_kv_heads=Hk, seq_len=N, head_dim=D,
+                                    n_planted=8, n_planted_queries=16, seed=seed, dtype=dt))
+    tau = torch.full((H,), 5.0)
+    invf = rope_inv_freq(D, 1e4)
+    g = Geometry(invf, ps, 1.0)
+    res = core.select(cu(q[0]), cu(k[0]), tau, g, tile=T, wmode=wmode, bits=want_bits)
+    torch.cuda.synchronize()
+    assert core.device_error() == 0
+    kx = k[0].float().repeat_interleave(H // Hk, 0).numpy()
+    o = oracle.select_vote(q[0].float().numpy(), kx, tau.numpy(), invf.numpy(), ps, 1.0,
+                           1.0 / math.sqrt(D), T, wmode=wmode, want_bits=want_bits)
+    np.testing.assert_allclose(res["row_max"].cpu().numpy(), o["m"], rtol=2e-5, atol=2e-4)
+    votes = core.expand_compact(res["votes"], H, N, T).cpu().numpy().astype(np.int32)
+    diff = int(np.abs(votes - o["votes"]).sum())
+    assert diff <= o["boundary"], (diff, o["boundary"])
+    rc = res["row_count"].cpu().numpy()
+    assert int(np.abs(rc - o["row_counts"]).sum()) <= o["boundary"]
+    if wmode:
+        wv = core.expand_compact(res["wvotes"], H, N, T).cpu().numpy()
+        np.testing.assert_allclose(wv, o["wvotes"], rtol=1e-3, atol=2e-3)
+    if want_bits:
+        b = core.expand_compact(res["bits"], H, N, T).cpu().numpy().view(np.uint32)
+        nb = sum(bin(int(x)).count("1") for x in (b ^ o["bits"]).ravel() if x)
+        assert nb <= o["boundary"]
+
+
+def test_select_tau_zero_keeps_argmax():
+    """Both passes issue identical tensor-core sequences: with tau = 0 every real query keeps
+    at least its own maximum key."""
+    H, N, D = 2, 700, 128
+    q, k, _ = make_inputs(SynthSpec(n_heads=H, n_kv_heads=H, seq_len=N, head_dim=D, seed=9,
+                                    dtype=torch.bfloat16))
+    res = core.select(cu(q[0]), cu(k[0]), torch.zeros(H), Geometry(rope_inv_freq(D, 1e4)),
+                      tile=64)
+    assert int(res["row_count"].min()) >= 1
+
+
+# ---------------------------------------------------------------------------------------------
+# selection stage: bit-exact on the reference's own votes
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("name", names("shared"))
+def test_build_sets_bit_exact_on_reference_votes(name):
+    meta, a = load(name)
+    H, N, T = meta["H"], meta["N"], meta["T"]
+    votes = core.compact_from_dense(cu(a["votes"].astype(np.uint8)), T)
+    wv = None
+    if meta["select_score"] != "freq":
+        wv = core.compact_from_dense(cu(a["wvotes"].astype(np.float32)), T)
+    o = core.build_sets(votes, wv, H, N, tile=T, k_max=meta["k_max"], n_global=meta["n_global"],
+                        n_local=meta["n_local"], pct=meta["pct"], pos_scale=meta["pos_scale_c"],
+                        select_score=meta["select_score"], measure=meta["measure"])
+    np.testing.assert_array_equal(o["idx"].cpu().numpy(), a["idx"])
+    np.testing.assert_array_equal(o["newpos_k"].cpu().numpy(), a["newpos_k"])
+    np.testing.assert_array_equal(o["newpos_q"].cpu().numpy(), a["newpos_q"])
+    np.testing.assert_array_equal(o["shared_size"].cpu().numpy(), a["shared_size"])
+    np.testing.assert_array_equal(o["kept_size"].cpu().numpy(), a["kept_size"])
+    np.testing.assert_array_equal(o["chosen"].cpu().numpy(), a["kpct"])
+    np.testing.assert_array_equal(o["overflow"].cpu().numpy(), a["overflow"])
+    np.testing.assert_array_equal(o["kpct_meas"].cpu().numpy(), a["kpct_meas"])
+    np.testing.assert_array_equal(o["overflow20"].cpu().numpy(), a["overflow20"])
+
+
+@pytest.mark.parametrize("name", names("pq_union"))
+def test_build_sets_pq_bit_exact_on_reference_votes(name):
+    meta, a = load(name)
+    H, N = meta["H"], meta["N"]
+    votes = core.compact_from_dense(cu(a["votes"].astype(np.uint8)), 32)
+    bits = core.compact_from_dense(cu(a["bits"].astype(np.int32)), 32)
+    wv = None
+    if meta["select_score"] != "freq":
+        wv = core.compact_from_dense(cu(a["wvotes"].astype(np.float32)), 32)
+    o = core.build_sets_pq(votes, wv, bits, H, N, k_max=meta["k_max"],
+                           select_score=meta["select_score"])
+    for key in ("idx", "newpos_k", "newpos_q", "mask"):
+        np.testing.assert_array_equal(o[key].cpu().numpy(), a[key], err_msg=key)
+    np.testing.assert_array_equal(o["usize"].cpu().numpy(), a["usize"])
+    np.testing.assert_array_equal(o["kept_size"].cpu().numpy(), a["kept_size"])
+    np.testing.assert_array_equal(o["overflow"].cpu().numpy(), a["overflow"])
+
+
+# ---------------------------------------------------------------------------------------------
+# Kernel C on the reference's own sets
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("name", names("shared") + names("pq_union"))
+def test_gather_attend_on_reference_sets(name):
+    meta, a = load(name)
+    T = meta["T"]
+    is_pq = meta["kind"] == "pq"
+    g = Geometry(torch.from_numpy(a["inv_freq_c"]), 1.0,
+                 1.0 if is_pq else meta["rope_scale_c"])
+    out = core.gather_attend(cu(a["q"]), cu(a["k"]), cu(a["v"]), cu(a["idx"]),
+                             cu(a["newpos_k"]), cu(a["newpos_q"]), g, tile=T,
+                             mask=cu(a["mask"]) if is_pq else None)
+    assert_close_out(out, a["out"], torch.float32)
+
+
+# ---------------------------------------------------------------------------------------------
+# end to end through the reference call surfaces
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("name", names("shared"))
+def test_shared_end_to_end_vs_reference(name):
+    meta, a = load(name)
+    q, k, v = (cu(a[x])[None] for x in ("q", "k", "v"))
+    tau = torch.from_numpy(a["tau"])
+    kw = dict(pct=meta["pct"], n_global=meta["n_global"], n_local=meta["n_local"],
+              tile=meta["T"], k_max=meta["k_max"], measure=meta["measure"])
+    if meta["geom"] == "hybrid":
+        res = hyb.shared_pi_attention(q, k, v, tau, torch.from_numpy(a["inv_freq_a"]),
+                                      meta["pos_scale_a"], meta["rope_scale_a"],
+                                      torch.from_numpy(a["inv_freq_c"]), meta["pos_scale_c"],
+                                      meta["rope_scale_c"], select_score=meta["select_score"], **kw)
+    elif meta["module"] == "shared_selection_triton_exact":
+        res = ex1.shared_pi_attention(q, k, v, tau, torch.from_numpy(a["inv_freq_a"]),
+                                      meta["pos_scale_a"], rope_scale=meta["rope_scale_a"], **kw)
+    else:
+        res = ex2.shared_pi_attention(q, k, v, tau, torch.from_numpy(a["inv_freq_a"]),
+                                      meta["pos_scale_a"], rope_scale=meta["rope_scale_a"],
+                                      select_score=meta["select_score"], **kw)
+    out = res[0][0]
+    assert out.dtype == torch.float32 and out.shape == q.shape[1:]
+    sel = oracle.select_vote(a["q"], a["k"], a["tau"], a["inv_freq_a"], meta["pos_scale_a"],
+                             meta["rope_scale_a"], 1.0 / math.sqrt(meta["D"]), meta["T"])
+    if sel["boundary"] == 0:
+        np.testing.assert_array_equal(res[1].cpu().numpy(), a["shared_size"])
+        np.testing.assert_array_equal(res[2].cpu().numpy(), a["kept_size"])
+        np.testing.assert_array_equal(res[3].cpu().numpy(), a["kpct"])
+        np.testing.assert_array_equal(res[4].cpu().numpy(), a["overflow"].astype(bool))
+        assert_close_out(out, a["out"], torch.float32)
+    assert res[1].dtype == torch.int64 and res[4].dtype == torch.bool
+
+
+@pytest.mark.parametrize("name", names("pq_union"))
+def test_pq_union_end_to_end_vs_reference(name):
+    meta, a = load(name)
+    q, k, v = (cu(a[x])[None] for x in ("q", "k", "v"))
+    out, usize, kept, ovf = pq.shared_pq_attention(
+        q, k, v, torch.from_numpy(a["tau"]), torch.from_numpy(a["inv_freq_a"]),
+        torch.from_numpy(a["inv_freq_c"]), meta["pos_scale_a"], meta["rope_scale_a"],
+        k_max=meta["k_max"], select_score=meta["select_score"])
+    np.testing.assert_array_equal(usize.cpu().numpy(), a["usize"])
+    np.testing.assert_array_equal(kept.cpu().numpy(), a["kept_size"])
+    assert_close_out(out[0], a["out"], torch.float32)
+    assert_close_out(out[0], a["out_torch_golden"], torch.float32)
+
+
+@pytest.mark.parametrize("name", names("pqstream"))
+def test_pqstream_end_to_end_vs_reference(name):
+    meta, a = load(name)
+    q, k, v = (cu(a[x])[None] for x in ("q", "k", "v"))
+    out, span, kept, blocks, skipped = pqs.pqstream_attention(
+        q, k, v, torch.from_numpy(a["tau"]), torch.from_numpy(a["inv_freq_a"]),
+        torch.from_numpy(a["inv_freq_c"]), meta["pos_scale_a"], meta["rope_scale_a"],
+        block_n=meta["block_n"], pos_advance=meta["pos_advance"], use_skip=meta["use_skip"])
+    np.testing.assert_array_equal(span.cpu().numpy(), a["span"])
+    np.testing.assert_array_equal(kept.cpu().numpy(), a["kept"])
+    np.testing.assert_array_equal(blocks.cpu().numpy(), a["blocks"])
+    np.testing.assert_array_equal(skipped.cpu().numpy(), a["skipped"])
+    ok = np.isfinite(a["out"])
+    got = out[0].float().cpu().numpy()
+    assert np.abs(got[ok] - a["out"][ok]).max() <= F32_TOL
+
+
+# ---------------------------------------------------------------------------------------------
+# bf16 / GQA / larger shapes against the oracle (the interpreter cannot run bf16)
+# ---------------------------------------------------------------------------------------------
+BF16_CASES = [
+    # H, Hkv, N, D, T, geom, select_score, k_max, seed
+    (4, 1, 1024, 128, 64, "yarn", "freq", 256, 40),
+    (2, 2, 777, 64, 32, "pi", "expmass", 200, 41),
+    (4, 4, 1536, 128, 64, "pi", "freq", 2048, 42),
+]
+
+
+@pytest.mark.parametrize("case", BF16_CASES, ids=[f"bf16_{i}" for i in range(len(BF16_CASES))])
+def test_shared_bf16_gqa_vs_oracle(case):
+    H, Hk, N, D, T, geom, score, k_max, seed = case
+    q, k, v = make_inputs(SynthSpec(n_heads=H, n_kv_heads=Hk, seq_len=N, head_dim=D,
+                                    n_planted=16, seed=seed, dtype=torch.bfloat16))
+    tau = torch.full((H,), 5.0)
+    if geom == "yarn":
+        invf, rs = yarn_inv_freq(D, 5e5, 4.0, 256)
+        ps = 1.0
+    else:
+        invf, rs, ps = rope_inv_freq(D, 1e4), 1.0, 0.5
+    res = ex2.shared_pi_attention(cu(q), cu(k), cu(v), tau, invf, ps, rope_scale=rs, tile=T,
+                                  k_max=k_max, select_score=score)
+    G = H // Hk
+    qx, kx, vx = (x[0].float().numpy() for x in (q, k, v))
+    kx, vx = np.repeat(kx, G, 0), np.repeat(vx, G, 0)
+    o = oracle.shared_attention(qx, kx, vx, tau.numpy(), invf.numpy(), ps, rs, invf.numpy(), ps,
+                                rs, tile=T, k_max=k_max, select_score=score, v_is_bf16=True)
+    if o[-1]["select"]["boundary"] == 0:
+        np.testing.assert_array_equal(res[2].cpu().numpy(), o[2])
+    err = np.abs(res[0][0].float().cpu().numpy() - o[0])
+    # bf16 output rounding + bf16 P rounding, plus rare boundary-key flips
+    assert err.mean() <= BF16_MEAN, err.mean()
+    assert np.quantile(err, 0.9999) <= BF16_MAX, err.max()
+
+
+def test_pq_bf16_vs_oracle():
+    H, N, D = 2, 640, 128
+    q, k, v = make_inputs(SynthSpec(n_heads=H, n_kv_heads=H, seq_len=N, head_dim=D, seed=50,
+                                    dtype=torch.bfloat16))
+    tau = torch.full((H,), 5.0)
+    invf = rope_inv_freq(D, 1e4)
+    out, usize, kept, ovf = pq.shared_pq_attention(cu(q), cu(k), cu(v), tau, invf, invf,
+                                                   0.5, 1.0, k_max=256)
+    o = oracle.pq_attention(*(x[0].float().numpy() for x in (q, k, v)), tau.numpy(),
+                            invf.numpy(), invf.numpy(), 0.5, 1.0, k_max=256, v_is_bf16=True)
+    err = np.abs(out[0].float().cpu().numpy() - o[0])
+    assert err.mean() <= BF16_MEAN and np.quantile(err, 0.9999) <= BF16_MAX
+
+
+def test_pqstream_bf16_vs_oracle():
+    H, N, D = 2, 600, 128
+    q, k, v = make_inputs(SynthSpec(n_heads=H, n_kv_heads=1, seq_len=N, head_dim=D, seed=51,
+                                    dtype=torch.bfloat16))
+    tau = torch.full((H,), 5.0)
+    invf = rope_inv_freq(D, 1e4)
+    out, span, kept, _, _ = pqs.pqstream_attention(cu(q), cu(k), cu(v), tau, invf, invf, 0.5,
+                                                    block_n=64)
+    kx = np.repeat(k[0].float().numpy(), H, 0)
+    vx = np.repeat(v[0].float().numpy(), H, 0)
+    o = oracle.pqstream_attention(q[0].float().numpy(), kx, vx, tau.numpy(), invf.numpy(),
+                                  invf.numpy(), 0.5, block_n=64, v_is_bf16=True)
+    err = np.abs(out[0].float().cpu().numpy() - o[0])
+    assert err.mean() <= BF16_MEAN and np.quantile(err, 0.9999) <= BF16_MAX
+
+
+def test_pqstream_tau_inf_full_is_dense_rope():
+    """Invariant oracle of pqstream_kernel.py:301-307: tau=+inf with pos_advance='full'
+    reproduces native-RoPE dense causal attention."""
+    H, N, D = 2, 320, 64
+    q, k, v = make_inputs(SynthSpec(n_heads=H, n_kv_heads=H, seq_len=N, head_dim=D, seed=52))
+    invf = rope_inv_freq(D, 1e4)
+    out, *_ = pqs.pqstream_attention(cu(q), cu(k), cu(v), torch.full((H,), float("inf")), invf,
+                                     invf, pos_advance="full")
+    ref = oracle.dense_rope_attention(q[0].numpy(), k[0].numpy(), v[0].numpy(), invf.numpy())
+    assert np.abs(out[0].cpu().numpy() - ref).max() <= 2e-4
+
+
+def test_errors_are_loud():
+    q = torch.zeros((1, 2, 64, 64), device=DEV, dtype=torch.float16)
+    with pytest.raises(TypeError):
+        ex2.shared_pi_attention(q, q, q, torch.ones(2), rope_inv_freq(64, 1e4))
+    q = torch.zeros((1, 2, 64, 64), device=DEV)
+    with pytest.raises(NotImplementedError):
+        ex2.shared_pi_attention(q, q, q, torch.ones(2), rope_inv_freq(64, 1e4), q_pos_base=3)
+    with pytest.raises((ValueError, RuntimeError)):
+        ex2.shared_pi_attention(q, q, q, torch.ones(2), rope_inv_freq(64, 1e4), tile=48)
