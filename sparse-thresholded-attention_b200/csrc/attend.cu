@@ -7,8 +7,10 @@
 //   online softmax over 64-slot blocks with the reference's -inf guard, P rounded to the value
 //   dtype before the PV product, out = acc / l.
 // Differences in execution only: the slot loop stops at the tile's kept size instead of
-// sweeping all k_max slots (padding slots contribute exactly nothing), QK uses the 3xBF16 split
-// (fp32-accurate) and an fp32 V uses the split for PV too.
+// sweeping all k_max slots (padding slots contribute exactly nothing); QK runs on bf16 tensor
+// cores with the rotated fp32 operands split into bf16 pieces (2 pieces / 3 products for bf16
+// inputs, 3 pieces / 6 products -- fp32-accurate -- for fp32 inputs, where P and V are split
+// the same way).
 #include "common.cuh"
 #include "mma_frag.cuh"
 #include "sta_internal.h"
@@ -56,14 +58,13 @@ gather_attend_kernel(const AttendP p) {
   constexpr int NTH = NW * 32;
   constexpr int LD = D + 8;  // padded smem row (bf16 elements)
   constexpr int HALF = D / 2;
+  constexpr int NQ = F32 ? 3 : 2;  // bf16 pieces of the rotated Q / K rows
+  constexpr int NV = F32 ? 3 : 1;  // pieces of P and V (1: P rounded to bf16 like the reference)
   extern __shared__ __align__(16) uint8_t smem[];
-  __nv_bfloat16* sQh = reinterpret_cast<__nv_bfloat16*>(smem);
-  __nv_bfloat16* sQl = sQh + T * LD;
-  __nv_bfloat16* sKh = sQl + T * LD;
-  __nv_bfloat16* sKl = sKh + BK * LD;
-  __nv_bfloat16* sVh = sKl + BK * LD;
-  __nv_bfloat16* sVl = sVh + BK * LD;  // used when F32
-  int* sIdx = reinterpret_cast<int*>(sVl + (F32 ? BK * LD : 0));
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem);   // [NQ][T][LD]
+  __nv_bfloat16* sK = sQ + NQ * T * LD;                           // [NQ][BK][LD]
+  __nv_bfloat16* sV = sK + NQ * BK * LD;                          // [NV][BK][LD]
+  int* sIdx = reinterpret_cast<int*>(sV + NV * BK * LD);
   float* sNpk = reinterpret_cast<float*>(sIdx + BK);
   int* sMask = reinterpret_cast<int*>(sNpk + BK);
 
@@ -71,6 +72,7 @@ gather_attend_kernel(const AttendP p) {
   const int64_t bh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c4 = lane & 3;
+  const int mi = lane >> 3, rr = lane & 7;
   const int64_t N = p.N;
   const int64_t kvh = (bh / p.H) * p.Hkv + (bh % p.H) / (p.H / p.Hkv);
   const TV* qg = static_cast<const TV*>(p.q) + bh * p.qsh;
@@ -81,8 +83,9 @@ gather_attend_kernel(const AttendP p) {
   const float* npk_row = p.npk + row_base * p.k_max;
   const float* npq_row = p.npq + row_base * T;
   const int32_t* mask_row = p.mask ? p.mask + row_base * p.k_max : nullptr;
+  const bool use_mask = mask_row != nullptr;
 
-  // ---- Q prologue: rotate at newpos_q, split, stage, load A fragments
+  // ---- Q prologue: rotate at newpos_q, split into pieces, stage in smem
   for (int it = tid; it < T * HALF; it += NTH) {
     const int r = it / HALF, f = it % HALF;
     const int64_t qp = (int64_t)t * T + r;
@@ -94,24 +97,13 @@ gather_attend_kernel(const AttendP p) {
     const float ang = __fmul_rn(npq_row[r], __ldg(p.inv_freq + f));
     float r1, r2;
     rope_pair(x1, x2, ang, p.rope_scale, r1, r2);
-    __nv_bfloat16 h1, l1, h2, l2;
-    split_bf16(r1, h1, l1);
-    split_bf16(r2, h2, l2);
-    sQh[r * LD + f] = h1;
-    sQl[r * LD + f] = l1;
-    sQh[r * LD + f + HALF] = h2;
-    sQl[r * LD + f + HALF] = l2;
-  }
-  __syncthreads();
-  uint32_t qa_h[D / 16][4], qa_l[D / 16][4];
-  {
-    const int mi = lane >> 3;
-    const int r = warp * 16 + (lane & 7) + (mi & 1) * 8;
+    __nv_bfloat16 a[NQ], b[NQ];
+    split_pieces<NQ>(r1, a);
+    split_pieces<NQ>(r2, b);
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      const int col = ks * 16 + (mi >> 1) * 8;
-      ldsm_x4(smem_u32(sQh + r * LD + col), qa_h[ks][0], qa_h[ks][1], qa_h[ks][2], qa_h[ks][3]);
-      ldsm_x4(smem_u32(sQl + r * LD + col), qa_l[ks][0], qa_l[ks][1], qa_l[ks][2], qa_l[ks][3]);
+    for (int i = 0; i < NQ; ++i) {
+      sQ[(i * T + r) * LD + f] = a[i];
+      sQ[(i * T + r) * LD + f + HALF] = b[i];
     }
   }
 
@@ -137,7 +129,7 @@ gather_attend_kernel(const AttendP p) {
       if (slot < p.k_max) {
         id = idx_row[slot];
         if (id < N) np = npk_row[slot];
-        if (mask_row) mk = mask_row[slot];
+        if (use_mask) mk = mask_row[slot];
       }
       sIdx[i] = id;
       sNpk[i] = np;
@@ -156,50 +148,47 @@ gather_attend_kernel(const AttendP p) {
       const float ang = __fmul_rn(sNpk[i], __ldg(p.inv_freq + f));
       float r1, r2;
       rope_pair(x1, x2, ang, p.rope_scale, r1, r2);
-      __nv_bfloat16 h1, l1, h2, l2;
-      split_bf16(r1, h1, l1);
-      split_bf16(r2, h2, l2);
-      sKh[i * LD + f] = h1;
-      sKl[i * LD + f] = l1;
-      sKh[i * LD + f + HALF] = h2;
-      sKl[i * LD + f + HALF] = l2;
+      __nv_bfloat16 a[NQ], b[NQ];
+      split_pieces<NQ>(r1, a);
+      split_pieces<NQ>(r2, b);
+#pragma unroll
+      for (int j = 0; j < NQ; ++j) {
+        sK[(j * BK + i) * LD + f] = a[j];
+        sK[(j * BK + i) * LD + f + HALF] = b[j];
+      }
     }
     for (int it = tid; it < BK * D; it += NTH) {
       const int i = it / D, d = it % D;
       const int id = sIdx[i];
       const float x = id < N ? ldf(vg + (int64_t)id * p.vsn + d) : 0.f;
-      if (F32) {
-        __nv_bfloat16 h, l;
-        split_bf16(x, h, l);
-        sVh[i * LD + d] = h;
-        sVl[i * LD + d] = l;
-      } else {
-        sVh[i * LD + d] = __float2bfloat16_rn(x);
-      }
+      __nv_bfloat16 a[NV];
+      split_pieces<NV>(x, a);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) sV[(j * BK + i) * LD + d] = a[j];
     }
     __syncthreads();
 
     float s[BK / 8][4];
 #pragma unroll
     for (int i = 0; i < BK / 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-    {
-      const int mi = lane >> 3, rr = lane & 7;
 #pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
+    for (int ks = 0; ks < D / 16; ++ks) {
+      uint32_t a[NQ][4];
+      const int ar = warp * 16 + rr + (mi & 1) * 8;
+      const int ac = ks * 16 + (mi >> 1) * 8;
 #pragma unroll
-        for (int np2 = 0; np2 < BK / 16; ++np2) {
-          const int row = (2 * np2 + (mi >> 1)) * 8 + rr;
-          const int col = ks * 16 + (mi & 1) * 8;
-          uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
-          ldsm_x4(smem_u32(sKh + row * LD + col), h0, h1, h2, h3);
-          ldsm_x4(smem_u32(sKl + row * LD + col), l0, l1, l2, l3);
-          mma_bf16(s[2 * np2], qa_h[ks], h0, h1);
-          mma_bf16(s[2 * np2], qa_h[ks], l0, l1);
-          mma_bf16(s[2 * np2], qa_l[ks], h0, h1);
-          mma_bf16(s[2 * np2 + 1], qa_h[ks], h2, h3);
-          mma_bf16(s[2 * np2 + 1], qa_h[ks], l2, l3);
-          mma_bf16(s[2 * np2 + 1], qa_l[ks], h2, h3);
-        }
+      for (int j = 0; j < NQ; ++j)
+        ldsm_x4(smem_u32(sQ + (j * T + ar) * LD + ac), a[j][0], a[j][1], a[j][2], a[j][3]);
+#pragma unroll
+      for (int np2 = 0; np2 < BK / 16; ++np2) {
+        const int row = (2 * np2 + (mi >> 1)) * 8 + rr;
+        const int col = ks * 16 + (mi & 1) * 8;
+        uint32_t b0[NQ][2], b1[NQ][2];
+#pragma unroll
+        for (int j = 0; j < NQ; ++j)
+          ldsm_x4(smem_u32(sK + (j * BK + row) * LD + col), b0[j][0], b0[j][1], b1[j][0], b1[j][1]);
+        mma_pieces<NQ>(s[2 * np2], a, b0);
+        mma_pieces<NQ>(s[2 * np2 + 1], a, b1);
       }
     }
     // scale + mask, row max
@@ -212,7 +201,7 @@ gather_attend_kernel(const AttendP p) {
         const int row = e < 2 ? ra : rb;
         const int64_t qp = e < 2 ? qpa : qpb;
         const int id = sIdx[col];
-        const bool keep = id < N && qp >= id && ((sMask[col] >> row) & 1);
+        const bool keep = id < N && qp >= id && (!use_mask || ((sMask[col] >> row) & 1));
         const float v = keep ? __fmul_rn(s[nt][e], p.sm_scale) : -INFINITY;
         s[nt][e] = v;
         if (e < 2) mxA = fmaxf(mxA, v);
@@ -253,46 +242,39 @@ gather_attend_kernel(const AttendP p) {
     mA = mnA;
     mB = mnB;
     // PV
-    {
-      const int mi = lane >> 3, rr = lane & 7;
 #pragma unroll
-      for (int kk = 0; kk < BK / 16; ++kk) {
-        uint32_t ph[4], pl[4];
-        if (F32) {
-          pack_split(s[2 * kk][0], s[2 * kk][1], ph[0], pl[0]);
-          pack_split(s[2 * kk][2], s[2 * kk][3], ph[1], pl[1]);
-          pack_split(s[2 * kk + 1][0], s[2 * kk + 1][1], ph[2], pl[2]);
-          pack_split(s[2 * kk + 1][2], s[2 * kk + 1][3], ph[3], pl[3]);
-        } else {
-          ph[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-          ph[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-          ph[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-          ph[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-        }
-        const int row = kk * 16 + rr + (mi & 1) * 8;
+    for (int kk = 0; kk < BK / 16; ++kk) {
+      uint32_t pp[NV][4];
+      {
+        uint32_t x0[NV], x1[NV], x2[NV], x3[NV];
+        pack_pieces<NV>(s[2 * kk][0], s[2 * kk][1], x0);
+        pack_pieces<NV>(s[2 * kk][2], s[2 * kk][3], x1);
+        pack_pieces<NV>(s[2 * kk + 1][0], s[2 * kk + 1][1], x2);
+        pack_pieces<NV>(s[2 * kk + 1][2], s[2 * kk + 1][3], x3);
 #pragma unroll
-        for (int dp = 0; dp < D / 16; ++dp) {
-          const int col = (2 * dp + (mi >> 1)) * 8;
-          uint32_t v0, v1, v2, v3;
-          ldsm_x4_t(smem_u32(sVh + row * LD + col), v0, v1, v2, v3);
-          mma_bf16(o[2 * dp], ph, v0, v1);
-          mma_bf16(o[2 * dp + 1], ph, v2, v3);
-          if (F32) {
-            uint32_t w0, w1, w2, w3;
-            ldsm_x4_t(smem_u32(sVl + row * LD + col), w0, w1, w2, w3);
-            mma_bf16(o[2 * dp], ph, w0, w1);
-            mma_bf16(o[2 * dp + 1], ph, w2, w3);
-            mma_bf16(o[2 * dp], pl, v0, v1);
-            mma_bf16(o[2 * dp + 1], pl, v2, v3);
-          }
+        for (int j = 0; j < NV; ++j) {
+          pp[j][0] = x0[j];
+          pp[j][1] = x1[j];
+          pp[j][2] = x2[j];
+          pp[j][3] = x3[j];
         }
+      }
+      const int row = kk * 16 + rr + (mi & 1) * 8;
+#pragma unroll
+      for (int dp = 0; dp < D / 16; ++dp) {
+        const int col = (2 * dp + (mi >> 1)) * 8;
+        uint32_t v0[NV][2], v1[NV][2];
+#pragma unroll
+        for (int j = 0; j < NV; ++j)
+          ldsm_x4_t(smem_u32(sV + (j * BK + row) * LD + col), v0[j][0], v0[j][1], v1[j][0], v1[j][1]);
+        mma_pieces<NV>(o[2 * dp], pp, v0);
+        mma_pieces<NV>(o[2 * dp + 1], pp, v1);
       }
     }
   }
 
   // ---- epilogue
   TV* og = static_cast<TV*>(p.out) + bh * N * D;
-  const float iA = 1.f / lA, iB = 1.f / lB;
 #pragma unroll
   for (int dt = 0; dt < D / 8; ++dt) {
     const int col = dt * 8 + 2 * c4;
@@ -313,14 +295,13 @@ gather_attend_kernel(const AttendP p) {
       }
     }
   }
-  (void)iA;
-  (void)iB;
 }
 
 template <int D, int T, bool F32>
 int launch_one(const AttendP& p, cudaStream_t stream) {
   constexpr int LD = D + 8;
-  const size_t smem = (size_t)(2 * T * LD + 2 * BK * LD + (F32 ? 2 : 1) * BK * LD) * 2 + 3 * BK * 4;
+  constexpr int NQ = F32 ? 3 : 2, NV = F32 ? 3 : 1;
+  const size_t smem = (size_t)(NQ * T * LD + NQ * BK * LD + NV * BK * LD) * 2 + 3 * BK * 4;
   auto kern = gather_attend_kernel<D, T, F32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return fail(STA_ERR_CUDA, cudaGetErrorString(e));
@@ -338,6 +319,8 @@ int launch_gather_attend(const sta_attend_args* a, cudaStream_t stream) {
     return fail(STA_ERR_ARG, "sta_gather_attend: null pointer");
   if (a->d != 64 && a->d != 128) return fail(STA_ERR_UNSUPPORTED, "sta_gather_attend: d must be 64 or 128");
   if (a->tile != 32 && a->tile != 64) return fail(STA_ERR_UNSUPPORTED, "sta_gather_attend: tile must be 32 or 64");
+  if (a->mask && a->tile != 32)
+    return fail(STA_ERR_UNSUPPORTED, "sta_gather_attend: a per-query mask needs tile 32");
   if (a->n_heads <= 0 || a->n_kv_heads <= 0 || a->n_heads % a->n_kv_heads)
     return fail(STA_ERR_ARG, "sta_gather_attend: bad head counts");
   if (a->n <= 0 || a->batch <= 0) return STA_OK;

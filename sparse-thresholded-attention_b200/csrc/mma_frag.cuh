@@ -48,3 +48,49 @@ __device__ __forceinline__ void pack_split(float x0, float x1, uint32_t& hi, uin
 }
 
 }  // namespace sta
+
+namespace sta {
+
+// x ~= sum_i piece_i, each piece a bf16 (NP = 1: plain rounding, 2: hi + lo, 3: hi + mid + lo).
+// Every residual is formed exactly in fp32, so NP pieces keep ~8*NP significant bits.
+template <int NP>
+__device__ __forceinline__ void split_pieces(float x, __nv_bfloat16 (&o)[NP]) {
+  float r = x;
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    o[i] = __float2bfloat16_rn(r);
+    r = __fsub_rn(r, __bfloat162float(o[i]));
+  }
+}
+
+// two fp32 values -> NP packed bf16x2 pieces
+template <int NP>
+__device__ __forceinline__ void pack_pieces(float x0, float x1, uint32_t (&o)[NP]) {
+  __nv_bfloat16 a[NP], b[NP];
+  split_pieces<NP>(x0, a);
+  split_pieces<NP>(x1, b);
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    __nv_bfloat162 v;
+    v.x = a[i];
+    v.y = b[i];
+    o[i] = *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// C += sum over piece pairs (pa, pb) with pa + pb < NP of A_pa * B_pb, smallest terms first.
+// NP = 2 gives the 3-product "3xBF16" form, NP = 3 the 6-product fp32-accurate form.
+template <int NP>
+__device__ __forceinline__ void mma_pieces(float (&c)[4], const uint32_t (&a)[NP][4],
+                                           const uint32_t (&b)[NP][2]) {
+#pragma unroll
+  for (int s = NP - 1; s >= 0; --s) {
+#pragma unroll
+    for (int pa = s; pa >= 0; --pa) {
+      const int pb = s - pa;
+      mma_bf16(c, a[pa], b[pb][0], b[pb][1]);
+    }
+  }
+}
+
+}  // namespace sta

@@ -55,9 +55,9 @@ __device__ __forceinline__ float ldv<__nv_bfloat16>(const __nv_bfloat16* p) {
   return __bfloat162float(*p);
 }
 
-template <int D, int BN>
-__device__ __forceinline__ void score_tile(const __nv_bfloat16* sAh, const __nv_bfloat16* sAl,
-                                           const __nv_bfloat16* sBh, const __nv_bfloat16* sBl,
+// s (16 rows of this warp x BN keys) = sum of piece products of A [NP][T][LD] and B [NP][BN][LD]
+template <int D, int BN, int NP>
+__device__ __forceinline__ void score_tile(const __nv_bfloat16* sA, const __nv_bfloat16* sB,
                                            float (&s)[BN / 8][4]) {
   constexpr int LD = D + 8;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -66,24 +66,22 @@ __device__ __forceinline__ void score_tile(const __nv_bfloat16* sAh, const __nv_
   for (int i = 0; i < BN / 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
 #pragma unroll
   for (int ks = 0; ks < D / 16; ++ks) {
-    uint32_t ah[4], al[4];
+    uint32_t a[NP][4];
     const int ar = warp * 16 + rr + (mi & 1) * 8;
     const int ac = ks * 16 + (mi >> 1) * 8;
-    ldsm_x4(smem_u32(sAh + ar * LD + ac), ah[0], ah[1], ah[2], ah[3]);
-    ldsm_x4(smem_u32(sAl + ar * LD + ac), al[0], al[1], al[2], al[3]);
+#pragma unroll
+    for (int j = 0; j < NP; ++j)
+      ldsm_x4(smem_u32(sA + (j * T + ar) * LD + ac), a[j][0], a[j][1], a[j][2], a[j][3]);
 #pragma unroll
     for (int np2 = 0; np2 < BN / 16; ++np2) {
       const int row = (2 * np2 + (mi >> 1)) * 8 + rr;
       const int col = ks * 16 + (mi & 1) * 8;
-      uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
-      ldsm_x4(smem_u32(sBh + row * LD + col), h0, h1, h2, h3);
-      ldsm_x4(smem_u32(sBl + row * LD + col), l0, l1, l2, l3);
-      mma_bf16(s[2 * np2], ah, h0, h1);
-      mma_bf16(s[2 * np2], ah, l0, l1);
-      mma_bf16(s[2 * np2], al, h0, h1);
-      mma_bf16(s[2 * np2 + 1], ah, h2, h3);
-      mma_bf16(s[2 * np2 + 1], ah, l2, l3);
-      mma_bf16(s[2 * np2 + 1], al, h2, h3);
+      uint32_t b0[NP][2], b1[NP][2];
+#pragma unroll
+      for (int j = 0; j < NP; ++j)
+        ldsm_x4(smem_u32(sB + (j * BN + row) * LD + col), b0[j][0], b0[j][1], b1[j][0], b1[j][1]);
+      mma_pieces<NP>(s[2 * np2], a, b0);
+      mma_pieces<NP>(s[2 * np2 + 1], a, b1);
     }
   }
 }
@@ -93,17 +91,14 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   using TV = typename std::conditional<F32, float, __nv_bfloat16>::type;
   constexpr int LD = D + 8;
   constexpr int HALF = D / 2;
+  constexpr int NQ = F32 ? 3 : 2;  // pieces of the attend-geometry Q / K
+  constexpr int NV = F32 ? 3 : 1;  // pieces of P / V
   extern __shared__ __align__(16) uint8_t smem[];
-  __nv_bfloat16* sQsh = reinterpret_cast<__nv_bfloat16*>(smem);  // select-geometry Q
-  __nv_bfloat16* sQsl = sQsh + T * LD;
-  __nv_bfloat16* sQah = sQsl + T * LD;                            // attend-geometry Q
-  __nv_bfloat16* sQal = sQah + T * LD;
-  __nv_bfloat16* sKsh = sQal + T * LD;                            // select-geometry K block
-  __nv_bfloat16* sKsl = sKsh + BN * LD;
-  __nv_bfloat16* sKah = sKsl + BN * LD;                           // attend-geometry K block
-  __nv_bfloat16* sKal = sKah + BN * LD;
-  __nv_bfloat16* sVh = sKal + BN * LD;
-  __nv_bfloat16* sVl = sVh + BN * LD;
+  __nv_bfloat16* sQs = reinterpret_cast<__nv_bfloat16*>(smem);  // [2][T][LD] select geometry
+  __nv_bfloat16* sQa = sQs + 2 * T * LD;                         // [NQ][T][LD] attend geometry
+  __nv_bfloat16* sKs = sQa + NQ * T * LD;                        // [2][BN][LD]
+  __nv_bfloat16* sKa = sKs + 2 * BN * LD;                        // [NQ][BN][LD]
+  __nv_bfloat16* sV = sKa + NQ * BN * LD;                        // [NV][BN][LD]
   __shared__ int s_cmax[NW];
 
   const int t = blockIdx.x;
@@ -132,8 +127,8 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
     const int r = it / D, d = it % D;
     const int64_t qp = tstart + r;
     __nv_bfloat16 zh = __float2bfloat16_rn(0.f);
-    sQsh[r * LD + d] = qp < N ? qhg[qp * D + d] : zh;
-    sQsl[r * LD + d] = qp < N ? qlg[qp * D + d] : zh;
+    sQs[r * LD + d] = qp < N ? qhg[qp * D + d] : zh;
+    sQs[(T + r) * LD + d] = qp < N ? qlg[qp * D + d] : zh;
   }
   for (int it = tid; it < T * HALF; it += NTH) {
     const int r = it / HALF, f = it % HALF;
@@ -147,13 +142,14 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
     const float ang = __fmul_rn(npq, __ldg(p.inv_freq_c + f));
     float r1, r2;
     rope_pair(x1, x2, ang, 1.f, r1, r2);
-    __nv_bfloat16 h1, l1, h2, l2;
-    split_bf16(r1, h1, l1);
-    split_bf16(r2, h2, l2);
-    sQah[r * LD + f] = h1;
-    sQal[r * LD + f] = l1;
-    sQah[r * LD + f + HALF] = h2;
-    sQal[r * LD + f + HALF] = l2;
+    __nv_bfloat16 a[NQ], b[NQ];
+    split_pieces<NQ>(r1, a);
+    split_pieces<NQ>(r2, b);
+#pragma unroll
+    for (int j = 0; j < NQ; ++j) {
+      sQa[(j * T + r) * LD + f] = a[j];
+      sQa[(j * T + r) * LD + f + HALF] = b[j];
+    }
   }
 
   const int ra = warp * 16 + g, rb = ra + 8;
@@ -179,17 +175,13 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
       const int i = it / D, d = it % D;
       const int64_t j = sn + i;
       __nv_bfloat16 zh = __float2bfloat16_rn(0.f);
-      sKsh[i * LD + d] = j < N ? khg[j * D + d] : zh;
-      sKsl[i * LD + d] = j < N ? klg[j * D + d] : zh;
+      sKs[i * LD + d] = j < N ? khg[j * D + d] : zh;
+      sKs[(BN + i) * LD + d] = j < N ? klg[j * D + d] : zh;
       const float x = j < N ? ldv(vg + j * p.vsn + d) : 0.f;
-      if (F32) {
-        __nv_bfloat16 h, l;
-        split_bf16(x, h, l);
-        sVh[i * LD + d] = h;
-        sVl[i * LD + d] = l;
-      } else {
-        sVh[i * LD + d] = __float2bfloat16_rn(x);
-      }
+      __nv_bfloat16 pv[NV];
+      split_pieces<NV>(x, pv);
+#pragma unroll
+      for (int q2 = 0; q2 < NV; ++q2) sV[(q2 * BN + i) * LD + d] = pv[q2];
     }
     for (int it = tid; it < BN * HALF; it += NTH) {
       const int i = it / HALF, f = it % HALF;
@@ -204,19 +196,20 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
       const float ang = __fmul_rn(npk, __ldg(p.inv_freq_c + f));
       float r1, r2;
       rope_pair(x1, x2, ang, 1.f, r1, r2);
-      __nv_bfloat16 h1, l1, h2, l2;
-      split_bf16(r1, h1, l1);
-      split_bf16(r2, h2, l2);
-      sKah[i * LD + f] = h1;
-      sKal[i * LD + f] = l1;
-      sKah[i * LD + f + HALF] = h2;
-      sKal[i * LD + f + HALF] = l2;
+      __nv_bfloat16 a[NQ], b[NQ];
+      split_pieces<NQ>(r1, a);
+      split_pieces<NQ>(r2, b);
+#pragma unroll
+      for (int q2 = 0; q2 < NQ; ++q2) {
+        sKa[(q2 * BN + i) * LD + f] = a[q2];
+        sKa[(q2 * BN + i) * LD + f + HALF] = b[q2];
+      }
     }
     __syncthreads();
 
     // selection scores and keep mask
     float s[BN / 8][4];
-    score_tile<D, BN>(sQsh, sQsl, sKsh, sKsl, s);
+    score_tile<D, BN, 2>(sQs, sKs, s);
     uint32_t keepbits[BN / 8];
     int cA = 0, cB = 0;
 #pragma unroll
@@ -255,7 +248,7 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
     if (p.use_skip && !(adv > 0.f)) continue;
 
     // attend scores at the streamed positions
-    score_tile<D, BN>(sQah, sQal, sKah, sKal, s);
+    score_tile<D, BN, NQ>(sQa, sKa, s);
     float mxA = -INFINITY, mxB = -INFINITY;
 #pragma unroll
     for (int nt = 0; nt < BN / 8; ++nt) {
@@ -305,34 +298,31 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
       const int mi = lane >> 3, rr = lane & 7;
 #pragma unroll
       for (int kk = 0; kk < BN / 16; ++kk) {
-        uint32_t ph[4], pl[4];
-        if (F32) {
-          pack_split(s[2 * kk][0], s[2 * kk][1], ph[0], pl[0]);
-          pack_split(s[2 * kk][2], s[2 * kk][3], ph[1], pl[1]);
-          pack_split(s[2 * kk + 1][0], s[2 * kk + 1][1], ph[2], pl[2]);
-          pack_split(s[2 * kk + 1][2], s[2 * kk + 1][3], ph[3], pl[3]);
-        } else {
-          ph[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-          ph[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-          ph[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-          ph[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+        uint32_t pp[NV][4];
+        {
+          uint32_t x0[NV], x1[NV], x2[NV], x3[NV];
+          pack_pieces<NV>(s[2 * kk][0], s[2 * kk][1], x0);
+          pack_pieces<NV>(s[2 * kk][2], s[2 * kk][3], x1);
+          pack_pieces<NV>(s[2 * kk + 1][0], s[2 * kk + 1][1], x2);
+          pack_pieces<NV>(s[2 * kk + 1][2], s[2 * kk + 1][3], x3);
+#pragma unroll
+          for (int j = 0; j < NV; ++j) {
+            pp[j][0] = x0[j];
+            pp[j][1] = x1[j];
+            pp[j][2] = x2[j];
+            pp[j][3] = x3[j];
+          }
         }
         const int row = kk * 16 + rr + (mi & 1) * 8;
 #pragma unroll
         for (int dp = 0; dp < D / 16; ++dp) {
           const int col = (2 * dp + (mi >> 1)) * 8;
-          uint32_t v0, v1, v2, v3;
-          ldsm_x4_t(smem_u32(sVh + row * LD + col), v0, v1, v2, v3);
-          mma_bf16(o[2 * dp], ph, v0, v1);
-          mma_bf16(o[2 * dp + 1], ph, v2, v3);
-          if (F32) {
-            uint32_t w0, w1, w2, w3;
-            ldsm_x4_t(smem_u32(sVl + row * LD + col), w0, w1, w2, w3);
-            mma_bf16(o[2 * dp], ph, w0, w1);
-            mma_bf16(o[2 * dp + 1], ph, w2, w3);
-            mma_bf16(o[2 * dp], pl, v0, v1);
-            mma_bf16(o[2 * dp + 1], pl, v2, v3);
-          }
+          uint32_t v0[NV][2], v1[NV][2];
+#pragma unroll
+          for (int j = 0; j < NV; ++j)
+            ldsm_x4_t(smem_u32(sV + (j * BN + row) * LD + col), v0[j][0], v0[j][1], v1[j][0], v1[j][1]);
+          mma_pieces<NV>(o[2 * dp], pp, v0);
+          mma_pieces<NV>(o[2 * dp + 1], pp, v1);
         }
       }
     }
@@ -376,7 +366,8 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
 template <int D, int BN, bool F32>
 int launch_one(const PQSP& p, cudaStream_t stream) {
   constexpr int LD = D + 8;
-  const size_t smem = (size_t)(4 * T * LD + 6 * BN * LD) * 2;
+  constexpr int NQ = F32 ? 3 : 2, NV = F32 ? 3 : 1;
+  const size_t smem = (size_t)((2 + NQ) * T * LD + (2 + NQ + NV) * BN * LD) * 2;
   auto kern = pqstream_kernel<D, BN, F32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return fail(STA_ERR_CUDA, cudaGetErrorString(e));

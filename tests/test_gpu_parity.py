@@ -43,7 +43,10 @@ def load(name):
 
 
 def cu(x, dtype=None):
-    t = torch.from_numpy(np.ascontiguousarray(x)).to(DEV)
+    if isinstance(x, torch.Tensor):
+        t = x.to(DEV)
+    else:
+        t = torch.from_numpy(np.ascontiguousarray(x)).to(DEV)
     return t.to(dtype) if dtype is not None else t
 
 
@@ -52,8 +55,11 @@ def names(pattern):
 
 
 def assert_close_out(got, ref, dtype):
-    err = (got.float().cpu().numpy() - np.asarray(ref, np.float32))
-    err = np.abs(err[np.isfinite(err)])
+    ref = np.asarray(ref, np.float32)
+    got = got.float().cpu().numpy()
+    ok = np.isfinite(ref)
+    assert np.isfinite(got[ok]).all(), "non-finite output where the reference is finite"
+    err = np.abs(got[ok] - ref[ok])
     if dtype == torch.float32:
         assert err.max() <= F32_TOL, err.max()
     else:
