@@ -1,0 +1,386 @@
+#!/usr/bin/env python3
+"""Prefill tokens/s per attention layer of exact-max shared-selection thresholded attention.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--variant shared]
+    python bench.py --impl reference ...      # the reference algorithm on the host cores
+
+Workload (default): benchmark config 2 -- Llama-3-8B-shaped GQA layer (32 q / 8 kv heads,
+D=128), S=32768, B=1, bf16, YaRN factor 4 (orig 8192, mscale 1.1386), exact max, tau=5,
+top 30% with the 25/20% fallback, cap 2048, query tile 64.  Synthetic seeded inputs
+(sta.synth) stand in for the model activations.  A "step" is one call of the attention op on
+pre-projected q, k, v: RoPE prologue + Kernel A (2 passes) + selection + attend.
+
+Multi-GPU: one process per GPU (torchrun); the 8 kv heads of the sequence are partitioned
+across ranks with no data-path collective (strong scaling: the job's total work is fixed).
+Timing: CUDA events on torch's current stream, W untimed warm-up steps, K timed steps between
+barrier + synchronize, max over ranks.  Inputs (268 MB of q alone) exceed L2 (126 MB).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "sparse-thresholded-attention_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "prefill tokens/s per attention layer"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["sta", "reference"], default="sta")
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--variant", choices=["shared", "pq_union", "pq_stream"], default="shared")
+    ap.add_argument("--seq-len", type=int, default=None, help="override S (profiling only)")
+    ap.add_argument("--heads", type=int, default=None, help="override q heads (profiling only)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def workload(args):
+    """Inputs + geometry of the benchmark config (full tensors, on the CPU)."""
+    import torch
+    from sta.synth import config, make_config_inputs, rope_inv_freq, yarn_inv_freq
+    c = config(args.config)
+    q, k, v, c = make_config_inputs(args.config, seq_len=args.seq_len, n_heads=args.heads)
+    D = c["D"]
+    if c["geom"] == "yarn":
+        invf, ms = yarn_inv_freq(D, c["theta"], c["yarn_factor"], c["yarn_orig"])
+        geo = dict(inv_freq=invf, pos_scale=1.0, rope_scale=ms)
+        geo_c = dict(geo)
+    else:
+        invf = rope_inv_freq(D, c["theta"])
+        geo = dict(inv_freq=invf, pos_scale=c.get("pos_scale", 1.0), rope_scale=1.0)
+        geo_c = dict(geo)
+    if args.variant != "shared":
+        geo_c = dict(inv_freq=rope_inv_freq(D, c["theta"]), pos_scale=1.0, rope_scale=1.0)
+    tau = torch.full((c["H"],), float(c["tau"]))
+    return q, k, v, tau, geo, geo_c, c
+
+
+def workload_desc(c, args, world):
+    name = c["name"] + ("" if args.variant == "shared" else f"-{args.variant}")
+    return {"workload": name, "batch": c["B"], "q_heads": c["H"], "kv_heads": c["Hkv"],
+            "seq_len": c["S"], "head_dim": c["D"], "tile": c["T"] if args.variant == "shared" else 32,
+            "k_max": c["k_max"], "tau": c["tau"], "pct": c.get("pct", 30.0),
+            "geometry": c["geom"], "parallelism": f"kv-head partition x{world}" if world > 1 else "single GPU",
+            "l2": "no flush: inputs exceed L2 (q alone %.0f MB > 126 MB)" % (c["B"] * c["H"] * c["S"] * c["D"] * 2 / 1e6)}
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baseline: the oracle restatement of the reference algorithm on a bounded sample
+# ---------------------------------------------------------------------------------------------
+def cpu_sample(q, k, v, tau, geo, c, n_tiles=12, head=0, seed=0):
+    """Run the reference algorithm (oracle port) on `n_tiles` query tiles of one q head and
+    extrapolate to the whole layer by causal work (cost of a tile ~ its key count).
+    Returns (tokens/s estimate, seconds spent, description)."""
+    import numpy as np
+    from oracle import sta_oracle as oracle
+    T, N, D, H, Hk = c["T"], c["S"], c["D"], c["H"], c["Hkv"]
+    nt = (N + T - 1) // T
+    rng = np.random.default_rng(seed)
+    tiles = sorted(rng.choice(nt, size=min(n_tiles, nt), replace=False).tolist())
+    kv = head // (H // Hk)
+    qh = q[0, head:head + 1].float().numpy()
+    kh = k[0, kv:kv + 1].float().numpy()
+    vh = v[0, kv:kv + 1].float().numpy()
+    invf = geo["inv_freq"].numpy()
+    sm = 1.0 / math.sqrt(D)
+    t0 = time.perf_counter()
+    sel = oracle.select_vote(qh, kh, tau[head:head + 1].numpy(), invf, geo["pos_scale"],
+                             geo["rope_scale"], sm, T, tiles=tiles)
+    idx = np.full((1, nt, c["k_max"]), N, np.int32)
+    npk = np.zeros((1, nt, c["k_max"]), np.float32)
+    npq = np.zeros((1, nt, T), np.float32)
+    for t in tiles:
+        s = oracle.build_sets(sel["votes"][:, t:t + 1], geo["pos_scale"], 32, 32, c["pct"], T,
+                              c["k_max"], q_pos_base=t * T)
+        idx[:, t], npk[:, t], npq[:, t] = s[0][:, 0], s[1][:, 0], s[2][:, 0]
+    oracle.gather_attn(qh, kh, vh, invf, idx, npk, npq, sm, geo["rope_scale"], T,
+                       v_is_bf16=True, tiles=tiles)
+    dt = time.perf_counter() - t0
+    work_sample = sum(min((t + 1) * T, N) for t in tiles)
+    work_total = H * c["B"] * sum(min((t + 1) * T, N) for t in range(nt))
+    est = dt * work_total / work_sample
+    tok_s = c["B"] * N / est
+    desc = (f"oracle port (numpy) on {len(tiles)} of {nt} query tiles of 1 of {H} q heads, "
+            f"{dt:.1f} s; extrapolated by causal key count to the whole layer ({est:.0f} s)")
+    return tok_s, dt, desc
+
+
+def run_reference(args):
+    """--impl reference: the reference's algorithm on the host cores (oracle port)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    q, k, v, tau, geo, geo_c, c = workload(args)
+    world = args.gpus
+    for i in range(args.warmup):
+        cpu_sample(q, k, v, tau, geo, c, n_tiles=2, seed=100 + i)
+    vals, secs = [], 0.0
+    t0 = time.perf_counter()
+    desc = ""
+    for i in range(args.steps):
+        tok, dt, desc = cpu_sample(q, k, v, tau, geo, c, n_tiles=48, seed=i)
+        vals.append(tok)
+        secs += dt
+    value = statistics.median(vals)
+    cores = os.cpu_count() or 1
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * c["B"] * c["S"] / value, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32 (numpy oracle on bf16 inputs)",
+            "data": "synthetic (seeded, sta.synth)", "config": workload_desc(c, args, 1),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "wall_s": time.perf_counter() - t0}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------------------------
+class ClockSampler:
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except Exception:
+                self.p.kill()
+
+    def summary(self):
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.f.name)
+        load = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+    from sta import core
+    from sta.core import Geometry
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", device_id=dev)
+    q, k, v, tau, geo, geo_c, c = workload(args)
+    H, Hk, N, D, B = c["H"], c["Hkv"], c["S"], c["D"], c["B"]
+    if Hk % world:
+        raise SystemExit(f"{Hk} kv heads do not split over {world} GPUs")
+    G = H // Hk
+    k0, k1 = rank * Hk // world, (rank + 1) * Hk // world
+    qs = q[:, k0 * G:k1 * G].contiguous()
+    ks = k[:, k0:k1].contiguous()
+    vs = v[:, k0:k1].contiguous()
+    taus = tau[k0 * G:k1 * G]
+    qd, kd, vd = qs.to(dev), ks.to(dev), vs.to(dev)
+    ga = Geometry(geo["inv_freq"], geo["pos_scale"], geo["rope_scale"])
+    gc = Geometry(geo_c["inv_freq"], geo_c["pos_scale"], geo_c["rope_scale"])
+    T = c["T"] if args.variant == "shared" else 32
+    kw = dict(tile=T, k_max=c["k_max"], pct=c.get("pct", 30.0), select_score="freq",
+              block_n=32)
+
+    def step(qq, kk, vv, evs=None):
+        return core.forward(args.variant, qq, kk, vv, taus, ga, gc, stage_events=evs, **kw)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        out, st, _ = step(qd, kd, vd)
+    torch.cuda.synchronize()
+
+    K = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(K)]
+    for row in evs:
+        for e in row:
+            e.record()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(K):
+            out, st, _ = step(qd, kd, vd, evs[i])
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+    ms_total = start.elapsed_time(end)
+    stage_ms = [0.0] * 4
+    for row in evs:
+        for j in range(4):
+            stage_ms[j] += row[j].elapsed_time(row[j + 1]) / K
+    t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t.item()) / K
+    tokens = B * N
+    value = tokens / (ms_step / 1e3)
+
+    # ---- end to end through the public API with host buffers (H2D + op + D2H per step)
+    e2e = None
+    if not args.no_e2e:
+        qh, kh, vh = qs.pin_memory(), ks.pin_memory(), vs.pin_memory()
+        out_h = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+        for _ in range(2):
+            o, _, _ = step(qh.to(dev, non_blocking=True), kh.to(dev, non_blocking=True),
+                           vh.to(dev, non_blocking=True))
+            out_h.copy_(o, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(K):
+            o, _, _ = step(qh.to(dev, non_blocking=True), kh.to(dev, non_blocking=True),
+                           vh.to(dev, non_blocking=True))
+            out_h.copy_(o, non_blocking=True)
+        e2.record()
+        torch.cuda.synchronize()
+        t2 = torch.tensor([s2.elapsed_time(e2)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t2.item()) / K
+        h2d = sum(x.numel() * x.element_size() for x in (qs, ks, vs))
+        e2e = {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": int(h2d) * world,
+               "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()) * world}
+
+    # ---- roofline of the dominant kernel (Kernel A on tensor cores)
+    pk, pk_kind = peaks()
+    Hr = qs.shape[1]
+    flops_sel = 2 * 2 * D * Hr * B * N * (N + 1) / 2 if args.variant != "pq_stream" else \
+        2 * D * Hr * B * N * (N + 1) / 2
+    sel_ms = stage_ms[1]
+    achieved = flops_sel / (sel_ms / 1e3) / 1e12
+    peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
+    traffic = select_traffic_bytes(c, Hr, args)
+    roof = {"kernel": "select_kernel (tcgen05 exact-max two-pass Kernel A)", "bound": "tensor",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "peak_kind": f"{pk_kind} bf16 sustained", "traffic": traffic,
+            "algorithmic_flops_per_launch": flops_sel, "launch_ms": sel_ms,
+            "tensor_flops_issued_per_launch": 3 * flops_sel,
+            "note": "3 bf16 products per fp32-accurate score (hi*hi + hi*lo + lo*hi)"}
+
+    launches_per_step = {"shared": 5, "pq_union": 5, "pq_stream": 4}[args.variant]
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import torch as _t
+        _t.set_num_threads(os.cpu_count() or 1)
+        tok_cpu, _, desc = cpu_sample(q, k, v, tau, geo, c, n_tiles=240)
+        cpu = {"value": tok_cpu, "unit": "tokens/s", "cores": os.cpu_count() or 1,
+               "kind": "port", "sample": desc}
+    stats = {}
+    if args.variant == "shared":
+        ks_ = st["kept_size"].float()
+        stats = {"mean_kept_size": float(ks_.mean()), "max_kept_size": float(ks_.max()),
+                 "overflow_frac": float(st["overflow"].float().mean()),
+                 "unresolved_frac": float(st["overflow20"].float().mean()),
+                 "fallback_tiles": int(((st["chosen"] > 0) & (st["chosen"] < 30)).sum())}
+    clocks = clk.summary()
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+                "steps": K, "warmup": args.warmup, "ms_per_step": ms_step,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (seeded generator sta.synth, BASELINE config shapes)",
+                "config": workload_desc(c, args, world), "clocks": clocks, "e2e": e2e,
+                "gpu_launches": launches_per_step * K,
+                "stage_ms": {"rope_prologue": stage_ms[0], "select_tcgen05": stage_ms[1],
+                             "build_sets": stage_ms[2], "attend": stage_ms[3]},
+                "roofline": roof, "cpu_baseline": cpu, "selection": stats}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def select_traffic_bytes(c, heads, args):
+    """DRAM bytes per select launch from the committed ncu summary, scaled by causal work."""
+    p = os.path.join(ROOT, "profiles", "select_kernel_traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        d = json.load(f)
+    scale = (heads * c["S"] * (c["S"] + 1)) / (d["heads"] * d["seq_len"] * (d["seq_len"] + 1))
+    return d["dram_bytes"] * scale
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -271,6 +271,10 @@ typedef struct sta_forward_args {
   /* scratch cap: the op runs over groups of kv heads so that its workspace stays below this
    * many bytes (0 = one group holding every kv head) */
   int64_t max_workspace_bytes;
+  /* optional: 5 cudaEvent_t recorded on `stream` before the RoPE prologue, before Kernel A,
+   * before the selection, before the attend kernel and at the end (NULL = none); with more
+   * than one kv-head group they bracket the last group */
+  void* const* stage_events;
 } sta_forward_args;
 
 size_t sta_shared_workspace_bytes(const sta_forward_args* a);

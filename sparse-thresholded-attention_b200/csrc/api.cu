@@ -197,6 +197,10 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       const uint8_t* vv = static_cast<const uint8_t*>(a->v) + k0 * a->v_stride_h * es;
       uint8_t* out = static_cast<uint8_t*>(a->out) + h0 * N * a->d * es;
       const float* tau = a->tau + g0 * G;
+      auto mark = [&](int i) {
+        if (a->stage_events) cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), st);
+      };
+      mark(0);
       STA_TRY(launch_rope_split(q, a->dtype, qn, N, a->d, a->q_stride_h, a->q_stride_n,
                                 a->inv_freq_a, a->pos_scale_a, a->rope_scale_a, w + L.qh,
                                 w + L.ql, st));
@@ -216,10 +220,12 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       s.tile = T;
       s.sm_scale = a->sm_scale;
       s.tau = tau;
+      mark(1);
       if (v == kPQStream) {
         s.max_only = 1;
         s.row_max = reinterpret_cast<float*>(w + L.rowmax);
         STA_TRY(launch_select(&s, st));
+        mark(2);
         sta_pqstream_args pa{};
         pa.q = q; pa.q_stride_h = a->q_stride_h; pa.q_stride_n = a->q_stride_n;
         pa.k = k; pa.k_stride_h = a->k_stride_h; pa.k_stride_n = a->k_stride_n;
@@ -246,7 +252,9 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
         pa.kept = a->kept_rows + h0 * N;
         pa.blocks = a->blocks + h0 * nt;
         pa.skipped = a->skipped + h0 * nt;
+        mark(3);
         STA_TRY(launch_pqstream(&pa, st));
+        mark(4);
         continue;
       }
       s.wmode = a->select_score;
@@ -254,6 +262,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       s.wvotes = a->select_score != STA_SCORE_FREQ ? reinterpret_cast<float*>(w + L.wvotes) : nullptr;
       s.bits = v == kPQUnion ? reinterpret_cast<uint32_t*>(w + L.bits) : nullptr;
       STA_TRY(launch_select(&s, st));
+      mark(2);
       int32_t* idx = a->idx_out ? a->idx_out + h0 * nt * kmax : reinterpret_cast<int32_t*>(w + L.idx);
       float* npk = a->newpos_k_out ? a->newpos_k_out + h0 * nt * kmax : reinterpret_cast<float*>(w + L.npk);
       float* npq = a->newpos_q_out ? a->newpos_q_out + h0 * nt * T : reinterpret_cast<float*>(w + L.npq);
@@ -304,6 +313,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
         ba.overflow = a->overflow + h0 * nt;
         STA_TRY(launch_build_sets_pq(&ba, st));
       }
+      mark(3);
       sta_attend_args ca{};
       ca.q = q; ca.q_stride_h = a->q_stride_h; ca.q_stride_n = a->q_stride_n;
       ca.k = k; ca.k_stride_h = a->k_stride_h; ca.k_stride_n = a->k_stride_n;
@@ -326,6 +336,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       ca.rope_scale = v == kShared ? a->rope_scale_c : 1.0f;
       ca.sm_scale = a->sm_scale;
       STA_TRY(launch_gather_attend(&ca, st));
+      mark(4);
     }
   }
   return STA_OK;

@@ -87,7 +87,8 @@ class ForwardArgs(ctypes.Structure):
                 ("chosen", c_vp), ("overflow", c_vp), ("kpct_meas", c_vp),
                 ("overflow20", c_vp), ("span", c_vp), ("kept_rows", c_vp), ("blocks", c_vp),
                 ("skipped", c_vp), ("idx_out", c_vp), ("newpos_k_out", c_vp),
-                ("newpos_q_out", c_vp), ("mask_out", c_vp), ("max_workspace_bytes", c_i64)]
+                ("newpos_q_out", c_vp), ("mask_out", c_vp), ("max_workspace_bytes", c_i64),
+                ("stage_events", c_vp)]
 
 
 # every symbol include/sta.h declares (checked by the CPU test suite)

@@ -68,7 +68,7 @@ def _check_inputs(q, k, v):
 def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=None,
             pct=30.0, n_global=32, n_local=32, tile=32, k_max=1024, select_score="freq",
             measure=False, block_n=32, pos_advance="max", use_skip=True, keep_sets=False,
-            max_workspace_bytes=0):
+            max_workspace_bytes=0, stage_events=None):
     """Run one prefill op.  variant: 'shared' | 'pq_union' | 'pq_stream'.
     q (Z,H,N,D); k, v (Z,Hkv,N,D) with H % Hkv == 0 (Hkv == H for repeat_kv-expanded input).
     Returns (out (Z,H,N,D), dict of per-(head, tile) statistics [+ sets when keep_sets])."""
@@ -163,6 +163,9 @@ def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=
             if "mask" in sets:
                 a.mask_out = sets["mask"][b].data_ptr()
         a.max_workspace_bytes = int(max_workspace_bytes)
+        if stage_events is not None:
+            arr = (ctypes.c_void_p * len(stage_events))(*[e.cuda_event for e in stage_events])
+            a.stage_events = ctypes.cast(arr, ctypes.c_void_p)
         nbytes = fn_ws(ctypes.byref(a))
         if nbytes == 0:
             L.check(1, f"sta_{variant}_workspace_bytes")
