@@ -287,6 +287,21 @@ size_t sta_pq_stream_workspace_bytes(const sta_forward_args* a);
 int sta_pq_stream_forward(const sta_forward_args* a, void* workspace, size_t workspace_bytes,
                           void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Allocation-free variant of sta_shared_forward.  No counterpart in the reference: it exists
+ * for hosts that may not allocate device memory themselves (plugins whose runtime owns every
+ * device allocation, code under a fixed pre-reserved memory budget).  Scratch comes from a
+ * STA_STATIC_SCRATCH_BYTES array of device memory that the library holds on every GPU that
+ * loads it, until the process exits; the call allocates nothing.  Larger problems run over
+ * smaller groups of kv heads; if one kv head needs more than the array, the call returns
+ * STA_ERR_WORKSPACE.  The first call on a device looks the array up (with that device
+ * current) -- make it before any stream capture.  All calls share the array and it keeps the
+ * last call's contents (the op reads no scratch before writing it); calls that overlap on the
+ * GPU race on it.
+ * ------------------------------------------------------------------------------------- */
+#define STA_STATIC_SCRATCH_BYTES (64ull << 20)
+int sta_shared_forward_static(const sta_forward_args* a, void* stream);
+
 /* Error flag of the last bounded device wait on this device: 0 = none. */
 int sta_device_error(void* stream, int32_t* code_out);
 

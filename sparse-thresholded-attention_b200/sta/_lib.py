@@ -96,7 +96,8 @@ EXPORTED = ["sta_last_error", "sta_version", "sta_tri_head_stride", "sta_rope_sp
             "sta_select", "sta_build_sets", "sta_build_sets_pq", "sta_gather_attend",
             "sta_pqstream_attend", "sta_shared_workspace_bytes", "sta_shared_forward",
             "sta_pq_union_workspace_bytes", "sta_pq_union_forward",
-            "sta_pq_stream_workspace_bytes", "sta_pq_stream_forward", "sta_device_error"]
+            "sta_pq_stream_workspace_bytes", "sta_pq_stream_forward", "sta_device_error",
+            "sta_shared_forward_static"]
 
 _lib = None
 
@@ -130,6 +131,8 @@ def lib():
         f = getattr(L, f"sta_{v}_forward")
         f.restype = ctypes.c_int
         f.argtypes = [ctypes.POINTER(ForwardArgs), c_vp, ctypes.c_size_t, c_vp]
+    L.sta_shared_forward_static.restype = ctypes.c_int
+    L.sta_shared_forward_static.argtypes = [ctypes.POINTER(ForwardArgs), c_vp]
     L.sta_device_error.restype = ctypes.c_int
     L.sta_device_error.argtypes = [c_vp, ctypes.POINTER(c_i32)]
     _lib = L
