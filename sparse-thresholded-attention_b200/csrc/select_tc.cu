@@ -76,6 +76,32 @@ __device__ __forceinline__ float transpose_reduce32(float (&v)[32]) {
   return v[0];
 }
 
+// 32 x 32 bit-matrix transpose across the warp: on entry lane r holds row r (bit c = M[r][c]);
+// on exit lane c holds column c (bit r = M[r][c]).  Five block-swap rounds, one shuffle each.
+__device__ __forceinline__ uint32_t transpose32(uint32_t x) {
+  const int l = lane_id();
+  const uint32_t lo_masks[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    const int s = 16 >> i;
+    const uint32_t lo = lo_masks[i], hi = ~lo;
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, x, s);
+    x = (l & s) ? ((x & hi) | ((y & hi) >> s)) : ((x & lo) | ((y & lo) << s));
+  }
+  return x;
+}
+
+// Smallest fp32 x with fl(x * sm) >= thr (sm > 0).  fl(x * sm) is non-decreasing in x, so
+// "fl(acc * sm) >= thr" is exactly "acc >= x": the keep test can run on raw accumulators.
+__device__ __forceinline__ float raw_threshold(float thr, float sm) {
+  if (!(thr > -INFINITY)) return -INFINITY;
+  if (thr == INFINITY) return INFINITY;
+  float x = __fdiv_rn(thr, sm);
+  for (int i = 0; i < 8 && __fmul_rn(x, sm) >= thr; ++i) x = nextafterf(x, -INFINITY);
+  for (int i = 0; i < 16 && __fmul_rn(x, sm) < thr; ++i) x = nextafterf(x, INFINITY);
+  return x;
+}
+
 __device__ __forceinline__ void decode_item(int64_t w, const Params& p, int64_t& bh, int& qb,
                                             int64_t& kvh) {
   qb = p.nqb - 1 - (int)(w / p.BH);
@@ -233,6 +259,9 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 0-3)
+    // Thread r owns accumulator row r.  Scores are compared in raw accumulator units against a
+    // per-row threshold derived exactly (see raw_threshold), so no per-element scaling is
+    // needed for the keep decision; pass 1 keeps the raw row max and scales it once.
     const int quad = warp;                 // TMEM lane quadrant
     const int row = quad * 32 + lane;
     const int64_t nt = (p.N + p.T - 1) / p.T;
@@ -250,70 +279,77 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
       const bool row_ok = qp < p.N;
       const float tau_h = __ldg(p.tau + (bh % p.H));
       const int nb = qb + 1;
-      float m = -INFINITY, thr = -INFINITY;
+      float mraw = -INFINITY, m = -INFINITY, thr = -INFINITY, thr_raw = INFINITY;
       int cnt = 0;
       for (int pass = 0; pass < p.npass && ok; ++pass) {
-        if (pass == 1) thr = __fsub_rn(m, tau_h);
+        if (pass == 1) {
+          thr = __fsub_rn(m, tau_h);
+          thr_raw = row_ok ? raw_threshold(thr, p.sm_scale) : INFINITY;
+        }
         for (int kb = 0; kb < nb; ++kb, ++ac) {
           const uint32_t slot = ac % NACC, use = ac / NACC;
-          if (!mbar_wait(acc_full + slot, use & 1, s_abort, p.err, kErrTimeoutAcc)) {
+          int got = 1;
+          if (lane == 0) got = mbar_wait(acc_full + slot, use & 1, s_abort, p.err, kErrTimeoutAcc);
+          got = __shfl_sync(0xffffffffu, got, 0);
+          if (!got) {
             ok = false;
             break;
           }
+          __syncwarp();
           tc_fence_after();
           const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + slot * BN;
-          if (pass == 0) {
+          float v[32], vn[32];
+          tmem_ld32(taddr, v);
+          tmem_wait_ld();
 #pragma unroll 1
-            for (int ch = 0; ch < 4; ++ch) {
-              float v[32];
-              tmem_ld32(taddr + ch * 32, v);
-              tmem_wait_ld();
-              const int64_t kbase = (int64_t)kb * BN + ch * 32;
+          for (int ch = 0; ch < 4; ++ch) {
+            if (ch < 3) tmem_ld32(taddr + (ch + 1) * 32, vn);  // next chunk in flight
+            const int64_t kbase = (int64_t)kb * BN + ch * 32;
+            // causal mask of this row over the chunk's 32 keys (all ones off the diagonal)
+            const int64_t lim = qp - kbase;
+            const uint32_t cmask = lim >= 31 ? 0xffffffffu : (lim < 0 ? 0u : ((2u << lim) - 1u));
+            if (pass == 0) {
+              if (cmask == 0xffffffffu) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float sc = __fmul_rn(v[j], p.sm_scale);
-                if (kbase + j <= qp) m = fmaxf(m, sc);
-              }
-            }
-            tc_fence_before();
-            mbar_arrive(acc_empty + slot);
-          } else {
-            const uint32_t* bufv = s_vote + rb * 512;
-#pragma unroll 1
-            for (int ch = 0; ch < 4; ++ch) {
-              float v[32];
-              tmem_ld32(taddr + ch * 32, v);
-              tmem_wait_ld();
-              const int64_t kbase = (int64_t)kb * BN + ch * 32;
-              uint32_t myvote = 0, mybits = 0;
-              float wv[32];
+                for (int j = 0; j < 32; ++j) mraw = fmaxf(mraw, v[j]);
+              } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float sc = __fmul_rn(v[j], p.sm_scale);
-                const bool keep = row_ok && (kbase + j <= qp) && (sc >= thr);
-                cnt += keep ? 1 : 0;
-                const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-                if (lane == j) {
-                  myvote = __popc(bal);
-                  mybits = bal;
-                }
-                if (p.wmode == 1) {
-                  wv[j] = keep ? __fsub_rn(sc, thr) : 0.f;
-                } else if (p.wmode == 2) {
-                  wv[j] = keep ? expf(__fsub_rn(sc, m)) : 0.f;
-                }
+                for (int j = 0; j < 32; ++j)
+                  if ((cmask >> j) & 1u) mraw = fmaxf(mraw, v[j]);
               }
+            } else {
+              uint32_t word = 0;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) word |= (v[j] >= thr_raw ? 1u : 0u) << j;
+              word &= cmask;
+              if (!row_ok) word = 0;
+              cnt += __popc(word);
+              const uint32_t colw = transpose32(word);  // lane j: keep bits of column j, bit r = row r
               float myw = 0.f;
-              if (p.wmode != 0) myw = transpose_reduce32(wv);
-              const int col = ch * 32 + lane;
-              const int o = rb * 512 + quad * 128 + col;
-              s_vote[o] = myvote;
-              s_bits[o] = mybits;
+              if (p.wmode != 0) {
+                float wv[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  const float sc = __fmul_rn(v[j], p.sm_scale);
+                  const float c = p.wmode == 1 ? __fsub_rn(sc, thr) : expf(__fsub_rn(sc, m));
+                  wv[j] = ((word >> j) & 1u) ? c : 0.f;
+                }
+                myw = transpose_reduce32(wv);
+              }
+              const int o = rb * 512 + quad * 128 + ch * 32 + lane;
+              s_vote[o] = __popc(colw);
+              s_bits[o] = colw;
               s_w[o] = myw;
             }
-            (void)bufv;
-            tc_fence_before();
-            mbar_arrive(acc_empty + slot);
+            if (ch < 3) {
+              tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = vn[j];
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(acc_empty + slot);
+          if (pass == 1) {
             // combine the quadrants of each query tile, store compact votes / bits / wvotes
             named_bar_sync(1, 128);
             const int col = threadIdx.x;
@@ -338,6 +374,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             rb ^= 1;
           }
         }
+        if (pass == 0) m = __fmul_rn(mraw, p.sm_scale);  // scaling is monotone: max commutes
       }
       if (ok && row_ok) {
         if (p.row_max) p.row_max[bh * p.N + qp] = m;
