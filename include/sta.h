@@ -176,6 +176,14 @@ typedef struct sta_attend_args {
   const float* inv_freq;   /* attend geometry */
   float rope_scale;
   float sm_scale;
+  /* optional: selection-geometry rows pre-rotated by sta_rope_split (bf16 hi + lo, contiguous
+   * (batch*n_heads | batch*n_kv_heads, n, d)).  When same_geometry != 0 (attend and selection
+   * geometries share inv_freq and rope_scale) a query / slot whose position equals
+   * fl(position_index * pos_scale_sel) is bit-identical to its pre-rotated row, which is then
+   * copied instead of rotated again.  Ignored for fp32 inputs. */
+  const void* q_hi; const void* q_lo; const void* k_hi; const void* k_lo;
+  float pos_scale_sel;
+  int32_t same_geometry;
 } sta_attend_args;
 
 int sta_gather_attend(const sta_attend_args* a, void* stream);
@@ -275,6 +283,9 @@ typedef struct sta_forward_args {
    * before the selection, before the attend kernel and at the end (NULL = none); with more
    * than one kv-head group they bracket the last group */
   void* const* stage_events;
+  /* 1 when the selection and attend geometries share inv_freq and rope_scale (lets the attend
+   * kernel reuse pre-rotated rows, see sta_attend_args) */
+  int32_t same_geometry;
 } sta_forward_args;
 
 size_t sta_shared_workspace_bytes(const sta_forward_args* a);

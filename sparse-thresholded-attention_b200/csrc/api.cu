@@ -335,6 +335,12 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       ca.inv_freq = a->inv_freq_c;
       ca.rope_scale = v == kShared ? a->rope_scale_c : 1.0f;
       ca.sm_scale = a->sm_scale;
+      ca.q_hi = w + L.qh;
+      ca.q_lo = w + L.ql;
+      ca.k_hi = w + L.kh;
+      ca.k_lo = w + L.kl;
+      ca.pos_scale_sel = a->pos_scale_a;
+      ca.same_geometry = (v == kShared && a->same_geometry) ? 1 : 0;
       STA_TRY(launch_gather_attend(&ca, st));
       mark(4);
     }

@@ -39,7 +39,67 @@ struct AttendP {
   const int32_t* kept;
   const float* inv_freq;
   float rope_scale, sm_scale;
+  const __nv_bfloat16 *qh, *ql, *kh, *kl;  // pre-rotated selection-geometry rows (or null)
+  float ps_sel;
+  int direct;                             // reuse pre-rotated rows where bit-identical
 };
+
+// 8 consecutive elements as fp32
+__device__ __forceinline__ void load8(const float* p, float (&x)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&x)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+
+// Rotate 8 frequency pairs (f0..f0+7 with partners f0+HALF..) of one row and store the NP-piece
+// split into a padded smem row set (plane stride `plane`, row pointer `dst`).
+template <int NP, int HALF, typename TV>
+__device__ __forceinline__ void rotate8(const TV* src, bool valid, int f0, float pos,
+                                        const float* inv_freq, float rope_scale,
+                                        __nv_bfloat16* dst, int plane) {
+  float x1[8], x2[8];
+  if (valid) {
+    load8(src + f0, x1);
+    load8(src + f0 + HALF, x2);
+  } else {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) x1[u] = x2[u] = 0.f;
+  }
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const float ang = __fmul_rn(pos, __ldg(inv_freq + f0 + u));
+    float r1, r2;
+    rope_pair(x1[u], x2[u], ang, rope_scale, r1, r2);
+    __nv_bfloat16 a[NP], b[NP];
+    split_pieces<NP>(r1, a);
+    split_pieces<NP>(r2, b);
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+      dst[j * plane + f0 + u] = a[j];
+      dst[j * plane + f0 + u + HALF] = b[j];
+    }
+  }
+}
+
+// copy 8 pre-rotated bf16 (hi and lo) of both halves of a row
+template <int HALF>
+__device__ __forceinline__ void copy_rotated(const __nv_bfloat16* hi, const __nv_bfloat16* lo,
+                                             int f0, __nv_bfloat16* dst, int plane) {
+  *reinterpret_cast<uint4*>(dst + f0) = *reinterpret_cast<const uint4*>(hi + f0);
+  *reinterpret_cast<uint4*>(dst + f0 + HALF) = *reinterpret_cast<const uint4*>(hi + f0 + HALF);
+  *reinterpret_cast<uint4*>(dst + plane + f0) = *reinterpret_cast<const uint4*>(lo + f0);
+  *reinterpret_cast<uint4*>(dst + plane + f0 + HALF) = *reinterpret_cast<const uint4*>(lo + f0 + HALF);
+}
 
 template <typename TV>
 __device__ __forceinline__ float ldf(const TV* p);
@@ -85,25 +145,18 @@ gather_attend_kernel(const AttendP p) {
   const int32_t* mask_row = p.mask ? p.mask + row_base * p.k_max : nullptr;
   const bool use_mask = mask_row != nullptr;
 
-  // ---- Q prologue: rotate at newpos_q, split into pieces, stage in smem
-  for (int it = tid; it < T * HALF; it += NTH) {
-    const int r = it / HALF, f = it % HALF;
+  // ---- Q prologue: rotate at newpos_q (or reuse the pre-rotated row), split, stage in smem
+  constexpr int C8 = HALF / 8;
+  const bool direct = !F32 && p.direct;
+  for (int it = tid; it < T * C8; it += NTH) {
+    const int r = it / C8, f0 = (it % C8) * 8;
     const int64_t qp = (int64_t)t * T + r;
-    float x1 = 0.f, x2 = 0.f;
-    if (qp < N) {
-      x1 = ldf(qg + qp * p.qsn + f);
-      x2 = ldf(qg + qp * p.qsn + f + HALF);
-    }
-    const float ang = __fmul_rn(npq_row[r], __ldg(p.inv_freq + f));
-    float r1, r2;
-    rope_pair(x1, x2, ang, p.rope_scale, r1, r2);
-    __nv_bfloat16 a[NQ], b[NQ];
-    split_pieces<NQ>(r1, a);
-    split_pieces<NQ>(r2, b);
-#pragma unroll
-    for (int i = 0; i < NQ; ++i) {
-      sQ[(i * T + r) * LD + f] = a[i];
-      sQ[(i * T + r) * LD + f + HALF] = b[i];
+    const float pos = npq_row[r];
+    __nv_bfloat16* dst = sQ + r * LD;
+    if (direct && qp < N && pos == __fmul_rn((float)qp, p.ps_sel)) {
+      copy_rotated<HALF>(p.qh + (bh * N + qp) * D, p.ql + (bh * N + qp) * D, f0, dst, T * LD);
+    } else {
+      rotate8<NQ, HALF>(qg + qp * p.qsn, qp < N, f0, pos, p.inv_freq, p.rope_scale, dst, T * LD);
     }
   }
 
@@ -136,35 +189,43 @@ gather_attend_kernel(const AttendP p) {
       sMask[i] = mk;
     }
     __syncthreads();
-    // gather + rotate K, gather V
-    for (int it = tid; it < BK * HALF; it += NTH) {
-      const int i = it / HALF, f = it % HALF;
+    // gather K slots (pre-rotated rows where bit-identical, else rotate at newpos), gather V
+    for (int it = tid; it < BK * C8; it += NTH) {
+      const int i = it / C8, f0 = (it % C8) * 8;
       const int id = sIdx[i];
-      float x1 = 0.f, x2 = 0.f;
-      if (id < N) {
-        x1 = ldf(kg + (int64_t)id * p.ksn + f);
-        x2 = ldf(kg + (int64_t)id * p.ksn + f + HALF);
-      }
-      const float ang = __fmul_rn(sNpk[i], __ldg(p.inv_freq + f));
-      float r1, r2;
-      rope_pair(x1, x2, ang, p.rope_scale, r1, r2);
-      __nv_bfloat16 a[NQ], b[NQ];
-      split_pieces<NQ>(r1, a);
-      split_pieces<NQ>(r2, b);
-#pragma unroll
-      for (int j = 0; j < NQ; ++j) {
-        sK[(j * BK + i) * LD + f] = a[j];
-        sK[(j * BK + i) * LD + f + HALF] = b[j];
+      const float pos = sNpk[i];
+      __nv_bfloat16* dst = sK + i * LD;
+      if (direct && id < N && pos == __fmul_rn((float)id, p.ps_sel)) {
+        copy_rotated<HALF>(p.kh + (kvh * N + id) * D, p.kl + (kvh * N + id) * D, f0, dst, BK * LD);
+      } else {
+        rotate8<NQ, HALF>(kg + (int64_t)(id < N ? id : 0) * p.ksn, id < N, f0, pos, p.inv_freq,
+                          p.rope_scale, dst, BK * LD);
       }
     }
-    for (int it = tid; it < BK * D; it += NTH) {
-      const int i = it / D, d = it % D;
+    for (int it = tid; it < BK * (D / 8); it += NTH) {
+      const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
       const int id = sIdx[i];
-      const float x = id < N ? ldf(vg + (int64_t)id * p.vsn + d) : 0.f;
-      __nv_bfloat16 a[NV];
-      split_pieces<NV>(x, a);
+      __nv_bfloat16* dst = sV + i * LD + d0;
+      if (!F32) {
+        uint4 u = make_uint4(0u, 0u, 0u, 0u);
+        if (id < N) u = *reinterpret_cast<const uint4*>(vg + (int64_t)id * p.vsn + d0);
+        *reinterpret_cast<uint4*>(dst) = u;
+      } else {
+        float x[8];
+        if (id < N) {
+          load8(vg + (int64_t)id * p.vsn + d0, x);
+        } else {
 #pragma unroll
-      for (int j = 0; j < NV; ++j) sV[(j * BK + i) * LD + d] = a[j];
+          for (int u = 0; u < 8; ++u) x[u] = 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          __nv_bfloat16 a[NV];
+          split_pieces<NV>(x[u], a);
+#pragma unroll
+          for (int j = 0; j < NV; ++j) dst[j * BK * LD + u] = a[j];
+        }
+      }
     }
     __syncthreads();
 
@@ -324,6 +385,17 @@ int launch_gather_attend(const sta_attend_args* a, cudaStream_t stream) {
   if (a->n_heads <= 0 || a->n_kv_heads <= 0 || a->n_heads % a->n_kv_heads)
     return fail(STA_ERR_ARG, "sta_gather_attend: bad head counts");
   if (a->n <= 0 || a->batch <= 0) return STA_OK;
+  {
+    const int64_t es = a->dtype == STA_DTYPE_F32 ? 4 : 2;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->k) |
+                         reinterpret_cast<uintptr_t>(a->v);
+    const int64_t st = (a->q_stride_h | a->q_stride_n | a->k_stride_h | a->k_stride_n |
+                        a->v_stride_h | a->v_stride_n) * es;
+    if ((al & 15u) || (st & 15))
+      return fail(STA_ERR_UNSUPPORTED,
+                  "sta_gather_attend: q/k/v rows must start on 16-byte boundaries (pointers and "
+                  "strides); pass contiguous or row-aligned views");
+  }
   AttendP p;
   p.q = a->q; p.qsh = a->q_stride_h; p.qsn = a->q_stride_n;
   p.k = a->k; p.ksh = a->k_stride_h; p.ksn = a->k_stride_n;
@@ -343,6 +415,12 @@ int launch_gather_attend(const sta_attend_args* a, cudaStream_t stream) {
   p.inv_freq = a->inv_freq;
   p.rope_scale = a->rope_scale;
   p.sm_scale = a->sm_scale;
+  p.qh = static_cast<const __nv_bfloat16*>(a->q_hi);
+  p.ql = static_cast<const __nv_bfloat16*>(a->q_lo);
+  p.kh = static_cast<const __nv_bfloat16*>(a->k_hi);
+  p.kl = static_cast<const __nv_bfloat16*>(a->k_lo);
+  p.ps_sel = a->pos_scale_sel;
+  p.direct = a->same_geometry && a->q_hi && a->q_lo && a->k_hi && a->k_lo;
   if (p.BH > 65535) return fail(STA_ERR_UNSUPPORTED, "sta_gather_attend: too many heads");
   const bool f32 = a->dtype == STA_DTYPE_F32;
   if (a->d == 128) {

@@ -56,7 +56,9 @@ class AttendArgs(ctypes.Structure):
                 ("n_kv_heads", c_i64), ("n", c_i64), ("d", c_i32), ("tile", c_i32),
                 ("k_max", c_i32), ("idx", c_vp), ("newpos_k", c_vp), ("newpos_q", c_vp),
                 ("mask", c_vp), ("kept_size", c_vp), ("inv_freq", c_vp),
-                ("rope_scale", c_f32), ("sm_scale", c_f32)]
+                ("rope_scale", c_f32), ("sm_scale", c_f32), ("q_hi", c_vp), ("q_lo", c_vp),
+                ("k_hi", c_vp), ("k_lo", c_vp), ("pos_scale_sel", c_f32),
+                ("same_geometry", c_i32)]
 
 
 class PQStreamArgs(ctypes.Structure):
@@ -88,7 +90,7 @@ class ForwardArgs(ctypes.Structure):
                 ("overflow20", c_vp), ("span", c_vp), ("kept_rows", c_vp), ("blocks", c_vp),
                 ("skipped", c_vp), ("idx_out", c_vp), ("newpos_k_out", c_vp),
                 ("newpos_q_out", c_vp), ("mask_out", c_vp), ("max_workspace_bytes", c_i64),
-                ("stage_events", c_vp)]
+                ("stage_events", c_vp), ("same_geometry", c_i32)]
 
 
 # every symbol include/sta.h declares (checked by the CPU test suite)

@@ -83,6 +83,9 @@ def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=
         raise ValueError(f"tau must have one entry per q head ({H}), got {tau_d.numel()}")
     ia = _dev_f32(ga.inv_freq, dev)
     ic = _dev_f32(gc.inv_freq, dev)
+    same_geometry = int(ia.shape == ic.shape and float(ga.rope_scale) == float(gc.rope_scale)
+                        and bool(torch.equal(ga.inv_freq.detach().float().cpu(),
+                                             gc.inv_freq.detach().float().cpu())))
     if ia.numel() != D // 2 or ic.numel() != D // 2:
         raise ValueError("inv_freq must have head_dim/2 entries")
     out = torch.empty((Z, H, N, D), dtype=q.dtype, device=dev)
@@ -163,6 +166,7 @@ def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=
             if "mask" in sets:
                 a.mask_out = sets["mask"][b].data_ptr()
         a.max_workspace_bytes = int(max_workspace_bytes)
+        a.same_geometry = same_geometry
         if stage_events is not None:
             arr = (ctypes.c_void_p * len(stage_events))(*[e.cuda_event for e in stage_events])
             a.stage_events = ctypes.cast(arr, ctypes.c_void_p)
