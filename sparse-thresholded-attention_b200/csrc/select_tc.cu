@@ -12,11 +12,12 @@
 // bf16 tcgen05 products (hi*hi + hi*lo + lo*hi, fp32 accumulation in TMEM); both passes issue
 // the identical instruction sequence, so pass 2 reproduces pass 1's scores bit for bit.
 //
-// Roles (192 threads, one CTA per SM, persistent over a longest-first static schedule):
-//   warps 0-3  epilogue: thread r owns accumulator row r (TMEM lane r); row max in pass 1;
+// Roles (320 threads, one CTA per SM, persistent over a longest-first static schedule):
+//   warps 0-7  epilogue: warps w and w+4 share TMEM lane quadrant w%4 (rows 32(w%4)..+31) and
+//              split each block's 128 columns; row max in pass 1;
 //              keep / warp-ballot votes / per-query bits / weighted votes in pass 2;
-//   warp 4     TMA producer (Q tile once per item, K blocks through an NSTAGE smem ring);
-//   warp 5     MMA issuer (one thread), 4 TMEM accumulator slots of 128 columns.
+//   warp 8     TMA producer (Q tile once per item, K blocks through an NSTAGE smem ring);
+//   warp 9     MMA issuer (one thread), 4 TMEM accumulator slots of 128 columns.
 // All waits are bounded; on expiry the kernel records STA_ERR_TIMEOUT and unwinds.
 #include "common.cuh"
 #include "sta_internal.h"
@@ -28,7 +29,8 @@ namespace {
 constexpr int BM = 128;       // query rows per item == TMEM lanes
 constexpr int BN = 128;       // keys per block == MMA N
 constexpr int NACC = 4;       // accumulator slots (4 x 128 fp32 columns = all 512 TMEM columns)
-constexpr int kThreads = 192;
+constexpr int kEpi = 256;     // 8 epilogue warps: two per TMEM lane quadrant, splitting columns
+constexpr int kThreads = kEpi + 64;
 constexpr int kTileBytes = 128 * 128;  // 128 rows x 64 bf16 (one 128-byte swizzle chunk)
 
 template <int D>
@@ -38,7 +40,7 @@ struct Cfg {
   static constexpr int STAGE_BYTES = 2 * NC * kTileBytes;
   static constexpr int NSTAGE = (D == 64) ? 4 : 2;
   static constexpr int RED_WORDS = 2 * 4 * 128;  // [buffer][quadrant][column]
-  static constexpr int SMEM = 1024 + Q_BYTES + NSTAGE * STAGE_BYTES + 3 * RED_WORDS * 4 + 512;
+  static constexpr int SMEM = 1024 + Q_BYTES + NSTAGE * STAGE_BYTES + 3 * RED_WORDS * 4 + 2 * kEpi * 4 + 512;
 };
 
 struct Params {
@@ -74,6 +76,18 @@ __device__ __forceinline__ float transpose_reduce32(float (&v)[32]) {
     }
   }
   return v[0];
+}
+
+// OR of `pred` over the `n` threads that arrive at named barrier `id` (a barrier itself)
+__device__ __forceinline__ int bar_red_or(int id, int n, int pred) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %1, 0;\n\t"
+      "barrier.cta.red.or.pred q, %2, %3, p;\n\t"
+      "selp.s32 %0, 1, 0, q;\n\t}"
+      : "=r"(r) : "r"(pred), "r"(id), "r"(n) : "memory");
+  return r;
 }
 
 // 32 x 32 bit-matrix transpose across the warp: on entry lane r holds row r (bit c = M[r][c]);
@@ -124,7 +138,9 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
   uint32_t* s_vote = reinterpret_cast<uint32_t*>(sK + C::NSTAGE * C::STAGE_BYTES);
   float* s_w = reinterpret_cast<float*>(s_vote + C::RED_WORDS);
   uint32_t* s_bits = reinterpret_cast<uint32_t*>(s_w + C::RED_WORDS);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_bits + C::RED_WORDS);
+  float* s_rowx = reinterpret_cast<float*>(s_bits + C::RED_WORDS);     // [2 halves][128 rows]
+  int* s_rowc = reinterpret_cast<int*>(s_rowx + kEpi);                  // [2 halves][128 rows]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_rowc + kEpi);
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 1;
   uint64_t* k_full = bars + 2;
@@ -146,7 +162,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
     }
     for (int a = 0; a < NACC; ++a) {
       mbar_init(acc_full + a, 1);
-      mbar_init(acc_empty + a, 128);
+      mbar_init(acc_empty + a, kEpi);
     }
     *s_abort = 0;
     fence_barrier_init();
@@ -163,7 +179,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
 
   const int64_t total = p.BH * (int64_t)p.nqb;
 
-  if (warp == 4) {
+  if (warp == kEpi / 32) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       prefetch_tmap(&tm_qhi);
@@ -202,7 +218,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kEpi / 32 + 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
@@ -262,7 +278,8 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
     // Thread r owns accumulator row r.  Scores are compared in raw accumulator units against a
     // per-row threshold derived exactly (see raw_threshold), so no per-element scaling is
     // needed for the keep decision; pass 1 keeps the raw row max and scales it once.
-    const int quad = warp;                 // TMEM lane quadrant
+    const int quad = warp & 3;             // TMEM lane quadrant
+    const int half = warp >> 2;            // which two of the block's four 32-column chunks
     const int row = quad * 32 + lane;
     const int64_t nt = (p.N + p.T - 1) / p.T;
     const int tiles_per_item = BM / p.T;
@@ -288,40 +305,42 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
         }
         for (int kb = 0; kb < nb; ++kb, ++ac) {
           const uint32_t slot = ac % NACC, use = ac / NACC;
-          int got = 1;
-          if (lane == 0) got = mbar_wait(acc_full + slot, use & 1, s_abort, p.err, kErrTimeoutAcc);
-          got = __shfl_sync(0xffffffffu, got, 0);
-          if (!got) {
+          int bad = 0;
+          if (lane == 0) bad = !mbar_wait(acc_full + slot, use & 1, s_abort, p.err, kErrTimeoutAcc);
+          // one collective decision for all epilogue warps, so none is left at a named barrier
+          if (bar_red_or(1, kEpi, bad)) {
             ok = false;
             break;
           }
-          __syncwarp();
           tc_fence_after();
           const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + slot * BN;
           float v[32], vn[32];
-          tmem_ld32(taddr, v);
+          tmem_ld32(taddr + half * 64, v);
           tmem_wait_ld();
 #pragma unroll 1
-          for (int ch = 0; ch < 4; ++ch) {
-            if (ch < 3) tmem_ld32(taddr + (ch + 1) * 32, vn);  // next chunk in flight
+          for (int cc = 0; cc < 2; ++cc) {
+            const int ch = half * 2 + cc;
+            if (cc == 0) tmem_ld32(taddr + (ch + 1) * 32, vn);  // next chunk in flight
             const int64_t kbase = (int64_t)kb * BN + ch * 32;
             // causal mask of this row over the chunk's 32 keys (all ones off the diagonal)
             const int64_t lim = qp - kbase;
             const uint32_t cmask = lim >= 31 ? 0xffffffffu : (lim < 0 ? 0u : ((2u << lim) - 1u));
             if (pass == 0) {
+              float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
               if (cmask == 0xffffffffu) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) mraw = fmaxf(mraw, v[j]);
+                for (int j = 0; j < 32; ++j) m4[j & 3] = fmaxf(m4[j & 3], v[j]);
               } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
-                  if ((cmask >> j) & 1u) mraw = fmaxf(mraw, v[j]);
+                  m4[j & 3] = fmaxf(m4[j & 3], ((cmask >> j) & 1u) ? v[j] : -INFINITY);
               }
+              mraw = fmaxf(mraw, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
             } else {
-              uint32_t word = 0;
+              uint32_t w4[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-              for (int j = 0; j < 32; ++j) word |= (v[j] >= thr_raw ? 1u : 0u) << j;
-              word &= cmask;
+              for (int j = 0; j < 32; ++j) w4[j & 3] |= (v[j] >= thr_raw ? 1u : 0u) << j;
+              uint32_t word = ((w4[0] | w4[1]) | (w4[2] | w4[3])) & cmask;
               if (!row_ok) word = 0;
               cnt += __popc(word);
               const uint32_t colw = transpose32(word);  // lane j: keep bits of column j, bit r = row r
@@ -341,7 +360,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
               s_bits[o] = colw;
               s_w[o] = myw;
             }
-            if (ch < 3) {
+            if (cc == 0) {
               tmem_wait_ld();
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = vn[j];
@@ -351,10 +370,10 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
           mbar_arrive(acc_empty + slot);
           if (pass == 1) {
             // combine the quadrants of each query tile, store compact votes / bits / wvotes
-            named_bar_sync(1, 128);
-            const int col = threadIdx.x;
+            named_bar_sync(2, kEpi);
+            const int col = threadIdx.x & 127;
             const int64_t kj = (int64_t)kb * BN + col;
-            for (int tt = 0; tt < tiles_per_item; ++tt) {
+            for (int tt = threadIdx.x >> 7; tt < tiles_per_item; tt += 2) {
               const int64_t tg = q0 / p.T + tt;
               if (tg >= nt) break;
               const int64_t hi_t = min((tg + 1) * (int64_t)p.T, p.N);
@@ -374,9 +393,22 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             rb ^= 1;
           }
         }
-        if (pass == 0) m = __fmul_rn(mraw, p.sm_scale);  // scaling is monotone: max commutes
+        if (!ok) break;
+        if (pass == 0) {
+          // the two column halves of each row meet: exact row max, then scale once
+          s_rowx[half * 128 + row] = mraw;
+          named_bar_sync(3, kEpi);
+          mraw = fmaxf(s_rowx[row], s_rowx[128 + row]);
+          named_bar_sync(3, kEpi);
+          m = __fmul_rn(mraw, p.sm_scale);  // scaling is monotone: max commutes with it
+        }
       }
-      if (ok && row_ok) {
+      if (!ok) break;
+      s_rowc[half * 128 + row] = cnt;
+      named_bar_sync(3, kEpi);
+      cnt = s_rowc[row] + s_rowc[128 + row];
+      named_bar_sync(3, kEpi);
+      if (half == 0 && row_ok) {
         if (p.row_max) p.row_max[bh * p.N + qp] = m;
         if (p.row_count && p.npass == 2) p.row_count[bh * p.N + qp] = cnt;
       }
