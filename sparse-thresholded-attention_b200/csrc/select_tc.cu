@@ -5,7 +5,7 @@
 // shared_selection_triton_perquery.py:119-218 (packed per-query keep bits, tile 32).
 //
 // Work item: 128 consecutive query rows of one q head (query block qb), against all causal
-// key blocks [0, (qb+1)*128).  Pass 1 sweeps the blocks for the exact row max m_i; pass 2
+// 256-key blocks [0, ceil((qb+1)*128 / 256) * 256).  Pass 1 sweeps the blocks for the exact row max m_i; pass 2
 // sweeps them again and evaluates keep = s >= m_i - tau_h & causal & row < N per (query, key).
 //
 // Scores are s = (Qr . Kr) * sm_scale with Qr / Kr the fp32 rotated rows, formed as three
@@ -17,7 +17,8 @@
 //              split each block's 128 columns; row max in pass 1;
 //              keep / warp-ballot votes / per-query bits / weighted votes in pass 2;
 //   warp 8     TMA producer (Q tile once per item, K blocks through an NSTAGE smem ring);
-//   warp 9     MMA issuer (one thread), 4 TMEM accumulator slots of 128 columns.
+//   warp 9     MMA issuer (one thread), M=128 N=256 K=16, 2 TMEM accumulator slots of 256
+//              columns; the K ring holds one bf16 piece (hi or lo) of a key block per stage.
 // All waits are bounded; on expiry the kernel records STA_ERR_TIMEOUT and unwinds.
 #include "common.cuh"
 #include "sta_internal.h"
@@ -27,19 +28,21 @@ namespace sta {
 namespace {
 
 constexpr int BM = 128;       // query rows per item == TMEM lanes
-constexpr int BN = 128;       // keys per block == MMA N
-constexpr int NACC = 4;       // accumulator slots (4 x 128 fp32 columns = all 512 TMEM columns)
+constexpr int BN = 256;       // keys per block == MMA N
+constexpr int NACC = 2;       // accumulator slots (2 x 256 fp32 columns = all 512 TMEM columns)
 constexpr int kEpi = 256;     // 8 epilogue warps: two per TMEM lane quadrant, splitting columns
 constexpr int kThreads = kEpi + 64;
-constexpr int kTileBytes = 128 * 128;  // 128 rows x 64 bf16 (one 128-byte swizzle chunk)
+constexpr int kTileBytes = BM * 128;   // 128 query rows x 64 bf16 (one 128-byte swizzle chunk)
+constexpr int kKTileBytes = BN * 128;  // 256 key rows x 64 bf16
 
 template <int D>
 struct Cfg {
   static constexpr int NC = D / 64;
   static constexpr int Q_BYTES = 2 * NC * kTileBytes;
-  static constexpr int STAGE_BYTES = 2 * NC * kTileBytes;
+  // one stage holds ONE bf16 piece (hi or lo) of a 256-key block; a block uses two stages
+  static constexpr int STAGE_BYTES = NC * kKTileBytes;
   static constexpr int NSTAGE = (D == 64) ? 4 : 2;
-  static constexpr int RED_WORDS = 2 * 4 * 128;  // [buffer][quadrant][column]
+  static constexpr int RED_WORDS = 2 * 4 * BN;   // [buffer][quadrant][column]
   static constexpr int SMEM = 1024 + Q_BYTES + NSTAGE * STAGE_BYTES + 3 * RED_WORDS * 4 + 2 * kEpi * 4 + 512;
 };
 
@@ -199,20 +202,20 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
           tma_load_3d(sQ + c * kTileBytes, &tm_qhi, q_full, c * 64, qb * BM, (int)bh);
           tma_load_3d(sQ + (C::NC + c) * kTileBytes, &tm_qlo, q_full, c * 64, qb * BM, (int)bh);
         }
-        const int nb = qb + 1;
+        const int nb = qb / 2 + 1;  // 256-key blocks covering the item's causal keys
         for (int pass = 0; pass < p.npass && ok; ++pass) {
-          for (int kb = 0; kb < nb; ++kb, ++kc) {
-            const uint32_t s = kc % C::NSTAGE, r = kc / C::NSTAGE;
-            if (r > 0 && !mbar_wait(k_empty + s, (r - 1) & 1, s_abort, p.err, kErrTimeoutEmpty)) {
-              ok = false;
-              break;
-            }
-            uint8_t* st = sK + s * C::STAGE_BYTES;
-            mbar_arrive_expect_tx(k_full + s, C::STAGE_BYTES);
-            for (int c = 0; c < C::NC; ++c) {
-              tma_load_3d(st + c * kTileBytes, &tm_khi, k_full + s, c * 64, kb * BN, (int)kvh);
-              tma_load_3d(st + (C::NC + c) * kTileBytes, &tm_klo, k_full + s, c * 64, kb * BN,
-                          (int)kvh);
+          for (int kb = 0; kb < nb && ok; ++kb) {
+            for (int piece = 0; piece < 2; ++piece, ++kc) {  // hi piece, then lo piece
+              const uint32_t s = kc % C::NSTAGE, r = kc / C::NSTAGE;
+              if (r > 0 && !mbar_wait(k_empty + s, (r - 1) & 1, s_abort, p.err, kErrTimeoutEmpty)) {
+                ok = false;
+                break;
+              }
+              uint8_t* st = sK + s * C::STAGE_BYTES;
+              const CUtensorMap* tm = piece == 0 ? &tm_khi : &tm_klo;
+              mbar_arrive_expect_tx(k_full + s, C::STAGE_BYTES);
+              for (int c = 0; c < C::NC; ++c)
+                tma_load_3d(st + c * kKTileBytes, tm, k_full + s, c * 64, kb * BN, (int)kvh);
             }
           }
         }
@@ -233,40 +236,44 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
         decode_item(w, p, bh, qb, kvh);
         if (!mbar_wait(q_full, it & 1, s_abort, p.err, kErrTimeoutQ)) break;
         tc_fence_after();
-        const int nb = qb + 1;
+        const int nb = qb / 2 + 1;
         for (int pass = 0; pass < p.npass && ok; ++pass) {
-          for (int kb = 0; kb < nb; ++kb, ++kc, ++ac) {
+          for (int kb = 0; kb < nb; ++kb, ++ac) {
             const uint32_t slot = ac % NACC, use = ac / NACC;
             if (use > 0 && !mbar_wait(acc_empty + slot, (use - 1) & 1, s_abort, p.err,
                                       kErrTimeoutAcc)) {
               ok = false;
               break;
             }
-            const uint32_t s = kc % C::NSTAGE, r = kc / C::NSTAGE;
-            if (!mbar_wait(k_full + s, r & 1, s_abort, p.err, kErrTimeoutK)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
             const uint32_t d_tmem = tmem_base + slot * BN;
-            const uint32_t st = k_addr + s * C::STAGE_BYTES;
             uint32_t acc = 0;
-#pragma unroll
-            for (int c = 0; c < C::NC; ++c) {
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk) {
-                const uint32_t off = c * kTileBytes + kk * 32;
-                const uint64_t qh = sw128_kmajor_desc(q_addr + off);
-                const uint64_t ql = sw128_kmajor_desc(q_addr + C::NC * kTileBytes + off);
-                const uint64_t kh = sw128_kmajor_desc(st + off);
-                const uint64_t kl = sw128_kmajor_desc(st + C::NC * kTileBytes + off);
-                umma_bf16(d_tmem, qh, kh, idesc, acc);
-                acc = 1;
-                umma_bf16(d_tmem, qh, kl, idesc, 1);
-                umma_bf16(d_tmem, ql, kh, idesc, 1);
+            // piece 0 (K hi): Qhi.Khi + Qlo.Khi ; piece 1 (K lo): Qhi.Klo
+            for (int piece = 0; piece < 2; ++piece, ++kc) {
+              const uint32_t s = kc % C::NSTAGE, r = kc / C::NSTAGE;
+              if (!mbar_wait(k_full + s, r & 1, s_abort, p.err, kErrTimeoutK)) {
+                ok = false;
+                break;
               }
+              tc_fence_after();
+              const uint32_t st = k_addr + s * C::STAGE_BYTES;
+#pragma unroll
+              for (int c = 0; c < C::NC; ++c) {
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                  const uint32_t qoff = c * kTileBytes + kk * 32;
+                  const uint64_t qh = sw128_kmajor_desc(q_addr + qoff);
+                  const uint64_t kd = sw128_kmajor_desc(st + c * kKTileBytes + kk * 32);
+                  umma_bf16(d_tmem, qh, kd, idesc, acc);
+                  acc = 1;
+                  if (piece == 0) {
+                    const uint64_t ql = sw128_kmajor_desc(q_addr + C::NC * kTileBytes + qoff);
+                    umma_bf16(d_tmem, ql, kd, idesc, 1);
+                  }
+                }
+              }
+              umma_commit(k_empty + s);
             }
-            umma_commit(k_empty + s);
+            if (!ok) break;
             umma_commit(acc_full + slot);
           }
         }
@@ -295,7 +302,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
       const int64_t qp = q0 + row;
       const bool row_ok = qp < p.N;
       const float tau_h = __ldg(p.tau + (bh % p.H));
-      const int nb = qb + 1;
+      const int nb = qb / 2 + 1;
       float mraw = -INFINITY, m = -INFINITY, thr = -INFINITY, thr_raw = INFINITY;
       int cnt = 0;
       for (int pass = 0; pass < p.npass && ok; ++pass) {
@@ -315,12 +322,12 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
           tc_fence_after();
           const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + slot * BN;
           float v[32], vn[32];
-          tmem_ld32(taddr + half * 64, v);
+          tmem_ld32(taddr + half * (BN / 2), v);
           tmem_wait_ld();
 #pragma unroll 1
-          for (int cc = 0; cc < 2; ++cc) {
-            const int ch = half * 2 + cc;
-            if (cc == 0) tmem_ld32(taddr + (ch + 1) * 32, vn);  // next chunk in flight
+          for (int cc = 0; cc < BN / 64; ++cc) {
+            const int ch = half * (BN / 64) + cc;
+            if (cc + 1 < BN / 64) tmem_ld32(taddr + (ch + 1) * 32, vn);  // next chunk in flight
             const int64_t kbase = (int64_t)kb * BN + ch * 32;
             // causal mask of this row over the chunk's 32 keys (all ones off the diagonal)
             const int64_t lim = qp - kbase;
@@ -355,12 +362,12 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
                 }
                 myw = transpose_reduce32(wv);
               }
-              const int o = rb * 512 + quad * 128 + ch * 32 + lane;
+              const int o = rb * (4 * BN) + quad * BN + ch * 32 + lane;
               s_vote[o] = __popc(colw);
               s_bits[o] = colw;
               s_w[o] = myw;
             }
-            if (cc == 0) {
+            if (cc + 1 < BN / 64) {
               tmem_wait_ld();
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = vn[j];
@@ -371,9 +378,9 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
           if (pass == 1) {
             // combine the quadrants of each query tile, store compact votes / bits / wvotes
             named_bar_sync(2, kEpi);
-            const int col = threadIdx.x & 127;
+            const int col = threadIdx.x;  // kEpi == BN: one column per epilogue thread
             const int64_t kj = (int64_t)kb * BN + col;
-            for (int tt = threadIdx.x >> 7; tt < tiles_per_item; tt += 2) {
+            for (int tt = 0; tt < tiles_per_item; ++tt) {
               const int64_t tg = q0 / p.T + tt;
               if (tg >= nt) break;
               const int64_t hi_t = min((tg + 1) * (int64_t)p.T, p.N);
@@ -381,14 +388,14 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
               uint32_t vs = 0;
               float wsum = 0.f;
               for (int qq = tt * quads_per_tile; qq < (tt + 1) * quads_per_tile; ++qq) {
-                const int o = rb * 512 + qq * 128 + col;
+                const int o = rb * (4 * BN) + qq * BN + col;
                 vs += s_vote[o];
                 wsum += s_w[o];
               }
               const int64_t off = bh * p.head_stride + tri_tile_offset(tg, p.T) + kj;
               if (p.votes) p.votes[off] = (uint8_t)vs;
               if (p.wmode != 0 && p.wvotes) p.wvotes[off] = wsum;
-              if (p.bits && p.T == 32) p.bits[off] = s_bits[rb * 512 + tt * 128 + col];
+              if (p.bits && p.T == 32) p.bits[off] = s_bits[rb * (4 * BN) + tt * BN + col];
             }
             rb ^= 1;
           }
@@ -447,10 +454,10 @@ int launch_select(const sta_select_args* a, cudaStream_t stream) {
   const int64_t BH = a->batch * a->n_heads;
   const int64_t BHk = a->batch * a->n_kv_heads;
   CUtensorMap m_qhi, m_qlo, m_khi, m_klo;
-  bool okm = make_tmap_bf16_3d(&m_qhi, a->q_hi, a->d, a->n, BH, 64, 128) &&
-             make_tmap_bf16_3d(&m_qlo, a->q_lo, a->d, a->n, BH, 64, 128) &&
-             make_tmap_bf16_3d(&m_khi, a->k_hi, a->d, a->n, BHk, 64, 128) &&
-             make_tmap_bf16_3d(&m_klo, a->k_lo, a->d, a->n, BHk, 64, 128);
+  bool okm = make_tmap_bf16_3d(&m_qhi, a->q_hi, a->d, a->n, BH, 64, BM) &&
+             make_tmap_bf16_3d(&m_qlo, a->q_lo, a->d, a->n, BH, 64, BM) &&
+             make_tmap_bf16_3d(&m_khi, a->k_hi, a->d, a->n, BHk, 64, BN) &&
+             make_tmap_bf16_3d(&m_klo, a->k_lo, a->d, a->n, BHk, 64, BN);
   if (!okm) return fail(STA_ERR_CUDA, "sta_select: cuTensorMapEncodeTiled failed");
 
   Params p;
