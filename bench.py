@@ -162,7 +162,7 @@ def run_reference(args):
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
             "wall_s": time.perf_counter() - t0}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -358,7 +358,7 @@ def run_gpu(args):
                 "stage_ms": {"rope_prologue": stage_ms[0], "select_tcgen05": stage_ms[1],
                              "build_sets": stage_ms[2], "attend": stage_ms[3]},
                 "roofline": roof, "cpu_baseline": cpu, "selection": stats}
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.destroy_process_group()
 
@@ -374,8 +374,27 @@ def select_traffic_bytes(c, heads, args):
     return d["dram_bytes"] * scale
 
 
+_JSON_FD = None
+
+
+def emit(line: dict):
+    """Print the one JSON result line on the original stdout."""
+    data = (json.dumps(line) + "\n").encode()
+    if _JSON_FD is not None:
+        os.write(_JSON_FD, data)
+    else:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+
+
 def main():
+    global _JSON_FD
     args = parse()
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        # libraries (NCCL's version banner) write to fd 1; keep stdout for the JSON line only
+        sys.stdout.flush()
+        _JSON_FD = os.dup(1)
+        os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args)
     else:
