@@ -1,0 +1,79 @@
+"""The HuggingFace attention hooks on a tiny random-init Llama (needs a B200).
+
+Invariant used as the check: with tau = +inf every causal key passes the threshold, pct = 100
+keeps the whole pooled set, k_max >= N caps nothing and pos_scale = 1 leaves positions
+unchanged, so thresholded attention IS dense causal RoPE attention; the patched model must
+reproduce the unpatched model's logits, and greedy decoding must produce the same tokens.
+"""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def tiny_llama(seed=0, n_kv=2):
+    from transformers import LlamaConfig, LlamaForCausalLM
+    torch.manual_seed(seed)
+    cfg = LlamaConfig(vocab_size=211, hidden_size=256, intermediate_size=512,
+                      num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=n_kv,
+                      head_dim=64, max_position_embeddings=4096, rope_theta=10000.0,
+                      attn_implementation="eager")
+    return LlamaForCausalLM(cfg).cuda().float().eval()
+
+
+def set_tau(model, value):
+    for layer in model.model.layers:
+        sa = layer.self_attn
+        sa.tau_head_vec = torch.full((model.config.num_attention_heads,), value,
+                                     device="cuda")
+
+
+@pytest.mark.parametrize("modname", ["shared_selection_exact_2", "shared_selection_exact"])
+def test_hook_prefill_and_decode_match_dense_at_tau_inf(modname):
+    import importlib
+    import transformers.models.llama.modeling_llama as ml
+    mod = importlib.import_module("sta." + modname)
+    orig_forward = ml.LlamaAttention.forward
+    model = tiny_llama()
+    ids = torch.randint(0, 211, (1, 192), generator=torch.Generator().manual_seed(1)).cuda()
+    with torch.no_grad():
+        ref_logits = model(ids).logits
+        ref_gen = model.generate(ids, max_new_tokens=3, do_sample=False)
+    try:
+        set_tau(model, math.inf)
+        mod.install_shared_pi_forward(model, pct=100.0, context_window=4096, tile=64,
+                                      k_max=512)
+        with torch.no_grad():
+            logits = model(ids).logits
+            gen = model.generate(ids, max_new_tokens=3, do_sample=False)
+        assert torch.isfinite(logits).all()
+        err = (logits - ref_logits).abs().max().item()
+        assert err <= 1e-3, err
+        assert torch.equal(gen, ref_gen)
+        sa = model.model.layers[0].self_attn
+        assert sa.spi_last_kept.shape == (4, 3)
+        # every tile keeps all of its causal keys plus the in-tile future of its local block
+        assert int(sa.spi_last_kept[:, -1].min()) >= 192
+    finally:
+        ml.LlamaAttention.forward = orig_forward
+
+
+def test_hook_threshold_selects_and_runs():
+    """A finite tau selects (kept sets smaller than the causal count) and stays finite."""
+    import transformers.models.llama.modeling_llama as ml
+    from sta import shared_selection_exact_2 as st
+    orig_forward = ml.LlamaAttention.forward
+    model = tiny_llama(seed=3)
+    ids = torch.randint(0, 211, (1, 512), generator=torch.Generator().manual_seed(2)).cuda()
+    try:
+        set_tau(model, 0.5)
+        st.install_shared_pi_forward(model, pct=30.0, tile=64, k_max=256)
+        with torch.no_grad():
+            out = model(ids).logits
+        assert torch.isfinite(out).all()
+        sa = model.model.layers[1].self_attn
+        assert int(sa.spi_last_kept[:, -1].max()) < 512
+    finally:
+        ml.LlamaAttention.forward = orig_forward
