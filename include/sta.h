@@ -151,6 +151,35 @@ typedef struct sta_build_pq_args {
 int sta_build_sets_pq(const sta_build_pq_args* a, void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Stage 2'' -- chunk_exact selection: per-chunk (chunk_size keys) sums of the tile's passer
+ * rank values, the top n_chunk visible non-forced chunks (ties: lowest chunk index) plus the
+ * forced global/local chunks, causal-edge trim, dense ranks, pooled mask (-1 on valid slots).
+ * Replaces _build_sets_chunk (shared_selection_triton_chunked.py:149-243).
+ * ------------------------------------------------------------------------------------- */
+typedef struct sta_build_chunk_args {
+  const uint8_t* votes;
+  const float* wvotes;     /* compact, used when select_score != FREQ */
+  int64_t heads;
+  int64_t n;
+  int32_t tile;
+  int32_t k_max;
+  int32_t n_global;
+  int32_t n_local;
+  int32_t chunk_size;
+  int32_t n_chunk;
+  int32_t select_score;
+  int32_t chunk_agg;       /* 0 = sum, 1 = mean over the chunk's passers */
+  int32_t* idx;
+  float* newpos_k;
+  float* newpos_q;
+  int32_t* mask;           /* optional (NULL): -1 on valid slots, 0 on padding */
+  int32_t* usize;          /* (heads, nt) passers visible to the tile */
+  int32_t* kept_size;      /* (heads, nt) */
+} sta_build_chunk_args;
+
+int sta_build_sets_chunk(const sta_build_chunk_args* a, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * Stage 3 -- gather + repositioned attention over the selected slots (Kernel C / C').
  * Replaces _gather_attn_kernel (shared_selection_triton_exact_2.py:146-225) and
  * _gather_attn_pq_kernel (shared_selection_triton_perquery.py:226-312).
@@ -286,6 +315,10 @@ typedef struct sta_forward_args {
   /* 1 when the selection and attend geometries share inv_freq and rope_scale (lets the attend
    * kernel reuse pre-rotated rows, see sta_attend_args) */
   int32_t same_geometry;
+  /* chunk_exact only */
+  int32_t chunk_size;
+  int32_t n_chunk;
+  int32_t chunk_agg;
 } sta_forward_args;
 
 size_t sta_shared_workspace_bytes(const sta_forward_args* a);
@@ -294,6 +327,11 @@ int sta_shared_forward(const sta_forward_args* a, void* workspace, size_t worksp
 size_t sta_pq_union_workspace_bytes(const sta_forward_args* a);
 int sta_pq_union_forward(const sta_forward_args* a, void* workspace, size_t workspace_bytes,
                          void* stream);
+size_t sta_chunk_workspace_bytes(const sta_forward_args* a);
+/* chunk_exact (shared_chunk_attention, shared_selection_triton_chunked.py:249-320); statistics:
+ * shared_size <- usize, kept_size */
+int sta_chunk_forward(const sta_forward_args* a, void* workspace, size_t workspace_bytes,
+                      void* stream);
 size_t sta_pq_stream_workspace_bytes(const sta_forward_args* a);
 int sta_pq_stream_forward(const sta_forward_args* a, void* workspace, size_t workspace_bytes,
                           void* stream);

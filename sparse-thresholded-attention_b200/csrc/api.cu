@@ -86,7 +86,7 @@ bool make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t d, uint64_t 
 // ------------------------------------------------------------------------------------------
 namespace {
 
-enum Variant { kShared = 0, kPQUnion = 1, kPQStream = 2 };
+enum Variant { kShared = 0, kPQUnion = 1, kPQStream = 2, kChunk = 3 };
 
 inline size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -103,7 +103,7 @@ Layout layout_for(const sta_forward_args* a, Variant v, int64_t c) {
   const int64_t G = a->n_heads / a->n_kv_heads;
   const int64_t qh = c * G;  // q heads in the group
   const int64_t N = a->n, D = a->d;
-  const int T = v == kShared ? a->tile : 32;
+  const int T = (v == kShared || v == kChunk) ? a->tile : 32;
   const int64_t nt = (N + T - 1) / T;
   const int64_t HS = tri_head_stride(N, T);
   size_t o = 0;
@@ -150,9 +150,16 @@ int check_forward(const sta_forward_args* a, Variant v) {
     return fail(STA_ERR_ARG, "forward: n_heads must be a positive multiple of n_kv_heads");
   if (a->dtype != STA_DTYPE_F32 && a->dtype != STA_DTYPE_BF16)
     return fail(STA_ERR_UNSUPPORTED, "forward: dtype must be f32 or bf16");
-  if (v == kShared && a->tile != 32 && a->tile != 64)
+  if ((v == kShared || v == kChunk) && a->tile != 32 && a->tile != 64)
     return fail(STA_ERR_UNSUPPORTED, "forward: tile must be 32 or 64");
-  if (v != kShared && a->tile != 32) return fail(STA_ERR_UNSUPPORTED, "forward: tile must be 32");
+  if ((v == kPQUnion || v == kPQStream) && a->tile != 32)
+    return fail(STA_ERR_UNSUPPORTED, "forward: tile must be 32");
+  if (v == kChunk) {
+    if (a->chunk_size <= 0 || a->k_max % a->chunk_size || a->n_chunk <= 0)
+      return fail(STA_ERR_ARG, "forward: chunk_exact needs chunk_size | k_max and n_chunk > 0");
+    if (!(a->shared_size && a->kept_size))
+      return fail(STA_ERR_ARG, "forward: chunk statistics outputs required");
+  }
   if (v != kPQStream && a->k_max <= 0) return fail(STA_ERR_ARG, "forward: k_max must be > 0");
   if (v == kShared && !(a->shared_size && a->kept_size && a->chosen && a->overflow &&
                         a->kpct_meas && a->overflow20))
@@ -183,7 +190,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
   if (!ws || ws_len < L.total) return fail(STA_ERR_WORKSPACE, "forward: workspace too small");
   uint8_t* w = static_cast<uint8_t*>(ws);
   const int64_t H = a->n_heads, Hk = a->n_kv_heads, G = H / Hk, N = a->n;
-  const int T = v == kShared ? a->tile : 32;
+  const int T = (v == kShared || v == kChunk) ? a->tile : 32;
   const int64_t nt = (N + T - 1) / T;
   const int64_t es = esize(a->dtype);
   const int64_t kmax = a->k_max;
@@ -291,6 +298,28 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
         ba.kpct_meas = a->kpct_meas + h0 * nt;
         ba.overflow20 = a->overflow20 + h0 * nt;
         STA_TRY(launch_build_sets(&ba, st));
+      } else if (v == kChunk) {
+        int32_t* cmask = a->mask_out ? a->mask_out + h0 * nt * kmax : nullptr;
+        sta_build_chunk_args ba{};
+        ba.votes = w + L.votes;
+        ba.wvotes = s.wvotes;
+        ba.heads = qn;
+        ba.n = N;
+        ba.tile = T;
+        ba.k_max = a->k_max;
+        ba.n_global = a->n_global;
+        ba.n_local = a->n_local;
+        ba.chunk_size = a->chunk_size;
+        ba.n_chunk = a->n_chunk;
+        ba.select_score = a->select_score;
+        ba.chunk_agg = a->chunk_agg;
+        ba.idx = idx;
+        ba.newpos_k = npk;
+        ba.newpos_q = npq;
+        ba.mask = cmask;
+        ba.usize = a->shared_size + h0 * nt;
+        ba.kept_size = a->kept_size + h0 * nt;
+        STA_TRY(launch_build_sets_chunk(&ba, st));
       } else {
         mask = a->mask_out ? a->mask_out + h0 * nt * kmax : reinterpret_cast<int32_t*>(w + L.mask);
         sta_build_pq_args ba{};
@@ -387,6 +416,10 @@ int sta_build_sets_pq(const sta_build_pq_args* a, void* stream) {
   return launch_build_sets_pq(a, static_cast<cudaStream_t>(stream));
 }
 
+int sta_build_sets_chunk(const sta_build_chunk_args* a, void* stream) {
+  return launch_build_sets_chunk(a, static_cast<cudaStream_t>(stream));
+}
+
 int sta_gather_attend(const sta_attend_args* a, void* stream) {
   return launch_gather_attend(a, static_cast<cudaStream_t>(stream));
 }
@@ -398,6 +431,12 @@ int sta_pqstream_attend(const sta_pqstream_args* a, void* stream) {
 size_t sta_shared_workspace_bytes(const sta_forward_args* a) { return ws_bytes(a, kShared); }
 size_t sta_pq_union_workspace_bytes(const sta_forward_args* a) { return ws_bytes(a, kPQUnion); }
 size_t sta_pq_stream_workspace_bytes(const sta_forward_args* a) { return ws_bytes(a, kPQStream); }
+size_t sta_chunk_workspace_bytes(const sta_forward_args* a) { return ws_bytes(a, kChunk); }
+
+int sta_chunk_forward(const sta_forward_args* a, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  return run_forward(a, kChunk, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
 
 int sta_shared_forward(const sta_forward_args* a, void* workspace, size_t workspace_bytes,
                        void* stream) {

@@ -549,7 +549,234 @@ __global__ void __launch_bounds__(kBT) build_sets_pq_kernel(const BuildPQP p) {
   }
 }
 
+// ---- chunk_exact selection ----------------------------------------------------------------------
+struct BuildChunkP {
+  const uint8_t* votes;
+  const float* wvotes;
+  int64_t BH, N, nt, head_stride;
+  int T, k_max, n_global, n_local, C, n_chunk, weighted, mean_agg;
+  int32_t* idx;
+  float* newpos_k;
+  float* newpos_q;
+  int32_t* mask;
+  int32_t* usize;
+  int32_t* kept_size;
+};
+
+// dynamic smem: mass[nC] floats, then flags[nC] bytes (bit0 candidate, bit1 forced, bit2 selected)
+__global__ void __launch_bounds__(kBT) build_sets_chunk_kernel(const BuildChunkP p) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  const int64_t t = blockIdx.x;
+  const int64_t bh = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int64_t N = p.N;
+  const int T = p.T, C = p.C;
+  const int64_t tstart = t * T;
+  const int64_t nC = (N + C - 1) / C;
+  float* mass = reinterpret_cast<float*>(dsm);
+  uint8_t* flag = reinterpret_cast<uint8_t*>(mass + nC);
+  const int64_t off = bh * p.head_stride + tri_tile_offset(t, T);
+  const uint8_t* v = p.votes + off;
+  const float* w = p.weighted ? p.wvotes + off : nullptr;
+  const int64_t hi = min(tstart + T, N);      // causal keys of the tile (votes exist below)
+  const int64_t last_q = hi - 1;
+  const int64_t nvis = last_q / C + 1;        // chunks with c*C <= last_q
+  const int64_t gch = (p.n_global + C - 1) / C;
+  const int64_t lo_c = (tstart - p.n_local + 1 > 0 ? tstart - p.n_local + 1 : 0) / C;
+  const int64_t hi_c = last_q / C;
+
+  __shared__ int sh_i[32];
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t s_prefix;
+  __shared__ int64_t s_k, s_gt;
+
+  // chunk masses: fp32 sum of the passers' rank values in key order (chunk_agg "mean" divides by
+  // the passer count, at least 1), plus candidate / forced flags
+  int nu = 0, ncand = 0;
+  for (int64_t c = tid; c < nC; c += kBT) {
+    float m = 0.f;
+    int cnt = 0;
+    uint8_t f = 0;
+    if (c < nvis) {
+      const int64_t j1 = min((c + 1) * C, hi);
+      for (int64_t j = c * C; j < j1; ++j) {
+        const uint32_t vv = v[j];
+        if (vv) {
+          m = __fadd_rn(m, p.weighted ? w[j] : (float)vv);
+          ++cnt;
+        }
+      }
+      if (p.mean_agg) m = __fdiv_rn(m, (float)(cnt > 1 ? cnt : 1));
+      const bool forced = c < gch || (c >= lo_c && c <= hi_c);
+      f = forced ? 2 : 1;
+      if (!forced) ++ncand;
+      nu += cnt;
+    }
+    mass[c] = m;
+    flag[c] = f;
+  }
+  const int usize = block_sum(nu, sh_i);
+  const int n_cand = block_sum(ncand, sh_i);
+  const int64_t n_take = p.n_chunk < nC ? p.n_chunk : nC;
+
+  // top n_take candidates by mass: exact radix select of the n_take-th largest, ties to the
+  // lowest chunk index
+  float cut = -1.f;
+  int64_t need_eq = 0;
+  const bool all = n_cand <= n_take;
+  if (!all && n_take > 0) {
+    if (tid == 0) {
+      s_prefix = 0u;
+      s_k = n_take;
+      s_gt = 0;
+    }
+    uint32_t msk = 0u;
+    for (int round = 0; round < 4; ++round) {
+      const int shift = 24 - 8 * round;
+      for (int i = tid; i < 256; i += kBT) hist[i] = 0u;
+      __syncthreads();
+      const uint32_t prefix = s_prefix;
+      for (int64_t c = tid; c < nvis; c += kBT) {
+        if (flag[c] != 1) continue;
+        const uint32_t key = __float_as_uint(mass[c]);
+        if ((key & msk) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int64_t kk = s_k, cum = 0;
+        int d;
+        for (d = 255; d > 0; --d) {
+          if (cum + (int64_t)hist[d] >= kk) break;
+          cum += hist[d];
+        }
+        s_gt += cum;
+        s_k = kk - cum;
+        s_prefix = prefix | ((uint32_t)d << shift);
+      }
+      __syncthreads();
+      msk |= 255u << shift;
+    }
+    cut = __uint_as_float(s_prefix);
+    need_eq = n_take - s_gt;
+  }
+  __syncthreads();
+  // mark selected chunks (candidates above the cut, the first need_eq at the cut, forced)
+  {
+    int64_t tie_carry = 0;
+    for (int64_t c0 = 0; c0 < nvis; c0 += kBT) {
+      const int64_t c = c0 + tid;
+      int tie = 0;
+      bool sel = false;
+      if (c < nvis) {
+        const uint8_t f = flag[c];
+        if (f == 2) sel = true;
+        else if (f == 1) {
+          if (all && n_take > 0) sel = true;
+          else if (!all && mass[c] > cut) sel = true;
+          else if (!all && mass[c] == cut) tie = 1;
+        }
+      }
+      int tie_total;
+      const int tr = block_excl_sum(tie, sh_i, tie_total);
+      if (tie && tie_carry + tr < need_eq) sel = true;
+      if (c < nvis && sel) flag[c] |= 4;
+      tie_carry += tie_total;
+    }
+  }
+  __syncthreads();
+  // keys of the selected chunks up to the tile's last query: dense ranks, compaction
+  const int64_t nt_row = bh * p.nt + t;
+  int32_t* idx_row = p.idx + nt_row * p.k_max;
+  float* npk_row = p.newpos_k + nt_row * p.k_max;
+  float* npq_row = p.newpos_q + nt_row * T;
+  int32_t* mask_row = p.mask ? p.mask + nt_row * p.k_max : nullptr;
+  const int64_t E = hi;  // keys 0..last_q
+  int64_t carry = 0;
+  for (int64_t c0 = 0; c0 < E; c0 += kChunk) {
+    const int64_t j0 = c0 + (int64_t)tid * kItems;
+    uint32_t flags = 0;
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      const int64_t j = j0 + i;
+      if (j < E && (flag[j / C] & 4)) flags |= 1u << i;
+    }
+    int total;
+    const int base = block_excl_sum(__popc(flags), sh_i, total);
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      const int64_t j = j0 + i;
+      if (j >= E) break;
+      const bool f = (flags >> i) & 1u;
+      const int64_t rk = carry + base + __popc(flags & ((1u << i) - 1u)) + (f ? 1 : 0) - 1;
+      if (f && rk < p.k_max) {
+        idx_row[rk] = (int32_t)j;
+        npk_row[rk] = (float)rk;
+        if (mask_row) mask_row[rk] = -1;
+      }
+      if (j >= tstart && j < tstart + T) npq_row[j - tstart] = (float)rk;
+    }
+    carry += total;
+  }
+  __syncthreads();
+  if (tstart + T > N) {
+    const float last = npq_row[N - 1 - tstart];
+    for (int i = tid; i < T; i += kBT)
+      if (tstart + i > N - 1) npq_row[i] = last;
+  }
+  for (int64_t s2 = carry + tid; s2 < p.k_max; s2 += kBT) {
+    idx_row[s2] = (int32_t)N;
+    npk_row[s2] = 0.f;
+    if (mask_row) mask_row[s2] = 0;
+  }
+  if (tid == 0) {
+    p.usize[nt_row] = usize;
+    p.kept_size[nt_row] = (int32_t)carry;
+  }
+}
+
 }  // namespace
+
+int launch_build_sets_chunk(const sta_build_chunk_args* a, cudaStream_t stream) {
+  if (!a || !a->votes || !a->idx || !a->newpos_k || !a->newpos_q || !a->usize || !a->kept_size)
+    return fail(STA_ERR_ARG, "sta_build_sets_chunk: null pointer");
+  if (a->select_score != STA_SCORE_FREQ && !a->wvotes)
+    return fail(STA_ERR_ARG, "sta_build_sets_chunk: weighted ranking needs wvotes");
+  if (a->chunk_size <= 0 || a->n_chunk < 0 || a->k_max <= 0 || a->tile <= 0 || a->tile > 255)
+    return fail(STA_ERR_ARG, "sta_build_sets_chunk: bad chunk_size / n_chunk / k_max / tile");
+  if (a->n <= 0 || a->heads <= 0) return STA_OK;
+  BuildChunkP p;
+  p.votes = a->votes;
+  p.wvotes = a->wvotes;
+  p.BH = a->heads;
+  p.N = a->n;
+  p.T = a->tile;
+  p.nt = (a->n + a->tile - 1) / a->tile;
+  p.head_stride = tri_head_stride(a->n, a->tile);
+  p.k_max = a->k_max;
+  p.n_global = a->n_global;
+  p.n_local = a->n_local;
+  p.C = a->chunk_size;
+  p.n_chunk = a->n_chunk;
+  p.weighted = a->select_score != STA_SCORE_FREQ;
+  p.mean_agg = a->chunk_agg == 1;
+  p.idx = a->idx;
+  p.newpos_k = a->newpos_k;
+  p.newpos_q = a->newpos_q;
+  p.mask = a->mask;
+  p.usize = a->usize;
+  p.kept_size = a->kept_size;
+  const int64_t nC = (a->n + a->chunk_size - 1) / a->chunk_size;
+  const size_t smem = (size_t)nC * 5 + 16;
+  if (smem > 200 * 1024) return fail(STA_ERR_UNSUPPORTED, "sta_build_sets_chunk: too many chunks");
+  if (p.nt > 0x7fffffff || p.BH > 65535) return fail(STA_ERR_UNSUPPORTED, "sta_build_sets_chunk: grid");
+  cudaError_t e = cudaFuncSetAttribute(build_sets_chunk_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return fail(STA_ERR_CUDA, cudaGetErrorString(e));
+  dim3 grid((unsigned)p.nt, (unsigned)p.BH);
+  build_sets_chunk_kernel<<<grid, kBT, smem, stream>>>(p);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? STA_OK : fail(STA_ERR_CUDA, cudaGetErrorString(e));
+}
 
 int launch_build_sets(const sta_build_args* a, cudaStream_t stream) {
   if (!a || !a->votes || !a->idx || !a->newpos_k || !a->newpos_q || !a->shared_size ||

@@ -24,6 +24,7 @@ int launch_rope_split(const void* x, int dtype, int64_t heads, int64_t N, int D,
 int launch_select(const sta_select_args* a, cudaStream_t stream);
 int launch_build_sets(const sta_build_args* a, cudaStream_t stream);
 int launch_build_sets_pq(const sta_build_pq_args* a, cudaStream_t stream);
+int launch_build_sets_chunk(const sta_build_chunk_args* a, cudaStream_t stream);
 int launch_gather_attend(const sta_attend_args* a, cudaStream_t stream);
 int launch_pqstream(const sta_pqstream_args* a, cudaStream_t stream);
 

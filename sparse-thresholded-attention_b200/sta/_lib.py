@@ -48,6 +48,14 @@ class BuildPQArgs(ctypes.Structure):
                 ("kept_size", c_vp), ("overflow", c_vp)]
 
 
+class BuildChunkArgs(ctypes.Structure):
+    _fields_ = [("votes", c_vp), ("wvotes", c_vp), ("heads", c_i64), ("n", c_i64),
+                ("tile", c_i32), ("k_max", c_i32), ("n_global", c_i32), ("n_local", c_i32),
+                ("chunk_size", c_i32), ("n_chunk", c_i32), ("select_score", c_i32),
+                ("chunk_agg", c_i32), ("idx", c_vp), ("newpos_k", c_vp), ("newpos_q", c_vp),
+                ("mask", c_vp), ("usize", c_vp), ("kept_size", c_vp)]
+
+
 class AttendArgs(ctypes.Structure):
     _fields_ = [("q", c_vp), ("q_stride_h", c_i64), ("q_stride_n", c_i64),
                 ("k", c_vp), ("k_stride_h", c_i64), ("k_stride_n", c_i64),
@@ -90,7 +98,8 @@ class ForwardArgs(ctypes.Structure):
                 ("overflow20", c_vp), ("span", c_vp), ("kept_rows", c_vp), ("blocks", c_vp),
                 ("skipped", c_vp), ("idx_out", c_vp), ("newpos_k_out", c_vp),
                 ("newpos_q_out", c_vp), ("mask_out", c_vp), ("max_workspace_bytes", c_i64),
-                ("stage_events", c_vp), ("same_geometry", c_i32)]
+                ("stage_events", c_vp), ("same_geometry", c_i32), ("chunk_size", c_i32),
+                ("n_chunk", c_i32), ("chunk_agg", c_i32)]
 
 
 # every symbol include/sta.h declares (checked by the CPU test suite)
@@ -99,7 +108,8 @@ EXPORTED = ["sta_last_error", "sta_version", "sta_tri_head_stride", "sta_rope_sp
             "sta_pqstream_attend", "sta_shared_workspace_bytes", "sta_shared_forward",
             "sta_pq_union_workspace_bytes", "sta_pq_union_forward",
             "sta_pq_stream_workspace_bytes", "sta_pq_stream_forward", "sta_device_error",
-            "sta_shared_forward_static"]
+            "sta_shared_forward_static", "sta_build_sets_chunk", "sta_chunk_workspace_bytes",
+            "sta_chunk_forward"]
 
 _lib = None
 
@@ -122,11 +132,12 @@ def lib():
                                  c_f32, c_vp, c_vp, c_vp]
     for name, st in (("sta_select", SelectArgs), ("sta_build_sets", BuildArgs),
                      ("sta_build_sets_pq", BuildPQArgs), ("sta_gather_attend", AttendArgs),
+                     ("sta_build_sets_chunk", BuildChunkArgs),
                      ("sta_pqstream_attend", PQStreamArgs)):
         f = getattr(L, name)
         f.restype = ctypes.c_int
         f.argtypes = [ctypes.POINTER(st), c_vp]
-    for v in ("shared", "pq_union", "pq_stream"):
+    for v in ("shared", "pq_union", "pq_stream", "chunk"):
         f = getattr(L, f"sta_{v}_workspace_bytes")
         f.restype = ctypes.c_size_t
         f.argtypes = [ctypes.POINTER(ForwardArgs)]

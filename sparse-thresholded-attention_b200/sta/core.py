@@ -68,7 +68,8 @@ def _check_inputs(q, k, v):
 def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=None,
             pct=30.0, n_global=32, n_local=32, tile=32, k_max=1024, select_score="freq",
             measure=False, block_n=32, pos_advance="max", use_skip=True, keep_sets=False,
-            max_workspace_bytes=0, stage_events=None):
+            max_workspace_bytes=0, stage_events=None, chunk_size=16, n_chunk=0,
+            chunk_agg="sum"):
     """Run one prefill op.  variant: 'shared' | 'pq_union' | 'pq_stream'.
     q (Z,H,N,D); k, v (Z,Hkv,N,D) with H % Hkv == 0 (Hkv == H for repeat_kv-expanded input).
     Returns (out (Z,H,N,D), dict of per-(head, tile) statistics [+ sets when keep_sets])."""
@@ -100,6 +101,9 @@ def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=
         st["usize"] = torch.empty((Z, H, nt), **i32)
         st["kept_size"] = torch.empty((Z, H, nt), **i32)
         st["overflow"] = torch.empty((Z, H, nt), dtype=torch.uint8, device=dev)
+    elif variant == "chunk":
+        st["usize"] = torch.empty((Z, H, nt), **i32)
+        st["kept_size"] = torch.empty((Z, H, nt), **i32)
     elif variant == "pq_stream":
         f32 = dict(dtype=torch.float32, device=dev)
         st["span"] = torch.empty((Z, H, nt), **f32)
@@ -113,14 +117,11 @@ def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=
         sets["idx"] = torch.empty((Z, H, nt, k_max), **i32)
         sets["newpos_k"] = torch.empty((Z, H, nt, k_max), dtype=torch.float32, device=dev)
         sets["newpos_q"] = torch.empty((Z, H, nt, T), dtype=torch.float32, device=dev)
-        if variant == "pq_union":
+        if variant in ("pq_union", "chunk"):
             sets["mask"] = torch.empty((Z, H, nt, k_max), **i32)
     lib = L.lib()
-    fn_ws = getattr(lib, {"shared": "sta_shared_workspace_bytes",
-                          "pq_union": "sta_pq_union_workspace_bytes",
-                          "pq_stream": "sta_pq_stream_workspace_bytes"}[variant])
-    fn = getattr(lib, {"shared": "sta_shared_forward", "pq_union": "sta_pq_union_forward",
-                       "pq_stream": "sta_pq_stream_forward"}[variant])
+    fn_ws = getattr(lib, f"sta_{variant}_workspace_bytes")
+    fn = getattr(lib, f"sta_{variant}_forward")
     stream = _stream()
     ws = None
     for b in range(Z):
@@ -154,6 +155,11 @@ def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=
             a.shared_size = st["usize"][b].data_ptr()
             a.kept_size = st["kept_size"][b].data_ptr()
             a.overflow = st["overflow"][b].data_ptr()
+        elif variant == "chunk":
+            a.shared_size = st["usize"][b].data_ptr()
+            a.kept_size = st["kept_size"][b].data_ptr()
+            a.chunk_size, a.n_chunk = int(chunk_size), int(n_chunk)
+            a.chunk_agg = {"sum": 0, "mean": 1}[chunk_agg]
         else:
             a.span = st["span"][b].data_ptr()
             a.kept_rows = st["kept"][b].data_ptr()
@@ -352,3 +358,27 @@ def gather_attend(q, k, v, idx, newpos_k, newpos_q, g: Geometry, *, tile, sm_sca
     a.sm_scale = float(sm_scale)
     L.check(L.lib().sta_gather_attend(ctypes.byref(a), _stream()), "sta_gather_attend")
     return out
+
+
+def build_sets_chunk(votes_c, wvotes_c, H, N, *, k_max, chunk_size=16, n_chunk, tile=32,
+                     n_global=32, n_local=32, select_score="expmass", chunk_agg="sum"):
+    dev = votes_c.device
+    T = tile
+    nt = (N + T - 1) // T
+    i32 = dict(dtype=torch.int32, device=dev)
+    o = dict(idx=torch.empty((H, nt, k_max), **i32),
+             newpos_k=torch.empty((H, nt, k_max), dtype=torch.float32, device=dev),
+             newpos_q=torch.empty((H, nt, T), dtype=torch.float32, device=dev),
+             mask=torch.empty((H, nt, k_max), **i32), usize=torch.empty((H, nt), **i32),
+             kept_size=torch.empty((H, nt), **i32))
+    a = L.BuildChunkArgs()
+    a.votes = votes_c.data_ptr()
+    a.wvotes = wvotes_c.data_ptr() if wvotes_c is not None else None
+    a.heads, a.n, a.tile, a.k_max = H, N, T, k_max
+    a.n_global, a.n_local, a.chunk_size, a.n_chunk = n_global, n_local, chunk_size, n_chunk
+    a.select_score = L.SCORE[select_score]
+    a.chunk_agg = {"sum": 0, "mean": 1}[chunk_agg]
+    for name in ("idx", "newpos_k", "newpos_q", "mask", "usize", "kept_size"):
+        setattr(a, name, o[name].data_ptr())
+    L.check(L.lib().sta_build_sets_chunk(ctypes.byref(a), _stream()), "sta_build_sets_chunk")
+    return o

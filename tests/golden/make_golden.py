@@ -64,7 +64,12 @@ def inputs(H, N, D, seed, dtype, planted=8, Hkv=None):
     return q, k, v
 
 
+ONLY = None
+
+
 def save(name, meta, arrays):
+    if ONLY and ONLY not in name:
+        return
     path = os.path.join(HERE, name + ".npz")
     out = {k: _np(v) for k, v in arrays.items()}
     for k, v in list(out.items()):
@@ -177,10 +182,65 @@ def gen_pqstream(case, H, N, D, seed, dtype, block_n=32, pos_advance="max", use_
                           kept=kept, blocks=blocks, skipped=skipped))
 
 
+def install_chunk_shim():
+    """The reference's chunked module imports `chunk_recall_core.forced_chunk_mask`, which the
+    reference repository does not ship.  Its own golden (chunk_attention_torch,
+    shared_selection_triton_chunked.py:378-384) restates the rule inline; this test-only shim
+    returns the same (forced, visible) masks, shape (nt, nC), so the module can be imported."""
+    import types
+    shim = types.ModuleType("chunk_recall_core")
+
+    def forced_chunk_mask(nt, nC, C, N, T, n_global, n_local, q_pos_base, dev):
+        c = torch.arange(nC, device=dev)
+        t = torch.arange(nt, device=dev)
+        r0 = q_pos_base + t * T
+        last_q = (q_pos_base + (t + 1) * T).clamp(max=N) - 1
+        vis = c[None, :] * C <= last_q[:, None]
+        glob = (c < (n_global + C - 1) // C)[None, :]
+        lo = (r0 - n_local + 1).clamp(min=0) // C
+        hi = last_q // C
+        loc = (c[None, :] >= lo[:, None]) & (c[None, :] <= hi[:, None])
+        return (glob | loc) & vis, vis
+
+    shim.forced_chunk_mask = forced_chunk_mask
+    sys.modules["chunk_recall_core"] = shim
+
+
+def gen_chunk(case, H, N, D, k_max, seed, dtype, select_score="expmass", chunk_size=16,
+              chunk_agg="sum", tau_val=5.0, planted=8):
+    install_chunk_shim()
+    mod = __import__("shared_selection_triton_chunked")
+    q, k, v = inputs(H, N, D, seed, dtype, planted=planted)
+    tau = torch.full((H,), float(tau_val))
+    invf = rope_inv_freq(D, 1e4)
+    meta = dict(kind="chunk", H=H, N=N, D=D, T=32, k_max=k_max, seed=seed,
+                dtype=str(dtype).replace("torch.", ""), select_score=select_score,
+                chunk_size=chunk_size, chunk_agg=chunk_agg, pos_scale_a=0.5, rope_scale_a=1.0,
+                n_global=32, n_local=32, block_k=64)
+    with Capture(mod, "_build_sets_chunk") as cap:
+        res = mod.shared_chunk_attention(q, k, v, tau, invf, invf, pos_scale_a=0.5,
+                                         k_max=k_max, chunk_size=chunk_size,
+                                         select_score=select_score, chunk_agg=chunk_agg)
+    golden = mod.chunk_attention_torch(q, k, v, tau, invf, invf, pos_scale_a=0.5, k_max=k_max,
+                                       chunk_size=chunk_size, select_score=select_score,
+                                       chunk_agg=chunk_agg)
+    votes, wvotes = cap.args[0], cap.args[1]
+    sets = cap.result
+    arrays = dict(q=q[0], k=k[0], v=v[0], tau=tau, inv_freq_a=invf, inv_freq_c=invf,
+                  out=res[0][0], out_torch_golden=golden[0], usize=res[1], kept_size=res[2],
+                  votes=votes, idx=sets[0], newpos_k=sets[1], newpos_q=sets[2], mask=sets[3])
+    if wvotes.shape[-1] == N:
+        arrays["wvotes"] = wvotes
+    save(case, meta, arrays)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", default=None, help="generate only cases whose name contains this")
     args = ap.parse_args()
+    global ONLY
+    ONLY = args.only
     sys.path.insert(0, args.ref)
     torch.set_num_threads(os.cpu_count() or 1)
     # fp32 only: the Triton interpreter does not evaluate bf16 arithmetic faithfully (numpy has
@@ -207,6 +267,10 @@ def main():
     gen_pq("pq_union_freq_f32", 2, 256, 64, 4096, 22, f32, select_score="freq")
     gen_pq("pq_union_yarn_f32", 2, 256, 64, 128, 23, f32, geom="yarn")
     # PQ-Stream: max / full advance, skip on/off, ragged N, BN 32 and 64
+    # chunk_exact: chunk-granular selection, exact static budget
+    gen_chunk("chunk_expmass_f32", 2, 384, 64, 256, 41, f32)
+    gen_chunk("chunk_freq_f32", 2, 320, 64, 192, 42, f32, select_score="freq")
+    gen_chunk("chunk_mean_c32_f32", 2, 384, 64, 384, 43, f32, chunk_size=32, chunk_agg="mean")
     gen_pqstream("pqstream_max_f32", 2, 300, 64, 31, f32)
     gen_pqstream("pqstream_full_f32", 2, 256, 64, 32, f32, pos_advance="full")
     gen_pqstream("pqstream_bn64_f32", 2, 288, 64, 33, f32, block_n=64, geom="yarn")

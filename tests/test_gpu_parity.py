@@ -333,3 +333,70 @@ def test_errors_are_loud():
         ex2.shared_pi_attention(q, q, q, torch.ones(2), rope_inv_freq(64, 1e4), q_pos_base=3)
     with pytest.raises((ValueError, RuntimeError)):
         ex2.shared_pi_attention(q, q, q, torch.ones(2), rope_inv_freq(64, 1e4), tile=48)
+
+
+# ---------------------------------------------------------------------------------------------
+# chunk_exact
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("name", names("chunk"))
+def test_build_sets_chunk_on_reference_votes(name):
+    from test_oracle import chunk_tiles_without_ties
+    meta, a = load(name)
+    H, N, C = meta["H"], meta["N"], meta["chunk_size"]
+    votes = core.compact_from_dense(cu(a["votes"].astype(np.uint8)), 32)
+    wv = None
+    if meta["select_score"] != "freq":
+        wv = core.compact_from_dense(cu(a["wvotes"].astype(np.float32)), 32)
+    n_chunk = oracle.derive_n_chunk(meta["k_max"], C, 32, 32, 32)
+    o = core.build_sets_chunk(votes, wv, H, N, k_max=meta["k_max"], chunk_size=C,
+                              n_chunk=n_chunk, select_score=meta["select_score"],
+                              chunk_agg=meta["chunk_agg"])
+    idx = o["idx"].cpu().numpy()
+    exact = chunk_tiles_without_ties(a, meta, n_chunk, idx)
+    for key in ("idx", "newpos_k", "newpos_q", "mask", "usize", "kept_size"):
+        np.testing.assert_array_equal(o[key].cpu().numpy()[exact], a[key][exact], err_msg=key)
+    # identical to the oracle everywhere (same tie rule)
+    ws = a.get("wvotes") if meta["select_score"] != "freq" else None
+    ref = oracle.build_sets_chunk(a["votes"], ws, 32, 32, 32, meta["k_max"], C, n_chunk,
+                                  select_score=meta["select_score"], chunk_agg=meta["chunk_agg"])
+    np.testing.assert_array_equal(idx, ref[0])
+    np.testing.assert_array_equal(o["kept_size"].cpu().numpy(), ref[5])
+
+
+@pytest.mark.parametrize("name", names("chunk"))
+def test_chunk_end_to_end_vs_reference(name):
+    from sta import shared_selection_chunked as ch
+    meta, a = load(name)
+    q, k, v = (cu(a[x])[None] for x in ("q", "k", "v"))
+    out, usize, kept = ch.shared_chunk_attention(
+        q, k, v, torch.from_numpy(a["tau"]), torch.from_numpy(a["inv_freq_a"]),
+        torch.from_numpy(a["inv_freq_c"]), meta["pos_scale_a"], meta["rope_scale_a"],
+        k_max=meta["k_max"], chunk_size=meta["chunk_size"], select_score=meta["select_score"],
+        chunk_agg=meta["chunk_agg"])
+    np.testing.assert_array_equal(usize.cpu().numpy(), a["usize"])
+    np.testing.assert_array_equal(kept.cpu().numpy(), a["kept_size"])
+    res = oracle.chunk_attention(a["q"], a["k"], a["v"], a["tau"], a["inv_freq_a"],
+                                 a["inv_freq_c"], meta["pos_scale_a"], meta["rope_scale_a"],
+                                 k_max=meta["k_max"], chunk_size=meta["chunk_size"],
+                                 select_score=meta["select_score"], chunk_agg=meta["chunk_agg"])
+    assert_close_out(out[0], res[0], torch.float32)
+    if meta["select_score"] != "freq":      # no chunk-mass ties: the reference's own output
+        assert_close_out(out[0], a["out"], torch.float32)
+
+
+def test_chunk_bf16_gqa_vs_oracle():
+    from sta import shared_selection_chunked as ch
+    H, Hk, N, D = 4, 2, 1024, 128
+    q, k, v = make_inputs(SynthSpec(n_heads=H, n_kv_heads=Hk, seq_len=N, head_dim=D, seed=60,
+                                    dtype=torch.bfloat16))
+    tau = torch.full((H,), 5.0)
+    invf = rope_inv_freq(D, 1e4)
+    out, usize, kept = ch.shared_chunk_attention(cu(q), cu(k), cu(v), tau, invf, invf, 0.5,
+                                                 k_max=512)
+    G = H // Hk
+    res = oracle.chunk_attention(q[0].float().numpy(), np.repeat(k[0].float().numpy(), G, 0),
+                                 np.repeat(v[0].float().numpy(), G, 0), tau.numpy(),
+                                 invf.numpy(), invf.numpy(), 0.5, k_max=512, v_is_bf16=True)
+    err = np.abs(out[0].float().cpu().numpy() - res[0])
+    assert err.mean() <= BF16_MEAN and np.quantile(err, 0.9999) <= BF16_MAX
+    assert int(kept.max()) <= 512

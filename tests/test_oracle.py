@@ -149,3 +149,59 @@ def test_dca_position_rule():
     assert qc_t.max() - k_t.min() < 4096
     assert abs(oracle.dca_mscale(8192, 4096) - (0.05 * np.log(2.0) + 1)) < 1e-12
     assert oracle.dca_mscale(4096, 4096) == 1.0
+
+
+@pytest.mark.parametrize("path", [p for p in FIXTURES if "chunk" in p],
+                         ids=ids([p for p in FIXTURES if "chunk" in p]))
+def test_chunk(path):
+    meta, a = load(path)
+    ws = a.get("wvotes") if meta["select_score"] != "freq" else None
+    n_chunk = oracle.derive_n_chunk(meta["k_max"], meta["chunk_size"], 32, 32, 32)
+    sets = oracle.build_sets_chunk(a["votes"], ws, 32, 32, 32, meta["k_max"], meta["chunk_size"],
+                                   n_chunk, select_score=meta["select_score"],
+                                   chunk_agg=meta["chunk_agg"])
+    exact = chunk_tiles_without_ties(a, meta, n_chunk, sets[0])
+    for i, key in enumerate(("idx", "newpos_k", "newpos_q", "mask", "usize", "kept_size")):
+        np.testing.assert_array_equal(sets[i][exact], a[key][exact], err_msg=key)
+    if not exact.all():
+        return
+    res = oracle.chunk_attention(a["q"], a["k"], a["v"], a["tau"], a["inv_freq_a"],
+                                 a["inv_freq_c"], meta["pos_scale_a"], meta["rope_scale_a"],
+                                 k_max=meta["k_max"], chunk_size=meta["chunk_size"],
+                                 select_score=meta["select_score"], chunk_agg=meta["chunk_agg"])
+    for ref in (a["out"], a["out_torch_golden"]):
+        err = np.abs(res[0] - ref)
+        assert err.max() <= 1e-4, err.max()
+
+
+def chunk_tiles_without_ties(a, meta, n_chunk, idx):
+    """Tiles whose chunk selection does not depend on a tie at the top-n_chunk cut.  In the
+    other tiles the two selections may differ, but only inside the tied group: same number of
+    chunks, every difference a chunk whose mass equals the cut (checked here)."""
+    votes = a["votes"]
+    H, nt, N = votes.shape
+    C = meta["chunk_size"]
+    nC = (N + C - 1) // C
+    if meta["select_score"] == "freq" or "wvotes" not in a:
+        rv = votes.astype(np.float32)
+    else:
+        rv = a["wvotes"].astype(np.float32)
+    pad = nC * C - N
+    mass = np.pad(np.where(votes > 0, rv, 0), ((0, 0), (0, 0), (0, pad))).reshape(H, nt, nC, C).sum(-1)
+    forced, vis = oracle.forced_chunk_mask(nt, nC, C, N, 32, 32, 32)
+    exact = np.ones((H, nt), bool)
+    for h in range(H):
+        for t in range(nt):
+            cand = np.nonzero(vis[t] & ~forced[t])[0]
+            if len(cand) <= n_chunk:
+                continue
+            cut = np.sort(mass[h, t, cand])[::-1][n_chunk - 1]
+            ties = set(cand[mass[h, t, cand] == cut].tolist())
+            if len(ties) <= 1:
+                continue
+            ours = set((idx[h, t][idx[h, t] < N] // C).tolist())
+            ref = set((a["idx"][h, t][a["idx"][h, t] < N] // C).tolist())
+            assert len(ours) == len(ref)
+            assert (ours ^ ref) <= ties
+            exact[h, t] = ours == ref
+    return exact
