@@ -62,6 +62,15 @@ int sta_rope_split(const void* x, int32_t dtype, int64_t heads, int64_t n, int32
                    int64_t stride_h, int64_t stride_n, const float* inv_freq, float pos_scale,
                    float rope_scale, void* out_hi, void* out_lo, void* stream);
 
+/* Dual Chunk Attention position ids (ChunkLlama rotary tables, dca_kernel.py:194-231):
+ * chunk_len L = chunk_size - local_window; role 0 linear n, 1 keys and same-chunk queries
+ * n mod L, 2 queries scoring the previous chunk min(L + n mod L, chunk_size), 3 queries scoring
+ * older chunks min(2L - 1, chunk_size).  Otherwise as sta_rope_split (pos_scale 1). */
+int sta_rope_split_dca(const void* x, int32_t dtype, int64_t heads, int64_t n, int32_t d,
+                       int64_t stride_h, int64_t stride_n, const float* inv_freq, float rope_scale,
+                       int32_t chunk_size, int32_t local_window, int32_t role, void* out_hi,
+                       void* out_lo, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Stage 1 -- exact-max two-pass selection on tcgen05 tensor cores (Kernel A).
  * Replaces _select_vote_kernel (shared_selection_triton_exact_2.py:50-140) and
@@ -87,6 +96,10 @@ typedef struct sta_select_args {
   uint32_t* bits;          /* compact per-query keep bits (tile == 32 only), or NULL */
   float* row_max;          /* (batch*n_heads, n) exact row max, or NULL */
   int32_t* row_count;      /* (batch*n_heads, n) kept keys per query, or NULL */
+  /* > 0: Dual Chunk Attention selection geometry with this chunk length (multiple of 256);
+   * q_hi / q_lo then hold 3 planes (3, batch*n_heads, n, d): queries rotated for keys of the
+   * same chunk, of the previous chunk and of older chunks (sta_rope_split_dca roles 1, 2, 3) */
+  int32_t dca_chunk_len;
 } sta_select_args;
 
 int sta_select(const sta_select_args* a, void* stream);
@@ -319,6 +332,10 @@ typedef struct sta_forward_args {
   int32_t chunk_size;
   int32_t n_chunk;
   int32_t chunk_agg;
+  /* > 0: the selection geometry uses Dual Chunk Attention position ids (chunk_size s, local
+   * window w, chunk_len s - w a multiple of 256) with inv_freq_a / rope_scale_a */
+  int32_t dca_chunk_size;
+  int32_t dca_local_window;
 } sta_forward_args;
 
 size_t sta_shared_workspace_bytes(const sta_forward_args* a);

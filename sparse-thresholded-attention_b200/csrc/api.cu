@@ -112,8 +112,9 @@ Layout layout_for(const sta_forward_args* a, Variant v, int64_t c) {
     o += al(bytes);
     return r;
   };
-  L.qh = take(qh * N * D * 2);
-  L.ql = take(qh * N * D * 2);
+  const int64_t qplanes = a->dca_chunk_size > 0 ? 3 : 1;
+  L.qh = take(qplanes * qh * N * D * 2);
+  L.ql = take(qplanes * qh * N * D * 2);
   L.kh = take(c * N * D * 2);
   L.kl = take(c * N * D * 2);
   if (v == kPQStream) {
@@ -161,6 +162,13 @@ int check_forward(const sta_forward_args* a, Variant v) {
       return fail(STA_ERR_ARG, "forward: chunk statistics outputs required");
   }
   if (v != kPQStream && a->k_max <= 0) return fail(STA_ERR_ARG, "forward: k_max must be > 0");
+  if (a->dca_chunk_size > 0) {
+    const int64_t L = (int64_t)a->dca_chunk_size - a->dca_local_window;
+    if (a->dca_local_window <= 0 || L <= 0 || L % 256)
+      return fail(STA_ERR_UNSUPPORTED,
+                  "forward: DCA needs 0 < local_window < chunk_size and chunk_size - local_window a multiple of 256");
+    if (v == kPQStream) return fail(STA_ERR_UNSUPPORTED, "forward: DCA selection is not wired into PQ-Stream");
+  }
   if (v == kShared && !(a->shared_size && a->kept_size && a->chosen && a->overflow &&
                         a->kpct_meas && a->overflow20))
     return fail(STA_ERR_ARG, "forward: shared statistics outputs required");
@@ -208,12 +216,26 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
         if (a->stage_events) cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), st);
       };
       mark(0);
-      STA_TRY(launch_rope_split(q, a->dtype, qn, N, a->d, a->q_stride_h, a->q_stride_n,
-                                a->inv_freq_a, a->pos_scale_a, a->rope_scale_a, w + L.qh,
-                                w + L.ql, st));
-      STA_TRY(launch_rope_split(k, a->dtype, c, N, a->d, a->k_stride_h, a->k_stride_n,
-                                a->inv_freq_a, a->pos_scale_a, a->rope_scale_a, w + L.kh,
-                                w + L.kl, st));
+      const bool dca = a->dca_chunk_size > 0;
+      const int64_t dL = dca ? (int64_t)a->dca_chunk_size - a->dca_local_window : 0;
+      if (!dca) {
+        STA_TRY(launch_rope_split(q, a->dtype, qn, N, a->d, a->q_stride_h, a->q_stride_n,
+                                  a->inv_freq_a, a->pos_scale_a, a->rope_scale_a, w + L.qh,
+                                  w + L.ql, st));
+        STA_TRY(launch_rope_split(k, a->dtype, c, N, a->d, a->k_stride_h, a->k_stride_n,
+                                  a->inv_freq_a, a->pos_scale_a, a->rope_scale_a, w + L.kh,
+                                  w + L.kl, st));
+      } else {
+        const size_t plane = (size_t)qn * N * a->d * 2;
+        for (int role = 1; role <= 3; ++role)
+          STA_TRY(launch_rope_split(q, a->dtype, qn, N, a->d, a->q_stride_h, a->q_stride_n,
+                                    a->inv_freq_a, 1.0f, a->rope_scale_a,
+                                    w + L.qh + (role - 1) * plane, w + L.ql + (role - 1) * plane,
+                                    st, role, dL, a->dca_chunk_size));
+        STA_TRY(launch_rope_split(k, a->dtype, c, N, a->d, a->k_stride_h, a->k_stride_n,
+                                  a->inv_freq_a, 1.0f, a->rope_scale_a, w + L.kh, w + L.kl, st,
+                                  1, dL, a->dca_chunk_size));
+      }
       sta_select_args s{};
       s.q_hi = w + L.qh;
       s.q_lo = w + L.ql;
@@ -227,6 +249,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       s.tile = T;
       s.sm_scale = a->sm_scale;
       s.tau = tau;
+      s.dca_chunk_len = (int32_t)dL;
       mark(1);
       if (v == kPQStream) {
         s.max_only = 1;
@@ -369,7 +392,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       ca.k_hi = w + L.kh;
       ca.k_lo = w + L.kl;
       ca.pos_scale_sel = a->pos_scale_a;
-      ca.same_geometry = (v == kShared && a->same_geometry) ? 1 : 0;
+      ca.same_geometry = (v == kShared && a->same_geometry && !dca) ? 1 : 0;
       STA_TRY(launch_gather_attend(&ca, st));
       mark(4);
     }
@@ -402,6 +425,21 @@ int sta_rope_split(const void* x, int32_t dtype, int64_t heads, int64_t n, int32
     return fail(STA_ERR_UNSUPPORTED, "sta_rope_split: dtype");
   return launch_rope_split(x, dtype, heads, n, d, stride_h, stride_n, inv_freq, pos_scale,
                            rope_scale, out_hi, out_lo, static_cast<cudaStream_t>(stream));
+}
+
+int sta_rope_split_dca(const void* x, int32_t dtype, int64_t heads, int64_t n, int32_t d,
+                       int64_t stride_h, int64_t stride_n, const float* inv_freq, float rope_scale,
+                       int32_t chunk_size, int32_t local_window, int32_t role, void* out_hi,
+                       void* out_lo, void* stream) {
+  if (!x || !inv_freq || !out_hi || !out_lo) return fail(STA_ERR_ARG, "sta_rope_split_dca: null pointer");
+  if (d <= 0 || (d & 1)) return fail(STA_ERR_ARG, "sta_rope_split_dca: d must be even");
+  if (role < 0 || role > 3 || local_window <= 0 || chunk_size <= local_window)
+    return fail(STA_ERR_ARG, "sta_rope_split_dca: bad role / chunk_size / local_window");
+  if (dtype != STA_DTYPE_F32 && dtype != STA_DTYPE_BF16)
+    return fail(STA_ERR_UNSUPPORTED, "sta_rope_split_dca: dtype");
+  return launch_rope_split(x, dtype, heads, n, d, stride_h, stride_n, inv_freq, 1.0f, rope_scale,
+                           out_hi, out_lo, static_cast<cudaStream_t>(stream), role,
+                           (int64_t)chunk_size - local_window, chunk_size);
 }
 
 int sta_select(const sta_select_args* a, void* stream) {

@@ -20,14 +20,26 @@ __device__ __forceinline__ float load_f<__nv_bfloat16>(const __nv_bfloat16* p) {
   return __bfloat162float(*p);
 }
 
+// Position id of row n: linear n (mode 0) or one of the Dual Chunk Attention position sets of
+// ChunkLlama's rotary tables (dca_kernel.py:194-231, chunk_len L = chunk_size s - local window):
+// mode 1 keys and same-chunk queries n mod L; mode 2 queries against the previous chunk
+// min(L + n mod L, s); mode 3 queries against older chunks min(2L - 1, s).
+__device__ __forceinline__ int64_t position_id(int64_t n, int mode, int64_t L, int64_t s) {
+  if (mode == 1) return n % L;
+  if (mode == 2) return min(L + n % L, s);
+  if (mode == 3) return min(2 * L - 1, s);
+  return n;
+}
+
 // One thread per (row, frequency pair).  x is (rows = heads*N, D) with element strides
-// (stride_h, stride_n); last dim contiguous.  Position of row n is float(n) * pos_scale.
+// (stride_h, stride_n); last dim contiguous.  Angle = (float(position_id) * pos_scale) * inv_freq.
 template <typename T>
 __global__ void rope_split_kernel(const T* __restrict__ x, int64_t heads, int64_t N, int D,
                                   int64_t stride_h, int64_t stride_n,
                                   const float* __restrict__ inv_freq, float pos_scale,
                                   float rope_scale, __nv_bfloat16* __restrict__ hi,
-                                  __nv_bfloat16* __restrict__ lo) {
+                                  __nv_bfloat16* __restrict__ lo, int mode, int64_t dca_L,
+                                  int64_t dca_s) {
   const int half = D >> 1;
   const int64_t total = heads * N * half;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -39,7 +51,8 @@ __global__ void rope_split_kernel(const T* __restrict__ x, int64_t heads, int64_
     const T* src = x + h * stride_h + n * stride_n;
     const float x1 = load_f(src + f);
     const float x2 = load_f(src + f + half);
-    const float ang = __fmul_rn(__fmul_rn((float)n, pos_scale), __ldg(inv_freq + f));
+    const float pid = (float)position_id(n, mode, dca_L, dca_s);
+    const float ang = __fmul_rn(__fmul_rn(pid, pos_scale), __ldg(inv_freq + f));
     float r1, r2;
     rope_pair(x1, x2, ang, rope_scale, r1, r2);
     __nv_bfloat16 h1, l1, h2, l2;
@@ -56,7 +69,7 @@ __global__ void rope_split_kernel(const T* __restrict__ x, int64_t heads, int64_
 int launch_rope_split(const void* x, int dtype, int64_t heads, int64_t N, int D,
                       int64_t stride_h, int64_t stride_n, const float* inv_freq,
                       float pos_scale, float rope_scale, void* hi, void* lo,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, int mode, int64_t dca_L, int64_t dca_s) {
   const int64_t total = heads * N * (D / 2);
   if (total == 0) return 0;
   const int threads = 256;
@@ -65,12 +78,13 @@ int launch_rope_split(const void* x, int dtype, int64_t heads, int64_t N, int D,
   if (dtype == STA_DTYPE_F32) {
     rope_split_kernel<float><<<(unsigned)blocks, threads, 0, stream>>>(
         static_cast<const float*>(x), heads, N, D, stride_h, stride_n, inv_freq, pos_scale,
-        rope_scale, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo));
+        rope_scale, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), mode, dca_L,
+        dca_s);
   } else {
     rope_split_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(x), heads, N, D, stride_h, stride_n, inv_freq,
         pos_scale, rope_scale, static_cast<__nv_bfloat16*>(hi),
-        static_cast<__nv_bfloat16*>(lo));
+        static_cast<__nv_bfloat16*>(lo), mode, dca_L, dca_s);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : STA_ERR_CUDA;
 }

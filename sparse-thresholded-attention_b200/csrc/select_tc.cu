@@ -63,7 +63,16 @@ struct Params {
   int32_t* row_count;
   int* err;
   int64_t head_stride;  // compact per-head stride
+  int64_t dca_L;        // > 0: Dual Chunk Attention selection geometry, chunk_len (multiple of 256)
 };
+
+// Which rotated Q plane scores key block kb of query block qb: 0 = plain (or same DCA chunk),
+// 1 = the previous DCA chunk, 2 = older DCA chunks.
+__device__ __forceinline__ int q_plane(const Params& p, int qb, int kb) {
+  if (p.dca_L <= 0) return 0;
+  const int64_t rel = ((int64_t)qb * BM) / p.dca_L - ((int64_t)kb * BN) / p.dca_L;
+  return rel <= 0 ? 0 : (rel == 1 ? 1 : 2);
+}
 
 // lane l receives sum over the warp's lanes of v[l] (fixed butterfly order, 31 shuffles)
 __device__ __forceinline__ float transpose_reduce32(float (&v)[32]) {
@@ -189,22 +198,33 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
       prefetch_tmap(&tm_qlo);
       prefetch_tmap(&tm_khi);
       prefetch_tmap(&tm_klo);
-      uint32_t kc = 0;
+      uint32_t kc = 0, qloads = 0;
       int it = 0;
       bool ok = true;
       for (int64_t w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
         int64_t bh, kvh;
         int qb;
         decode_item(w, p, bh, qb, kvh);
-        if (it > 0 && !mbar_wait(q_empty, (it - 1) & 1, s_abort, p.err, kErrTimeoutQ)) break;
-        mbar_arrive_expect_tx(q_full, C::Q_BYTES);
-        for (int c = 0; c < C::NC; ++c) {
-          tma_load_3d(sQ + c * kTileBytes, &tm_qhi, q_full, c * 64, qb * BM, (int)bh);
-          tma_load_3d(sQ + (C::NC + c) * kTileBytes, &tm_qlo, q_full, c * 64, qb * BM, (int)bh);
-        }
         const int nb = qb / 2 + 1;  // 256-key blocks covering the item's causal keys
+        int cur = -1;               // Q plane resident in smem
         for (int pass = 0; pass < p.npass && ok; ++pass) {
           for (int kb = 0; kb < nb && ok; ++kb) {
+            const int plane = q_plane(p, qb, kb);
+            if (plane != cur) {
+              if (qloads > 0 &&
+                  !mbar_wait(q_empty, (qloads - 1) & 1, s_abort, p.err, kErrTimeoutQ)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+              const int z = (int)(plane * p.BH + bh);
+              for (int c = 0; c < C::NC; ++c) {
+                tma_load_3d(sQ + c * kTileBytes, &tm_qhi, q_full, c * 64, qb * BM, z);
+                tma_load_3d(sQ + (C::NC + c) * kTileBytes, &tm_qlo, q_full, c * 64, qb * BM, z);
+              }
+              ++qloads;
+              cur = plane;
+            }
             for (int piece = 0; piece < 2; ++piece, ++kc) {  // hi piece, then lo piece
               const uint32_t s = kc % C::NSTAGE, r = kc / C::NSTAGE;
               if (r > 0 && !mbar_wait(k_empty + s, (r - 1) & 1, s_abort, p.err, kErrTimeoutEmpty)) {
@@ -227,18 +247,29 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
       constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
       const uint32_t q_addr = smem_u32(sQ);
       const uint32_t k_addr = smem_u32(sK);
-      uint32_t kc = 0, ac = 0;
+      uint32_t kc = 0, ac = 0, qloads = 0;
       int it = 0;
       bool ok = true;
       for (int64_t w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
         int64_t bh, kvh;
         int qb;
         decode_item(w, p, bh, qb, kvh);
-        if (!mbar_wait(q_full, it & 1, s_abort, p.err, kErrTimeoutQ)) break;
-        tc_fence_after();
         const int nb = qb / 2 + 1;
+        int cur = -1;
         for (int pass = 0; pass < p.npass && ok; ++pass) {
           for (int kb = 0; kb < nb; ++kb, ++ac) {
+            const int plane = q_plane(p, qb, kb);
+            if (plane != cur) {
+              // the resident Q tile is released once every MMA issued so far has completed
+              if (qloads > 0) umma_commit(q_empty);
+              if (!mbar_wait(q_full, qloads & 1, s_abort, p.err, kErrTimeoutQ)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              ++qloads;
+              cur = plane;
+            }
             const uint32_t slot = ac % NACC, use = ac / NACC;
             if (use > 0 && !mbar_wait(acc_empty + slot, (use - 1) & 1, s_abort, p.err,
                                       kErrTimeoutAcc)) {
@@ -277,7 +308,6 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             umma_commit(acc_full + slot);
           }
         }
-        if (ok) umma_commit(q_empty);
       }
     }
   } else {
@@ -454,8 +484,9 @@ int launch_select(const sta_select_args* a, cudaStream_t stream) {
   const int64_t BH = a->batch * a->n_heads;
   const int64_t BHk = a->batch * a->n_kv_heads;
   CUtensorMap m_qhi, m_qlo, m_khi, m_klo;
-  bool okm = make_tmap_bf16_3d(&m_qhi, a->q_hi, a->d, a->n, BH, 64, BM) &&
-             make_tmap_bf16_3d(&m_qlo, a->q_lo, a->d, a->n, BH, 64, BM) &&
+  const int64_t qplanes = a->dca_chunk_len > 0 ? 3 : 1;  // DCA: intra / previous / older chunk Q
+  bool okm = make_tmap_bf16_3d(&m_qhi, a->q_hi, a->d, a->n, qplanes * BH, 64, BM) &&
+             make_tmap_bf16_3d(&m_qlo, a->q_lo, a->d, a->n, qplanes * BH, 64, BM) &&
              make_tmap_bf16_3d(&m_khi, a->k_hi, a->d, a->n, BHk, 64, BN) &&
              make_tmap_bf16_3d(&m_klo, a->k_lo, a->d, a->n, BHk, 64, BN);
   if (!okm) return fail(STA_ERR_CUDA, "sta_select: cuTensorMapEncodeTiled failed");
@@ -478,6 +509,8 @@ int launch_select(const sta_select_args* a, cudaStream_t stream) {
   p.row_count = a->row_count;
   p.err = device_error_word();
   p.head_stride = tri_head_stride(a->n, a->tile);
+  p.dca_L = a->dca_chunk_len;
+  if (p.dca_L > 0 && (p.dca_L % BN)) return fail(STA_ERR_UNSUPPORTED, "sta_select: DCA chunk_len must be a multiple of 256");
 
   int dev = 0, nsm = 148;
   cudaGetDevice(&dev);

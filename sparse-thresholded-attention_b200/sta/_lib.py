@@ -28,7 +28,8 @@ class SelectArgs(ctypes.Structure):
                 ("batch", c_i64), ("n_heads", c_i64), ("n_kv_heads", c_i64), ("n", c_i64),
                 ("d", c_i32), ("tile", c_i32), ("sm_scale", c_f32), ("wmode", c_i32),
                 ("tau", c_vp), ("max_only", c_i32), ("votes", c_vp), ("wvotes", c_vp),
-                ("bits", c_vp), ("row_max", c_vp), ("row_count", c_vp)]
+                ("bits", c_vp), ("row_max", c_vp), ("row_count", c_vp),
+                ("dca_chunk_len", c_i32)]
 
 
 class BuildArgs(ctypes.Structure):
@@ -99,7 +100,8 @@ class ForwardArgs(ctypes.Structure):
                 ("skipped", c_vp), ("idx_out", c_vp), ("newpos_k_out", c_vp),
                 ("newpos_q_out", c_vp), ("mask_out", c_vp), ("max_workspace_bytes", c_i64),
                 ("stage_events", c_vp), ("same_geometry", c_i32), ("chunk_size", c_i32),
-                ("n_chunk", c_i32), ("chunk_agg", c_i32)]
+                ("n_chunk", c_i32), ("chunk_agg", c_i32), ("dca_chunk_size", c_i32),
+                ("dca_local_window", c_i32)]
 
 
 # every symbol include/sta.h declares (checked by the CPU test suite)
@@ -109,7 +111,7 @@ EXPORTED = ["sta_last_error", "sta_version", "sta_tri_head_stride", "sta_rope_sp
             "sta_pq_union_workspace_bytes", "sta_pq_union_forward",
             "sta_pq_stream_workspace_bytes", "sta_pq_stream_forward", "sta_device_error",
             "sta_shared_forward_static", "sta_build_sets_chunk", "sta_chunk_workspace_bytes",
-            "sta_chunk_forward"]
+            "sta_chunk_forward", "sta_rope_split_dca"]
 
 _lib = None
 
@@ -144,6 +146,9 @@ def lib():
         f = getattr(L, f"sta_{v}_forward")
         f.restype = ctypes.c_int
         f.argtypes = [ctypes.POINTER(ForwardArgs), c_vp, ctypes.c_size_t, c_vp]
+    L.sta_rope_split_dca.restype = ctypes.c_int
+    L.sta_rope_split_dca.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i32, c_i64, c_i64, c_vp, c_f32,
+                                     c_i32, c_i32, c_i32, c_vp, c_vp, c_vp]
     L.sta_shared_forward_static.restype = ctypes.c_int
     L.sta_shared_forward_static.argtypes = [ctypes.POINTER(ForwardArgs), c_vp]
     L.sta_device_error.restype = ctypes.c_int

@@ -43,6 +43,8 @@ class Geometry:
     inv_freq: torch.Tensor
     pos_scale: float = 1.0
     rope_scale: float = 1.0
+    # (chunk_size, local_window): Dual Chunk Attention position ids (selection geometry only)
+    dca: tuple | None = None
 
 
 def _dev_f32(x, device):
@@ -173,6 +175,8 @@ def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=
                 a.mask_out = sets["mask"][b].data_ptr()
         a.max_workspace_bytes = int(max_workspace_bytes)
         a.same_geometry = same_geometry
+        if ga.dca is not None:
+            a.dca_chunk_size, a.dca_local_window = int(ga.dca[0]), int(ga.dca[1])
         if stage_events is not None:
             arr = (ctypes.c_void_p * len(stage_events))(*[e.cuda_event for e in stage_events])
             a.stage_events = ctypes.cast(arr, ctypes.c_void_p)

@@ -234,6 +234,19 @@ def gen_chunk(case, H, N, D, k_max, seed, dtype, select_score="expmass", chunk_s
     save(case, meta, arrays)
 
 
+def gen_dca_tables(case, chunk_size, local_window, pretrain, seq_len, dim=64):
+    """The reference's ChunkLlama rotary tables (dca_kernel.py:176-269) for a small setting."""
+    mod = __import__("dca_kernel")
+    mod._DCA_CHUNK_SIZE, mod._DCA_LOCAL_WINDOW = chunk_size, local_window
+    rot = mod.ChunkLlamaRotaryEmbedding(dim=dim, max_position_embeddings=pretrain, base=10000)
+    rot._set_cos_sin_cache(seq_len=seq_len, device=None, dtype=torch.float32)
+    meta = dict(kind="dca_tables", chunk_size=chunk_size, local_window=local_window,
+                pretrain=pretrain, seq_len=seq_len, dim=dim, mscale=rot._last_mscale)
+    save(case, meta, dict(inv_freq=rot.inv_freq, q_cos=rot.q_cos_cached, q_sin=rot.q_sin_cached,
+                          qc_cos=rot.qc_cos_cached, qc_sin=rot.qc_sin_cached,
+                          k_cos=rot.k_cos_cached, k_sin=rot.k_sin_cached))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -267,6 +280,8 @@ def main():
     gen_pq("pq_union_freq_f32", 2, 256, 64, 4096, 22, f32, select_score="freq")
     gen_pq("pq_union_yarn_f32", 2, 256, 64, 128, 23, f32, geom="yarn")
     # PQ-Stream: max / full advance, skip on/off, ragged N, BN 32 and 64
+    # Dual Chunk Attention position tables (the DCA selection geometry's position rule)
+    gen_dca_tables("dca_tables_s320_w64", 320, 64, 1024, 2048)
     # chunk_exact: chunk-granular selection, exact static budget
     gen_chunk("chunk_expmass_f32", 2, 384, 64, 256, 41, f32)
     gen_chunk("chunk_freq_f32", 2, 320, 64, 192, 42, f32, select_score="freq")

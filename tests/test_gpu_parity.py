@@ -400,3 +400,34 @@ def test_chunk_bf16_gqa_vs_oracle():
     err = np.abs(out[0].float().cpu().numpy() - res[0])
     assert err.mean() <= BF16_MEAN and np.quantile(err, 0.9999) <= BF16_MAX
     assert int(kept.max()) <= 512
+
+
+# ---------------------------------------------------------------------------------------------
+# Dual Chunk Attention selection geometry (hybrid: DCA select, PI attend)
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("D,T,dt", [(64, 64, torch.float32), (128, 64, torch.bfloat16),
+                                    (128, 32, torch.bfloat16)])
+def test_dca_select_and_hybrid_vs_oracle(D, T, dt):
+    H, Hk, N = 4, 2, 1100          # chunk_len 256: every chunk relation, ragged tail
+    s_, w_ = 320, 64
+    q, k, v = make_inputs(SynthSpec(n_heads=H, n_kv_heads=Hk, seq_len=N, head_dim=D, seed=70,
+                                    n_planted=16, dtype=dt))
+    tau = torch.full((H,), 5.0)
+    invf = rope_inv_freq(D, 1e4)
+    ms = oracle.dca_mscale(N, 512)
+    res = hyb.shared_pi_attention(cu(q), cu(k), cu(v), tau, invf, 1.0, ms, invf, 0.5, 1.0,
+                                  tile=T, k_max=512, dca_chunk_size=s_, dca_local_window=w_)
+    G = H // Hk
+    qx, kx, vx = q[0].float().numpy(), np.repeat(k[0].float().numpy(), G, 0), \
+        np.repeat(v[0].float().numpy(), G, 0)
+    o = oracle.shared_attention(qx, kx, vx, tau.numpy(), invf.numpy(), 1.0, ms, invf.numpy(), 0.5,
+                                1.0, tile=T, k_max=512, v_is_bf16=dt == torch.bfloat16,
+                                dca_a=(s_, w_))
+    if o[-1]["select"]["boundary"] == 0:
+        np.testing.assert_array_equal(res[2].cpu().numpy(), o[2])
+        np.testing.assert_array_equal(res[1].cpu().numpy(), o[1])
+    err = np.abs(res[0][0].float().cpu().numpy() - o[0])
+    if dt == torch.float32:
+        assert err.max() <= F32_TOL, err.max()
+    else:
+        assert err.mean() <= BF16_MEAN and np.quantile(err, 0.9999) <= BF16_MAX

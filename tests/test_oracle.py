@@ -205,3 +205,29 @@ def chunk_tiles_without_ties(a, meta, n_chunk, idx):
             assert (ours ^ ref) <= ties
             exact[h, t] = ours == ref
     return exact
+
+
+def test_dca_positions_match_reference_tables():
+    """The DCA selection geometry's positions reproduce the reference's ChunkLlama tables:
+    cos/sin(position * inv_freq) * mscale for keys, same-chunk and previous/older-chunk queries."""
+    meta, a = load(os.path.join(HERE, "golden", "dca_tables_s320_w64.npz"))
+    n = meta["seq_len"]
+    kpos, qi, qs, qo, L = oracle.dca_positions(n, meta["chunk_size"], meta["local_window"])
+    invf = a["inv_freq"].astype(np.float32)
+    ms = np.float32(meta["mscale"])
+
+    def tab(pos):
+        ang = pos.astype(np.float32)[:, None] * invf[None, :]
+        c, s = np.cos(ang).astype(np.float32) * ms, np.sin(ang).astype(np.float32) * ms
+        return np.concatenate([c, c], -1), np.concatenate([s, s], -1)
+
+    kc, ks = tab(kpos)
+    np.testing.assert_allclose(kc, a["k_cos"][:n], atol=2e-6)
+    np.testing.assert_allclose(ks, a["k_sin"][:n], atol=2e-6)
+    qc, qsn = tab(qi[:L])
+    np.testing.assert_allclose(qc, a["q_cos"], atol=2e-6)
+    np.testing.assert_allclose(qsn, a["q_sin"], atol=2e-6)
+    sc, ss = tab(qs[:L])                       # previous-chunk queries (qc table by offset)
+    np.testing.assert_allclose(sc, a["qc_cos"], atol=2e-6)
+    oc, _ = tab(qo[:1])                        # older chunks: the qc table at offset L - 1
+    np.testing.assert_allclose(oc[0], a["qc_cos"][L - 1], atol=2e-6)
