@@ -72,6 +72,15 @@ def workload(args):
         invf, ms = yarn_inv_freq(D, c["theta"], c["yarn_factor"], c["yarn_orig"])
         geo = dict(inv_freq=invf, pos_scale=1.0, rope_scale=ms)
         geo_c = dict(geo)
+    elif c["geom"] == "hybrid":
+        # selection: Dual Chunk Attention positions (ChunkLlama rule, s < c as the reference
+        # asserts: s = 6144, w = 1024, c = 8192 -> chunk_len 5120) with its mscale
+        # 0.05 ln(S / c) + 1; attend: PI with base RoPE at pos_scale 0.5
+        invf = rope_inv_freq(D, c["theta"])
+        ms = 0.05 * math.log(c["S"] / c["dca_pretrain"]) + 1.0 if c["S"] > c["dca_pretrain"] else 1.0
+        geo = dict(inv_freq=invf, pos_scale=1.0, rope_scale=ms,
+                   dca=(c["dca_chunk_size"], c["dca_local_window"]))
+        geo_c = dict(inv_freq=invf, pos_scale=c["pos_scale_c"], rope_scale=1.0)
     else:
         invf = rope_inv_freq(D, c["theta"])
         geo = dict(inv_freq=invf, pos_scale=c.get("pos_scale", 1.0), rope_scale=1.0)
@@ -94,7 +103,7 @@ def workload_desc(c, args, world):
 # ---------------------------------------------------------------------------------------------
 # CPU baseline: the oracle restatement of the reference algorithm on a bounded sample
 # ---------------------------------------------------------------------------------------------
-def cpu_sample(q, k, v, tau, geo, c, n_tiles=12, head=0, seed=0):
+def cpu_sample(q, k, v, tau, geo, c, n_tiles=12, head=0, seed=0, geo_c=None):
     """Run the reference algorithm (oracle port) on `n_tiles` query tiles of one q head and
     extrapolate to the whole layer by causal work (cost of a tile ~ its key count).
     Returns (tokens/s estimate, seconds spent, description)."""
@@ -108,20 +117,21 @@ def cpu_sample(q, k, v, tau, geo, c, n_tiles=12, head=0, seed=0):
     qh = q[0, head:head + 1].float().numpy()
     kh = k[0, kv:kv + 1].float().numpy()
     vh = v[0, kv:kv + 1].float().numpy()
+    geo_c = geo_c or geo
     invf = geo["inv_freq"].numpy()
     sm = 1.0 / math.sqrt(D)
     t0 = time.perf_counter()
     sel = oracle.select_vote(qh, kh, tau[head:head + 1].numpy(), invf, geo["pos_scale"],
-                             geo["rope_scale"], sm, T, tiles=tiles)
+                             geo["rope_scale"], sm, T, tiles=tiles, dca=geo.get("dca"))
     idx = np.full((1, nt, c["k_max"]), N, np.int32)
     npk = np.zeros((1, nt, c["k_max"]), np.float32)
     npq = np.zeros((1, nt, T), np.float32)
     for t in tiles:
-        s = oracle.build_sets(sel["votes"][:, t:t + 1], geo["pos_scale"], 32, 32, c["pct"], T,
+        s = oracle.build_sets(sel["votes"][:, t:t + 1], geo_c["pos_scale"], 32, 32, c["pct"], T,
                               c["k_max"], q_pos_base=t * T)
         idx[:, t], npk[:, t], npq[:, t] = s[0][:, 0], s[1][:, 0], s[2][:, 0]
-    oracle.gather_attn(qh, kh, vh, invf, idx, npk, npq, sm, geo["rope_scale"], T,
-                       v_is_bf16=True, tiles=tiles)
+    oracle.gather_attn(qh, kh, vh, geo_c["inv_freq"].numpy(), idx, npk, npq, sm,
+                       geo_c["rope_scale"], T, v_is_bf16=True, tiles=tiles)
     dt = time.perf_counter() - t0
     work_sample = sum(min((t + 1) * T, N) for t in tiles)
     work_total = H * c["B"] * sum(min((t + 1) * T, N) for t in range(nt))
@@ -142,12 +152,12 @@ def run_reference(args):
     q, k, v, tau, geo, geo_c, c = workload(args)
     world = args.gpus
     for i in range(args.warmup):
-        cpu_sample(q, k, v, tau, geo, c, n_tiles=2, seed=100 + i)
+        cpu_sample(q, k, v, tau, geo, c, n_tiles=2, seed=100 + i, geo_c=geo_c)
     vals, secs = [], 0.0
     t0 = time.perf_counter()
     desc = ""
     for i in range(args.steps):
-        tok, dt, desc = cpu_sample(q, k, v, tau, geo, c, n_tiles=48, seed=i)
+        tok, dt, desc = cpu_sample(q, k, v, tau, geo, c, n_tiles=48, seed=i, geo_c=geo_c)
         vals.append(tok)
         secs += dt
     value = statistics.median(vals)
@@ -243,7 +253,7 @@ def run_gpu(args):
     vs = v[:, k0:k1].contiguous()
     taus = tau[k0 * G:k1 * G]
     qd, kd, vd = qs.to(dev), ks.to(dev), vs.to(dev)
-    ga = Geometry(geo["inv_freq"], geo["pos_scale"], geo["rope_scale"])
+    ga = Geometry(geo["inv_freq"], geo["pos_scale"], geo["rope_scale"], geo.get("dca"))
     gc = Geometry(geo_c["inv_freq"], geo_c["pos_scale"], geo_c["rope_scale"])
     T = c["T"] if args.variant == "shared" else 32
     kw = dict(tile=T, k_max=c["k_max"], pct=c.get("pct", 30.0), select_score="freq",
@@ -277,10 +287,11 @@ def run_gpu(args):
         torch.cuda.synchronize()
         barrier()
     ms_total = start.elapsed_time(end)
+    # the op runs once per batch element and the events bracket the last one: scale by B
     stage_ms = [0.0] * 4
     for row in evs:
         for j in range(4):
-            stage_ms[j] += row[j].elapsed_time(row[j + 1]) / K
+            stage_ms[j] += B * row[j].elapsed_time(row[j + 1]) / K
     t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -337,7 +348,7 @@ def run_gpu(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import torch as _t
         _t.set_num_threads(os.cpu_count() or 1)
-        tok_cpu, _, desc = cpu_sample(q, k, v, tau, geo, c, n_tiles=240)
+        tok_cpu, _, desc = cpu_sample(q, k, v, tau, geo, c, n_tiles=240, geo_c=geo_c)
         cpu = {"value": tok_cpu, "unit": "tokens/s", "cores": os.cpu_count() or 1,
                "kind": "port", "sample": desc}
     stats = {}

@@ -136,6 +136,7 @@ def config(idx: int) -> dict:
     if idx == 3:
         return dict(name="cfg3-hybrid-dca-64k", B=2, H=32, Hkv=8, S=65536, D=128, dtype="bf16",
                     T=64, planted=1024, seed=3, theta=5e5, geom="hybrid", pos_scale_c=0.5,
+                    dca_chunk_size=6144, dca_local_window=1024, dca_pretrain=8192,
                     tau=5.0, pct=30.0, k_max=2048)
     if idx == 4:
         return dict(name="cfg4-pq-128k", B=1, H=32, Hkv=8, S=131072, D=128, dtype="bf16", T=32,
