@@ -71,6 +71,11 @@ int sta_rope_split_dca(const void* x, int32_t dtype, int64_t heads, int64_t n, i
                        int32_t chunk_size, int32_t local_window, int32_t role, void* out_hi,
                        void* out_lo, void* stream);
 
+/* cos/sin table of a RoPE geometry: out[i * d/2 + f] = (cos(a) * rope_scale, sin(a) * rope_scale)
+ * with a = fl(fl(i / R) * inv_freq[f]) (float2 pairs, len * d/2 entries; R a power of two). */
+int sta_rope_table(const float* inv_freq, int32_t d, float rope_scale, float R, int64_t len,
+                   void* out, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Stage 1 -- exact-max two-pass selection on tcgen05 tensor cores (Kernel A).
  * Replaces _select_vote_kernel (shared_selection_triton_exact_2.py:50-140) and
@@ -226,6 +231,12 @@ typedef struct sta_attend_args {
   const void* q_hi; const void* q_lo; const void* k_hi; const void* k_lo;
   float pos_scale_sel;
   int32_t same_geometry;
+  /* optional cos/sin table of the attend geometry (sta_rope_table): positions i / R for
+   * 0 <= i < rope_table_len, (cos, sin) * rope_scale pairs; a slot whose position lies on it
+   * reads the table instead of evaluating sincos (bit-identical) */
+  const void* rope_table;
+  float rope_table_R;
+  int64_t rope_table_len;
 } sta_attend_args;
 
 int sta_gather_attend(const sta_attend_args* a, void* stream);

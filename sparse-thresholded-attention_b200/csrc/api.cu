@@ -92,7 +92,9 @@ inline size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
   int64_t c;          // kv heads per group
-  size_t qh, ql, kh, kl, votes, wvotes, bits, idx, npk, npq, mask, rowmax, total;
+  size_t qh, ql, kh, kl, votes, wvotes, bits, idx, npk, npq, mask, rowmax, rtab, total;
+  float rtab_R;
+  int64_t rtab_len;
 };
 
 int64_t esize(int dt) { return dt == STA_DTYPE_F32 ? 4 : 2; }
@@ -128,6 +130,21 @@ Layout layout_for(const sta_forward_args* a, Variant v, int64_t c) {
     L.npq = take(qh * nt * T * 4);
     if (v == kPQUnion) L.mask = take(qh * nt * (int64_t)a->k_max * 4);
   }
+  // cos/sin table of the attend geometry: integer dense ranks (PQ-Union, chunk) or PI positions
+  // at a power-of-two fraction (shared path with pos_scale_c in {1, 1/2, 1/4})
+  L.rtab_R = 0.f;
+  L.rtab_len = 0;
+  if (v == kPQUnion || v == kChunk) {
+    L.rtab_R = 1.f;
+    L.rtab_len = (int64_t)a->k_max + 1;
+  } else if (v == kShared) {
+    for (int r = 1; r <= 4; r *= 2)
+      if (a->pos_scale_c * (float)r == 1.f) {
+        L.rtab_R = (float)r;
+        L.rtab_len = N * r + 1;
+      }
+  }
+  if (L.rtab_len > 0) L.rtab = take((size_t)L.rtab_len * (D / 2) * 8);
   L.total = o;
   return L;
 }
@@ -202,6 +219,9 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
   const int64_t nt = (N + T - 1) / T;
   const int64_t es = esize(a->dtype);
   const int64_t kmax = a->k_max;
+  if (L.rtab_len > 0)
+    STA_TRY(launch_rope_table(a->inv_freq_c, a->d, v == kShared ? a->rope_scale_c : 1.0f,
+                              L.rtab_R, L.rtab_len, w + L.rtab, st));
   for (int64_t b = 0; b < a->batch; ++b) {
     for (int64_t g0 = 0; g0 < Hk; g0 += c) {
       const int64_t h0 = b * H + g0 * G;   // first q head (flattened over batch)
@@ -393,6 +413,9 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       ca.k_lo = w + L.kl;
       ca.pos_scale_sel = a->pos_scale_a;
       ca.same_geometry = (v == kShared && a->same_geometry && !dca) ? 1 : 0;
+      ca.rope_table = L.rtab_len > 0 ? w + L.rtab : nullptr;
+      ca.rope_table_R = L.rtab_R;
+      ca.rope_table_len = L.rtab_len;
       STA_TRY(launch_gather_attend(&ca, st));
       mark(4);
     }
@@ -440,6 +463,14 @@ int sta_rope_split_dca(const void* x, int32_t dtype, int64_t heads, int64_t n, i
   return launch_rope_split(x, dtype, heads, n, d, stride_h, stride_n, inv_freq, 1.0f, rope_scale,
                            out_hi, out_lo, static_cast<cudaStream_t>(stream), role,
                            (int64_t)chunk_size - local_window, chunk_size);
+}
+
+int sta_rope_table(const float* inv_freq, int32_t d, float rope_scale, float R, int64_t len,
+                   void* out, void* stream) {
+  if (!inv_freq || !out) return fail(STA_ERR_ARG, "sta_rope_table: null pointer");
+  if (d <= 0 || (d & 1) || !(R == 1.f || R == 2.f || R == 4.f))
+    return fail(STA_ERR_ARG, "sta_rope_table: d even, R in {1, 2, 4}");
+  return launch_rope_table(inv_freq, d, rope_scale, R, len, out, static_cast<cudaStream_t>(stream));
 }
 
 int sta_select(const sta_select_args* a, void* stream) {

@@ -42,6 +42,9 @@ struct AttendP {
   const __nv_bfloat16 *qh, *ql, *kh, *kl;  // pre-rotated selection-geometry rows (or null)
   float ps_sel;
   int direct;                             // reuse pre-rotated rows where bit-identical
+  const float2* rtab;                     // (cos, sin) * rope_scale at positions i / rtab_R
+  float rtab_R;
+  int64_t rtab_len;
 };
 
 // 8 consecutive elements as fp32
@@ -63,10 +66,21 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&x)[8]) {
 
 // Rotate 8 frequency pairs (f0..f0+7 with partners f0+HALF..) of one row and store the NP-piece
 // split into a padded smem row set (plane stride `plane`, row pointer `dst`).
+// Position `pos` as an index of the cos/sin table (entries at i / R), or -1 when the table does
+// not hold it.  Entries are formed from the exact float i / R with the same fp32 expression as
+// the direct path, so a hit is bit-identical to recomputing.
+__device__ __forceinline__ int64_t table_index(float pos, float R, int64_t len) {
+  if (len <= 0) return -1;
+  const float fi = pos * R;  // exact: R is a power of two
+  if (!(fi >= 0.f) || fi != floorf(fi) || fi >= (float)len) return -1;
+  return (int64_t)fi;
+}
+
 template <int NP, int HALF, typename TV>
 __device__ __forceinline__ void rotate8(const TV* src, bool valid, int f0, float pos,
                                         const float* inv_freq, float rope_scale,
-                                        __nv_bfloat16* dst, int plane) {
+                                        __nv_bfloat16* dst, int plane,
+                                        const float2* tab = nullptr, int64_t ti = -1) {
   float x1[8], x2[8];
   if (valid) {
     load8(src + f0, x1);
@@ -77,9 +91,15 @@ __device__ __forceinline__ void rotate8(const TV* src, bool valid, int f0, float
   }
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
-    const float ang = __fmul_rn(pos, __ldg(inv_freq + f0 + u));
     float r1, r2;
-    rope_pair(x1[u], x2[u], ang, rope_scale, r1, r2);
+    if (ti >= 0) {
+      const float2 cs = __ldg(tab + ti * HALF + f0 + u);
+      r1 = __fsub_rn(__fmul_rn(x1[u], cs.x), __fmul_rn(x2[u], cs.y));
+      r2 = __fadd_rn(__fmul_rn(x2[u], cs.x), __fmul_rn(x1[u], cs.y));
+    } else {
+      const float ang = __fmul_rn(pos, __ldg(inv_freq + f0 + u));
+      rope_pair(x1[u], x2[u], ang, rope_scale, r1, r2);
+    }
     __nv_bfloat16 a[NP], b[NP];
     split_pieces<NP>(r1, a);
     split_pieces<NP>(r2, b);
@@ -156,7 +176,8 @@ gather_attend_kernel(const AttendP p) {
     if (direct && qp < N && pos == __fmul_rn((float)qp, p.ps_sel)) {
       copy_rotated<HALF>(p.qh + (bh * N + qp) * D, p.ql + (bh * N + qp) * D, f0, dst, T * LD);
     } else {
-      rotate8<NQ, HALF>(qg + qp * p.qsn, qp < N, f0, pos, p.inv_freq, p.rope_scale, dst, T * LD);
+      rotate8<NQ, HALF>(qg + qp * p.qsn, qp < N, f0, pos, p.inv_freq, p.rope_scale, dst, T * LD,
+                        p.rtab, table_index(pos, p.rtab_R, p.rtab_len));
     }
   }
 
@@ -199,7 +220,7 @@ gather_attend_kernel(const AttendP p) {
         copy_rotated<HALF>(p.kh + (kvh * N + id) * D, p.kl + (kvh * N + id) * D, f0, dst, BK * LD);
       } else {
         rotate8<NQ, HALF>(kg + (int64_t)(id < N ? id : 0) * p.ksn, id < N, f0, pos, p.inv_freq,
-                          p.rope_scale, dst, BK * LD);
+                          p.rope_scale, dst, BK * LD, p.rtab, table_index(pos, p.rtab_R, p.rtab_len));
       }
     }
     for (int it = tid; it < BK * (D / 8); it += NTH) {
@@ -421,6 +442,9 @@ int launch_gather_attend(const sta_attend_args* a, cudaStream_t stream) {
   p.kl = static_cast<const __nv_bfloat16*>(a->k_lo);
   p.ps_sel = a->pos_scale_sel;
   p.direct = a->same_geometry && a->q_hi && a->q_lo && a->k_hi && a->k_lo;
+  p.rtab = static_cast<const float2*>(a->rope_table);
+  p.rtab_R = a->rope_table_R;
+  p.rtab_len = a->rope_table ? a->rope_table_len : 0;
   if (p.BH > 65535) return fail(STA_ERR_UNSUPPORTED, "sta_gather_attend: too many heads");
   const bool f32 = a->dtype == STA_DTYPE_F32;
   if (a->d == 128) {

@@ -89,4 +89,30 @@ int launch_rope_split(const void* x, int dtype, int64_t heads, int64_t N, int D,
   return cudaGetLastError() == cudaSuccess ? 0 : STA_ERR_CUDA;
 }
 
+// (cos, sin) * rope_scale at positions i / R, formed exactly like the direct RoPE path
+__global__ void rope_table_kernel(const float* __restrict__ inv_freq, int half, float rope_scale,
+                                  float R, int64_t len, float2* __restrict__ out) {
+  const int64_t total = len * half;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int f = (int)(i % half);
+    const float pos = (float)(i / half) / R;
+    const float ang = __fmul_rn(pos, __ldg(inv_freq + f));
+    float s, c;
+    sincosf(ang, &s, &c);
+    out[i] = make_float2(__fmul_rn(c, rope_scale), __fmul_rn(s, rope_scale));
+  }
+}
+
+int launch_rope_table(const float* inv_freq, int D, float rope_scale, float R, int64_t len,
+                      void* out, cudaStream_t stream) {
+  const int64_t total = len * (D / 2);
+  if (total <= 0) return 0;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  rope_table_kernel<<<(unsigned)blocks, 256, 0, stream>>>(inv_freq, D / 2, rope_scale, R, len,
+                                                          static_cast<float2*>(out));
+  return cudaGetLastError() == cudaSuccess ? 0 : STA_ERR_CUDA;
+}
+
 }  // namespace sta

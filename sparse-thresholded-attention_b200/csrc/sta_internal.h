@@ -22,6 +22,8 @@ int launch_rope_split(const void* x, int dtype, int64_t heads, int64_t N, int D,
                       cudaStream_t stream, int mode = 0, int64_t dca_L = 0, int64_t dca_s = 0);
 
 int launch_select(const sta_select_args* a, cudaStream_t stream);
+int launch_rope_table(const float* inv_freq, int D, float rope_scale, float R, int64_t len,
+                      void* out, cudaStream_t stream);
 int launch_build_sets(const sta_build_args* a, cudaStream_t stream);
 int launch_build_sets_pq(const sta_build_pq_args* a, cudaStream_t stream);
 int launch_build_sets_chunk(const sta_build_chunk_args* a, cudaStream_t stream);

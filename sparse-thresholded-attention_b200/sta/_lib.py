@@ -67,7 +67,8 @@ class AttendArgs(ctypes.Structure):
                 ("mask", c_vp), ("kept_size", c_vp), ("inv_freq", c_vp),
                 ("rope_scale", c_f32), ("sm_scale", c_f32), ("q_hi", c_vp), ("q_lo", c_vp),
                 ("k_hi", c_vp), ("k_lo", c_vp), ("pos_scale_sel", c_f32),
-                ("same_geometry", c_i32)]
+                ("same_geometry", c_i32), ("rope_table", c_vp), ("rope_table_R", c_f32),
+                ("rope_table_len", c_i64)]
 
 
 class PQStreamArgs(ctypes.Structure):
@@ -111,7 +112,7 @@ EXPORTED = ["sta_last_error", "sta_version", "sta_tri_head_stride", "sta_rope_sp
             "sta_pq_union_workspace_bytes", "sta_pq_union_forward",
             "sta_pq_stream_workspace_bytes", "sta_pq_stream_forward", "sta_device_error",
             "sta_shared_forward_static", "sta_build_sets_chunk", "sta_chunk_workspace_bytes",
-            "sta_chunk_forward", "sta_rope_split_dca"]
+            "sta_chunk_forward", "sta_rope_split_dca", "sta_rope_table"]
 
 _lib = None
 
@@ -149,6 +150,8 @@ def lib():
     L.sta_rope_split_dca.restype = ctypes.c_int
     L.sta_rope_split_dca.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i32, c_i64, c_i64, c_vp, c_f32,
                                      c_i32, c_i32, c_i32, c_vp, c_vp, c_vp]
+    L.sta_rope_table.restype = ctypes.c_int
+    L.sta_rope_table.argtypes = [c_vp, c_i32, c_f32, c_f32, c_i64, c_vp, c_vp]
     L.sta_shared_forward_static.restype = ctypes.c_int
     L.sta_shared_forward_static.argtypes = [ctypes.POINTER(ForwardArgs), c_vp]
     L.sta_device_error.restype = ctypes.c_int

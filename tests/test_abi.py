@@ -37,7 +37,7 @@ def test_struct_layouts_match_header_order():
                        ("sta_pqstream_args", L.PQStreamArgs), ("sta_forward_args", L.ForwardArgs)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), src, re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
-        fields = re.findall(r"\**\s*([a-z_0-9]+)\s*;", body)
+        fields = re.findall(r"\**\s*([A-Za-z_0-9]+)\s*;", body)
         assert [f for f, _ in cls._fields_] == fields, cname
 
 
