@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--heads", type=int, default=None, help="override q heads (profiling only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--max-workspace-gb", type=int, default=48,
+                    help="scratch cap; larger problems run over groups of kv heads")
     return ap.parse_args()
 
 
@@ -256,8 +258,9 @@ def run_gpu(args):
     ga = Geometry(geo["inv_freq"], geo["pos_scale"], geo["rope_scale"], geo.get("dca"))
     gc = Geometry(geo_c["inv_freq"], geo_c["pos_scale"], geo_c["rope_scale"])
     T = c["T"] if args.variant == "shared" else 32
-    kw = dict(tile=T, k_max=c["k_max"], pct=c.get("pct", 30.0), select_score="freq",
-              block_n=32)
+    kw = dict(tile=T, k_max=c["k_max"], pct=c.get("pct", 30.0),
+              select_score="freq" if args.variant == "shared" else "expmass", block_n=32,
+              max_workspace_bytes=args.max_workspace_gb << 30)
 
     def step(qq, kk, vv, evs=None):
         return core.forward(args.variant, qq, kk, vv, taus, ga, gc, stage_events=evs, **kw)

@@ -72,7 +72,7 @@ int sta_rope_split_dca(const void* x, int32_t dtype, int64_t heads, int64_t n, i
                        void* out_lo, void* stream);
 
 /* cos/sin table of a RoPE geometry: out[i * d/2 + f] = (cos(a) * rope_scale, sin(a) * rope_scale)
- * with a = fl(fl(i / R) * inv_freq[f]) (float2 pairs, len * d/2 entries; R a power of two). */
+ * with a = fl(fl(i / R) * inv_freq[f]) (float2 pairs, len * d/2 entries; R in {1, 2, 4, -1}). */
 int sta_rope_table(const float* inv_freq, int32_t d, float rope_scale, float R, int64_t len,
                    void* out, void* stream);
 
@@ -268,6 +268,10 @@ typedef struct sta_pqstream_args {
   float sm_scale;
   int32_t pos_advance;     /* STA_ADV_* */
   int32_t use_skip;
+  /* optional cos/sin table of the attend geometry at positions -i (sta_rope_table, R = -1) */
+  const void* rope_table;
+  float rope_table_R;
+  int64_t rope_table_len;
   float* span;             /* (heads, nt) */
   int32_t* kept;           /* (heads, n) */
   float* blocks;           /* (heads, nt) */

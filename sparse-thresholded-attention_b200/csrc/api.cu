@@ -137,6 +137,9 @@ Layout layout_for(const sta_forward_args* a, Variant v, int64_t c) {
   if (v == kPQUnion || v == kChunk) {
     L.rtab_R = 1.f;
     L.rtab_len = (int64_t)a->k_max + 1;
+  } else if (v == kPQStream) {
+    L.rtab_R = -1.f;  // streamed positions -(d + o) are non-positive integers, |.| <= N
+    L.rtab_len = N + 1;
   } else if (v == kShared) {
     for (int r = 1; r <= 4; r *= 2)
       if (a->pos_scale_c * (float)r == 1.f) {
@@ -298,6 +301,9 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
         pa.sm_scale = a->sm_scale;
         pa.pos_advance = a->pos_advance;
         pa.use_skip = a->use_skip;
+        pa.rope_table = L.rtab_len > 0 ? w + L.rtab : nullptr;
+        pa.rope_table_R = L.rtab_R;
+        pa.rope_table_len = L.rtab_len;
         pa.span = a->span + h0 * nt;
         pa.kept = a->kept_rows + h0 * N;
         pa.blocks = a->blocks + h0 * nt;
@@ -468,8 +474,8 @@ int sta_rope_split_dca(const void* x, int32_t dtype, int64_t heads, int64_t n, i
 int sta_rope_table(const float* inv_freq, int32_t d, float rope_scale, float R, int64_t len,
                    void* out, void* stream) {
   if (!inv_freq || !out) return fail(STA_ERR_ARG, "sta_rope_table: null pointer");
-  if (d <= 0 || (d & 1) || !(R == 1.f || R == 2.f || R == 4.f))
-    return fail(STA_ERR_ARG, "sta_rope_table: d even, R in {1, 2, 4}");
+  if (d <= 0 || (d & 1) || !(R == 1.f || R == 2.f || R == 4.f || R == -1.f))
+    return fail(STA_ERR_ARG, "sta_rope_table: d even, R in {1, 2, 4, -1}");
   return launch_rope_table(inv_freq, d, rope_scale, R, len, out, static_cast<cudaStream_t>(stream));
 }
 

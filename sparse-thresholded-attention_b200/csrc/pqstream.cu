@@ -13,6 +13,7 @@
 // Outputs: out, span (= final d), kept (per-query kept count), blocks, skipped.
 #include "common.cuh"
 #include "mma_frag.cuh"
+#include "gather_rope.cuh"
 #include "sta_internal.h"
 
 namespace sta {
@@ -40,6 +41,9 @@ struct PQSP {
   const float* inv_freq_c;
   float sm_scale;
   int adv_full, use_skip;
+  const float2* rtab;
+  float rtab_R;
+  int64_t rtab_len;
   float* span;
   int32_t* kept;
   float* blocks;
@@ -139,9 +143,16 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
       x2 = ldv(qg + qp * p.qsn + f + HALF);
     }
     const float npq = (float)(qp - P_top);
-    const float ang = __fmul_rn(npq, __ldg(p.inv_freq_c + f));
     float r1, r2;
-    rope_pair(x1, x2, ang, 1.f, r1, r2);
+    const int64_t ti = table_index(npq, p.rtab_R, p.rtab_len);
+    if (ti >= 0) {
+      const float2 cs = __ldg(p.rtab + ti * HALF + f);
+      r1 = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+      r2 = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
+    } else {
+      const float ang = __fmul_rn(npq, __ldg(p.inv_freq_c + f));
+      rope_pair(x1, x2, ang, 1.f, r1, r2);
+    }
     __nv_bfloat16 a[NQ], b[NQ];
     split_pieces<NQ>(r1, a);
     split_pieces<NQ>(r2, b);
@@ -170,40 +181,17 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
     const int64_t sn = (int64_t)(nblk - 1 - tb) * BN;
     const int64_t hi_t = min(P_top, sn + BN - 1);
     __syncthreads();
-    // load the block: select-geometry K (hi/lo), raw K rotated at the streamed positions, V
-    for (int it = tid; it < BN * D; it += NTH) {
-      const int i = it / D, d = it % D;
+    // phase 1: selection-geometry K (hi/lo) of the block
+    for (int it = tid; it < BN * (D / 8); it += NTH) {
+      const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
       const int64_t j = sn + i;
-      __nv_bfloat16 zh = __float2bfloat16_rn(0.f);
-      sKs[i * LD + d] = j < N ? khg[j * D + d] : zh;
-      sKs[(BN + i) * LD + d] = j < N ? klg[j * D + d] : zh;
-      const float x = j < N ? ldv(vg + j * p.vsn + d) : 0.f;
-      __nv_bfloat16 pv[NV];
-      split_pieces<NV>(x, pv);
-#pragma unroll
-      for (int q2 = 0; q2 < NV; ++q2) sV[(q2 * BN + i) * LD + d] = pv[q2];
-    }
-    for (int it = tid; it < BN * HALF; it += NTH) {
-      const int i = it / HALF, f = it % HALF;
-      const int64_t j = sn + i;
-      float x1 = 0.f, x2 = 0.f;
+      uint4 h = make_uint4(0u, 0u, 0u, 0u), l = h;
       if (j < N) {
-        x1 = ldv(kg + j * p.ksn + f);
-        x2 = ldv(kg + j * p.ksn + f + HALF);
+        h = *reinterpret_cast<const uint4*>(khg + j * D + d0);
+        l = *reinterpret_cast<const uint4*>(klg + j * D + d0);
       }
-      const float o_j = (float)(hi_t - j);
-      const float npk = -__fadd_rn(dpos, o_j);
-      const float ang = __fmul_rn(npk, __ldg(p.inv_freq_c + f));
-      float r1, r2;
-      rope_pair(x1, x2, ang, 1.f, r1, r2);
-      __nv_bfloat16 a[NQ], b[NQ];
-      split_pieces<NQ>(r1, a);
-      split_pieces<NQ>(r2, b);
-#pragma unroll
-      for (int q2 = 0; q2 < NQ; ++q2) {
-        sKa[(q2 * BN + i) * LD + f] = a[q2];
-        sKa[(q2 * BN + i) * LD + f + HALF] = b[q2];
-      }
+      *reinterpret_cast<uint4*>(sKs + i * LD + d0) = h;
+      *reinterpret_cast<uint4*>(sKs + (BN + i) * LD + d0) = l;
     }
     __syncthreads();
 
@@ -246,6 +234,41 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
     for (int w = 0; w < NW; ++w) cmax = max(cmax, s_cmax[w]);
     const float adv = p.adv_full ? (float)(hi_t - sn + 1) : (float)cmax;
     if (p.use_skip && !(adv > 0.f)) continue;
+
+    // phase 2 (used blocks only): raw K rotated at the streamed positions, and V
+    for (int it = tid; it < BN * (HALF / 8); it += NTH) {
+      const int i = it / (HALF / 8), f0 = (it % (HALF / 8)) * 8;
+      const int64_t j = sn + i;
+      const float npk = -__fadd_rn(dpos, (float)(hi_t - j));
+      rotate8<NQ, HALF>(kg + (j < N ? j : 0) * p.ksn, j < N, f0, npk, p.inv_freq_c, 1.f,
+                        sKa + i * LD, BN * LD, p.rtab, table_index(npk, p.rtab_R, p.rtab_len));
+    }
+    for (int it = tid; it < BN * (D / 8); it += NTH) {
+      const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
+      const int64_t j = sn + i;
+      __nv_bfloat16* dst = sV + i * LD + d0;
+      if (!F32) {
+        uint4 u = make_uint4(0u, 0u, 0u, 0u);
+        if (j < N) u = *reinterpret_cast<const uint4*>(vg + j * p.vsn + d0);
+        *reinterpret_cast<uint4*>(dst) = u;
+      } else {
+        float x[8];
+        if (j < N) {
+          load8(vg + j * p.vsn + d0, x);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) x[u] = 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          __nv_bfloat16 pc[NV];
+          split_pieces<NV>(x[u], pc);
+#pragma unroll
+          for (int q2 = 0; q2 < NV; ++q2) dst[q2 * BN * LD + u] = pc[q2];
+        }
+      }
+    }
+    __syncthreads();
 
     // attend scores at the streamed positions
     score_tile<D, BN, NQ>(sQa, sKa, s);
@@ -390,6 +413,16 @@ int launch_pqstream(const sta_pqstream_args* a, cudaStream_t stream) {
   if (a->n_heads <= 0 || a->n_kv_heads <= 0 || a->n_heads % a->n_kv_heads)
     return fail(STA_ERR_ARG, "sta_pqstream_attend: bad head counts");
   if (a->n <= 0 || a->batch <= 0) return STA_OK;
+  {
+    const int64_t es = a->dtype == STA_DTYPE_F32 ? 4 : 2;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->k) |
+                         reinterpret_cast<uintptr_t>(a->v);
+    const int64_t st = (a->q_stride_h | a->q_stride_n | a->k_stride_h | a->k_stride_n |
+                        a->v_stride_h | a->v_stride_n) * es;
+    if ((al & 15u) || (st & 15))
+      return fail(STA_ERR_UNSUPPORTED,
+                  "sta_pqstream_attend: q/k/v rows must start on 16-byte boundaries");
+  }
   PQSP p;
   p.q = a->q; p.qsh = a->q_stride_h; p.qsn = a->q_stride_n;
   p.k = a->k; p.ksh = a->k_stride_h; p.ksn = a->k_stride_n;
@@ -412,6 +445,9 @@ int launch_pqstream(const sta_pqstream_args* a, cudaStream_t stream) {
   p.sm_scale = a->sm_scale;
   p.adv_full = a->pos_advance == STA_ADV_FULL;
   p.use_skip = a->use_skip;
+  p.rtab = static_cast<const float2*>(a->rope_table);
+  p.rtab_R = a->rope_table_R;
+  p.rtab_len = a->rope_table ? a->rope_table_len : 0;
   p.span = a->span;
   p.kept = a->kept;
   p.blocks = a->blocks;

@@ -80,7 +80,8 @@ class PQStreamArgs(ctypes.Structure):
                 ("block_n", c_i32), ("q_hi", c_vp), ("q_lo", c_vp), ("k_hi", c_vp),
                 ("k_lo", c_vp), ("row_max", c_vp), ("tau", c_vp), ("n_global", c_i32),
                 ("n_local", c_i32), ("inv_freq_c", c_vp), ("sm_scale", c_f32),
-                ("pos_advance", c_i32), ("use_skip", c_i32), ("span", c_vp), ("kept", c_vp),
+                ("pos_advance", c_i32), ("use_skip", c_i32), ("rope_table", c_vp),
+                ("rope_table_R", c_f32), ("rope_table_len", c_i64), ("span", c_vp), ("kept", c_vp),
                 ("blocks", c_vp), ("skipped", c_vp)]
 
 
