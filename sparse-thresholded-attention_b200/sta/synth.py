@@ -38,8 +38,11 @@ class SynthSpec:
     cosine: float = 0.8
     seed: int = 0
     dtype: torch.dtype = torch.float32
-    # optional "dense cluster": scale the queries of these (batch, tile_start, tile_len) ranges
-    # towards zero so that they keep almost every causal key (drives the 30->25->20% fallback)
+    # optional "dense clusters": scale the queries of these ranges towards zero so that they keep
+    # many causal keys (drives the 30->25->20% fallback).  Entries are (batch, start, length)
+    # -- every row scaled by ``flat_scale``, so all rows keep nearly every causal key and the
+    # votes tie -- or (batch, start, length, lo, hi): row r scaled by the geometric ramp
+    # lo * (hi/lo)^(r/(length-1)), which grades the votes so a 25% or 20% pick can fit k_max
     flat_query_ranges: list = field(default_factory=list)
     flat_scale: float = 0.02
 
@@ -85,8 +88,15 @@ def make_inputs(spec: SynthSpec):
                     qn = q[b, h, later].norm(dim=-1, keepdim=True)
                     q[b, h, later] = qn * (spec.cosine * u[None, :]
                                            + math.sqrt(1.0 - spec.cosine ** 2) * w)
-    for (b, start, length) in spec.flat_query_ranges:
-        q[b, :, start:start + length] *= spec.flat_scale
+    for rng in spec.flat_query_ranges:
+        b, start, length = rng[:3]
+        if len(rng) == 3:
+            q[b, :, start:start + length] *= spec.flat_scale
+        else:
+            lo, hi = float(rng[3]), float(rng[4])
+            r = torch.arange(length, dtype=torch.float32) / max(length - 1, 1)
+            ramp = lo * (hi / lo) ** r
+            q[b, :, start:start + length] *= ramp[None, :, None]
     return q.to(spec.dtype), k.to(spec.dtype), v.to(spec.dtype)
 
 
@@ -157,8 +167,12 @@ def make_config_inputs(idx: int, seq_len: int | None = None, n_heads: int | None
     planted = max(1, c["planted"] * S // c["S"])
     flat = []
     if idx == 2 and S >= 8192:
-        # one dense cluster deep in the sequence, to exercise the 30->25->20% fallback
-        flat = [(0, (S // 2 // c["T"]) * c["T"], c["T"])]
+        # dense clusters that exercise the 30->25->20% fallback: two graded tiles (query tiles
+        # 80 and 100: the 25% and 20% picks fit k_max on some heads, unresolved on others) and
+        # one flat tile half-way (every pick overflows: unresolved, keeps the 20% set)
+        T = c["T"]
+        flat = [(0, 80 * T, T, 0.02, 1.0), (0, 100 * T, T, 0.02, 1.0),
+                (0, (S // 2 // T) * T, T)]
     spec = SynthSpec(batch=B, n_heads=H, n_kv_heads=Hk, seq_len=S, head_dim=c["D"],
                      n_planted=planted, seed=c["seed"],
                      dtype=torch.float32 if c["dtype"] == "f32" else torch.bfloat16,

@@ -431,3 +431,47 @@ def test_dca_select_and_hybrid_vs_oracle(D, T, dt):
         assert err.max() <= F32_TOL, err.max()
     else:
         assert err.mean() <= BF16_MEAN and np.quantile(err, 0.9999) <= BF16_MAX
+
+
+def test_cfg2_fallback_clusters_vs_oracle():
+    """Config-2 inputs (YaRN, GQA, bf16) at S = 8192 with its dense query clusters: the graded
+    tiles 80 / 100 and the flat tile 64 drive the 30 -> 25 -> 20 % fallback.  On these seeds the
+    oracle picks 30 % on some heads, 25 % and 20 % on others, and leaves the rest unresolved;
+    the device selection must make the same pick and keep the same keys on those tiles."""
+    from sta.synth import make_config_inputs
+    q, k, v, c = make_config_inputs(2, seq_len=8192, n_heads=8)
+    H, N, D, T = 8, 8192, 128, 64
+    invf, rs = yarn_inv_freq(D, 5e5, 4.0, 8192)
+    tau = torch.full((H,), 5.0)
+    out, ssz, ksz, kpct, ovf, kmeas, ovf20 = ex2.shared_pi_attention(
+        cu(q), cu(k), cu(v), tau, invf, 1.0, rope_scale=rs, tile=T, k_max=2048)
+    tiles = [64, 80, 100]
+    qx, kx, vx = (x[0].float().numpy() for x in (q, k, v))
+    kx, vx = np.repeat(kx, H // 2, 0), np.repeat(vx, H // 2, 0)
+    sm = 1.0 / math.sqrt(D)
+    sel = oracle.select_vote(qx, kx, tau.numpy(), invf.numpy(), 1.0, rs, sm, T, tiles=tiles)
+    dev = core.select(cu(q[0]), cu(k[0]), tau, Geometry(invf, 1.0, rs), tile=T)
+    votes = core.expand_compact(dev["votes"], H, N, T).cpu().numpy().astype(np.int32)
+    diff = sum(int(np.abs(votes[:, t] - sel["votes"][:, t]).sum()) for t in tiles)
+    assert diff <= sel["boundary"], (diff, sel["boundary"])
+    # selection bit-exact on the device's own votes (isolates the float boundary)
+    seen = set()
+    nt = N // T
+    idx = np.full((H, nt, 2048), N, np.int32)
+    npk = np.zeros((H, nt, 2048), np.float32)
+    npq = np.zeros((H, nt, T), np.float32)
+    for t in tiles:
+        s = oracle.build_sets(votes[:, t:t + 1], 1.0, 32, 32, 30.0, T, 2048, q_pos_base=t * T)
+        idx[:, t], npk[:, t], npq[:, t] = s[0][:, 0], s[1][:, 0], s[2][:, 0]
+        seen |= set(int(x) for x in s[5][:, 0])
+        np.testing.assert_array_equal(kpct[:, t].cpu().numpy(), s[5][:, 0])
+        np.testing.assert_array_equal(ksz[:, t].cpu().numpy(), s[4][:, 0])
+        np.testing.assert_array_equal(ssz[:, t].cpu().numpy(), s[3][:, 0])
+        np.testing.assert_array_equal(ovf20[:, t].cpu().numpy(), s[8][:, 0])
+    assert {0, 20, 25, 30} <= seen, seen
+    ref = oracle.gather_attn(qx, kx, vx, invf.numpy(), idx, npk, npq, sm, rs, T,
+                             v_is_bf16=True, tiles=tiles)
+    for t in tiles:
+        got = out[0, :, t * T:(t + 1) * T].float().cpu().numpy()
+        err = np.abs(got - ref[:, t * T:(t + 1) * T])
+        assert err.mean() <= BF16_MEAN and err.max() <= BF16_MAX, (t, err.max(), err.mean())
