@@ -10,8 +10,9 @@ top 30% with the 25/20% fallback, cap 2048, query tile 64.  Synthetic seeded inp
 (sta.synth) stand in for the model activations.  A "step" is one call of the attention op on
 pre-projected q, k, v: RoPE prologue + Kernel A (2 passes) + selection + attend.
 
-Multi-GPU: one process per GPU (torchrun); the 8 kv heads of the sequence are partitioned
-across ranks with no data-path collective (strong scaling: the job's total work is fixed).
+Multi-GPU: one process per GPU (torchrun); the layer is partitioned across ranks by kv-head
+range and/or query slab (sta.partition) with no data-path collective (strong scaling: the
+job's total work is fixed).
 Timing: CUDA events on torch's current stream, W untimed warm-up steps, K timed steps between
 barrier + synchronize, max over ranks.  Inputs (268 MB of q alone) exceed L2 (126 MB).
 """
@@ -49,6 +50,8 @@ def parse():
     ap.add_argument("--heads", type=int, default=None, help="override q heads (profiling only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--partition", choices=["auto", "heads", "slabs", "grid"], default="auto",
+                    help="multi-GPU unit: kv-head ranges, query slabs, or both (sta.partition)")
     ap.add_argument("--max-workspace-gb", type=int, default=48,
                     help="scratch cap; larger problems run over groups of kv heads")
     return ap.parse_args()
@@ -93,12 +96,14 @@ def workload(args):
     return q, k, v, tau, geo, geo_c, c
 
 
-def workload_desc(c, args, world):
+def workload_desc(c, args, world, unit=None):
     name = c["name"] + ("" if args.variant == "shared" else f"-{args.variant}")
     return {"workload": name, "batch": c["B"], "q_heads": c["H"], "kv_heads": c["Hkv"],
             "seq_len": c["S"], "head_dim": c["D"], "tile": c["T"] if args.variant == "shared" else 32,
             "k_max": c["k_max"], "tau": c["tau"], "pct": c.get("pct", 30.0),
-            "geometry": c["geom"], "parallelism": f"kv-head partition x{world}" if world > 1 else "single GPU",
+            "geometry": c["geom"],
+            "parallelism": (f"{unit['mode']} partition x{world} ({unit['head_parts']} kv-head parts"
+                            f" x {unit['slab_parts']} query slabs)") if world > 1 and unit else "single GPU",
             "l2": "no flush: inputs exceed L2 (q alone %.0f MB > 126 MB)" % (c["B"] * c["H"] * c["S"] * c["D"] * 2 / 1e6)}
 
 
@@ -246,13 +251,14 @@ def run_gpu(args):
         dist.init_process_group("nccl", device_id=dev)
     q, k, v, tau, geo, geo_c, c = workload(args)
     H, Hk, N, D, B = c["H"], c["Hkv"], c["S"], c["D"], c["B"]
-    if Hk % world:
-        raise SystemExit(f"{Hk} kv heads do not split over {world} GPUs")
+    from sta.partition import plan
+    unit = plan(Hk, N, world, rank, args.partition)
     G = H // Hk
-    k0, k1 = rank * Hk // world, (rank + 1) * Hk // world
-    qs = q[:, k0 * G:k1 * G].contiguous()
-    ks = k[:, k0:k1].contiguous()
-    vs = v[:, k0:k1].contiguous()
+    k0, k1 = unit["kv"]
+    s0, s1 = unit["slab"]
+    qs = q[:, k0 * G:k1 * G, s0:s1].contiguous()
+    ks = k[:, k0:k1, :s1].contiguous()
+    vs = v[:, k0:k1, :s1].contiguous()
     taus = tau[k0 * G:k1 * G]
     qd, kd, vd = qs.to(dev), ks.to(dev), vs.to(dev)
     ga = Geometry(geo["inv_freq"], geo["pos_scale"], geo["rope_scale"], geo.get("dca"))
@@ -260,7 +266,7 @@ def run_gpu(args):
     T = c["T"] if args.variant == "shared" else 32
     kw = dict(tile=T, k_max=c["k_max"], pct=c.get("pct", 30.0),
               select_score="freq" if args.variant == "shared" else "expmass", block_n=32,
-              max_workspace_bytes=args.max_workspace_gb << 30)
+              max_workspace_bytes=args.max_workspace_gb << 30, q_pos_base=s0)
 
     def step(qq, kk, vv, evs=None):
         return core.forward(args.variant, qq, kk, vv, taus, ga, gc, stage_events=evs, **kw)
@@ -325,20 +331,22 @@ def run_gpu(args):
         if world > 1:
             dist.all_reduce(t2, op=dist.ReduceOp.MAX)
         e2e_ms = float(t2.item()) / K
-        h2d = sum(x.numel() * x.element_size() for x in (qs, ks, vs))
+        nb = torch.tensor([sum(x.numel() * x.element_size() for x in (qs, ks, vs)),
+                           out_h.numel() * out_h.element_size()], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(nb)  # bytes copied by all ranks together
         e2e = {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": int(h2d) * world,
-               "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()) * world}
+               "h2d_bytes_per_step": int(nb[0].item()), "d2h_bytes_per_step": int(nb[1].item())}
 
     # ---- roofline of the dominant kernel (Kernel A on tensor cores)
     pk, pk_kind = peaks()
     Hr = qs.shape[1]
-    flops_sel = 2 * 2 * D * Hr * B * N * (N + 1) / 2 if args.variant != "pq_stream" else \
-        2 * D * Hr * B * N * (N + 1) / 2
+    pairs = (s1 * (s1 + 1) - s0 * (s0 + 1)) / 2   # causal (query, key) pairs of this rank's slab
+    flops_sel = (2 if args.variant != "pq_stream" else 1) * 2 * D * Hr * B * pairs
     sel_ms = stage_ms[1]
     achieved = flops_sel / (sel_ms / 1e3) / 1e12
     peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
-    traffic = select_traffic_bytes(c, Hr, args)
+    traffic = select_traffic_bytes(c, Hr, pairs)
     roof = {"kernel": "select_kernel (tcgen05 exact-max two-pass Kernel A)", "bound": "tensor",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "peak_kind": f"{pk_kind} bf16 sustained", "traffic": traffic,
@@ -367,7 +375,7 @@ def run_gpu(args):
                 "steps": K, "warmup": args.warmup, "ms_per_step": ms_step,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic (seeded generator sta.synth, BASELINE config shapes)",
-                "config": workload_desc(c, args, world), "clocks": clocks, "e2e": e2e,
+                "config": workload_desc(c, args, world, unit), "clocks": clocks, "e2e": e2e,
                 "gpu_launches": launches_per_step * K,
                 "stage_ms": {"rope_prologue": stage_ms[0], "select_tcgen05": stage_ms[1],
                              "build_sets": stage_ms[2], "attend": stage_ms[3]},
@@ -377,14 +385,14 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
-def select_traffic_bytes(c, heads, args):
+def select_traffic_bytes(c, heads, pairs):
     """DRAM bytes per select launch from the committed ncu summary, scaled by causal work."""
     p = os.path.join(ROOT, "profiles", "select_kernel_traffic.json")
     if not os.path.exists(p):
         return None
     with open(p) as f:
         d = json.load(f)
-    scale = (heads * c["S"] * (c["S"] + 1)) / (d["heads"] * d["seq_len"] * (d["seq_len"] + 1))
+    scale = (heads * 2 * pairs) / (d["heads"] * d["seq_len"] * (d["seq_len"] + 1))
     return d["dram_bytes"] * scale
 
 

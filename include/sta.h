@@ -51,6 +51,9 @@ const char* sta_last_error(void);
 int sta_version(void);
 /* Number of elements of one head of a compact selection array. */
 int64_t sta_tri_head_stride(int64_t n, int32_t tile);
+/* Same for a query slab starting at q_pos_base: local tile t at offset
+ * t*q_pos_base + tile*t*(t+1)/2, keys j < min(q_pos_base + (t+1)*tile, n). */
+int64_t sta_tri_head_stride_q(int64_t n, int32_t tile, int64_t q_pos_base);
 
 /* ---------------------------------------------------------------------------------------
  * Stage 0 -- RoPE prologue of the selection geometry.
@@ -105,6 +108,11 @@ typedef struct sta_select_args {
    * q_hi / q_lo then hold 3 planes (3, batch*n_heads, n, d): queries rotated for keys of the
    * same chunk, of the previous chunk and of older chunks (sta_rope_split_dca roles 1, 2, 3) */
   int32_t dca_chunk_len;
+  /* absolute position of the first query row (multiple of 128; 0 for a whole-sequence
+   * prefill).  q_hi / q_lo then hold the n - q_pos_base rows q_pos_base..n-1, k holds all n
+   * keys, and row_max / row_count are (batch*n_heads, n - q_pos_base); compact arrays use the
+   * layout of sta_tri_head_stride_q */
+  int64_t q_pos_base;
 } sta_select_args;
 
 int sta_select(const sta_select_args* a, void* stream);
@@ -136,6 +144,8 @@ typedef struct sta_build_args {
   uint8_t* overflow;       /* (heads, nt) top-pct set exceeded k_max */
   int32_t* kpct_meas;      /* (heads, nt) */
   uint8_t* overflow20;     /* (heads, nt) still over k_max at the floor percentage */
+  int64_t q_pos_base;      /* first query position (the reference's q_pos_base, shared_selection_triton_exact_2.py:291);
+                            * nt = ceil((n - q_pos_base) / tile) local tiles */
 } sta_build_args;
 
 int sta_build_sets(const sta_build_args* a, void* stream);
@@ -164,6 +174,7 @@ typedef struct sta_build_pq_args {
   int32_t* usize;
   int32_t* kept_size;
   uint8_t* overflow;
+  int64_t q_pos_base;      /* as sta_build_args (shared_selection_triton_perquery.py:381) */
 } sta_build_pq_args;
 
 int sta_build_sets_pq(const sta_build_pq_args* a, void* stream);
@@ -193,6 +204,7 @@ typedef struct sta_build_chunk_args {
   int32_t* mask;           /* optional (NULL): -1 on valid slots, 0 on padding */
   int32_t* usize;          /* (heads, nt) passers visible to the tile */
   int32_t* kept_size;      /* (heads, nt) */
+  int64_t q_pos_base;      /* as sta_build_args */
 } sta_build_chunk_args;
 
 int sta_build_sets_chunk(const sta_build_chunk_args* a, void* stream);
@@ -237,6 +249,9 @@ typedef struct sta_attend_args {
   const void* rope_table;
   float rope_table_R;
   int64_t rope_table_len;
+  /* first query position: q / out / q_hi / q_lo hold rows q_pos_base..n-1 (n - q_pos_base
+   * rows), k / v / k_hi / k_lo all n keys (the reference's q_pos_base, shared_selection_triton_exact_2.py:169) */
+  int64_t q_pos_base;
 } sta_attend_args;
 
 int sta_gather_attend(const sta_attend_args* a, void* stream);
@@ -276,6 +291,7 @@ typedef struct sta_pqstream_args {
   int32_t* kept;           /* (heads, n) */
   float* blocks;           /* (heads, nt) */
   float* skipped;          /* (heads, nt) */
+  int64_t q_pos_base;      /* as sta_attend_args; row_max / kept are (heads, n - q_pos_base) */
 } sta_pqstream_args;
 
 int sta_pqstream_attend(const sta_pqstream_args* a, void* stream);
@@ -351,6 +367,12 @@ typedef struct sta_forward_args {
    * window w, chunk_len s - w a multiple of 256) with inv_freq_a / rope_scale_a */
   int32_t dca_chunk_size;
   int32_t dca_local_window;
+  /* > 0: query slab.  q / out hold the n - q_pos_base queries at positions q_pos_base..n-1
+   * (multiple of 128), k / v the n keys 0..n-1; per-tile statistics cover the slab's
+   * ceil((n - q_pos_base) / tile) tiles and PQ-Stream kept_rows its rows.  Every query tile's
+   * result is independent of the other tiles, so a sequence split into slabs reproduces the
+   * whole-sequence call exactly (single-sequence multi-GPU partition). */
+  int64_t q_pos_base;
 } sta_forward_args;
 
 size_t sta_shared_workspace_bytes(const sta_forward_args* a);

@@ -105,9 +105,10 @@ Layout layout_for(const sta_forward_args* a, Variant v, int64_t c) {
   const int64_t G = a->n_heads / a->n_kv_heads;
   const int64_t qh = c * G;  // q heads in the group
   const int64_t N = a->n, D = a->d;
+  const int64_t Nq = N - a->q_pos_base;  // query rows of the slab
   const int T = (v == kShared || v == kChunk) ? a->tile : 32;
-  const int64_t nt = (N + T - 1) / T;
-  const int64_t HS = tri_head_stride(N, T);
+  const int64_t nt = (Nq + T - 1) / T;
+  const int64_t HS = tri_head_stride(N, T, a->q_pos_base);
   size_t o = 0;
   auto take = [&](size_t bytes) {
     const size_t r = o;
@@ -115,12 +116,12 @@ Layout layout_for(const sta_forward_args* a, Variant v, int64_t c) {
     return r;
   };
   const int64_t qplanes = a->dca_chunk_size > 0 ? 3 : 1;
-  L.qh = take(qplanes * qh * N * D * 2);
-  L.ql = take(qplanes * qh * N * D * 2);
+  L.qh = take(qplanes * qh * Nq * D * 2);
+  L.ql = take(qplanes * qh * Nq * D * 2);
   L.kh = take(c * N * D * 2);
   L.kl = take(c * N * D * 2);
   if (v == kPQStream) {
-    L.rowmax = take(qh * N * 4);
+    L.rowmax = take(qh * Nq * 4);
   } else {
     L.votes = take(qh * HS);
     if (a->select_score != STA_SCORE_FREQ) L.wvotes = take(qh * HS * 4);
@@ -182,6 +183,8 @@ int check_forward(const sta_forward_args* a, Variant v) {
       return fail(STA_ERR_ARG, "forward: chunk statistics outputs required");
   }
   if (v != kPQStream && a->k_max <= 0) return fail(STA_ERR_ARG, "forward: k_max must be > 0");
+  if (a->q_pos_base < 0 || (a->n > 0 && a->q_pos_base >= a->n) || a->q_pos_base % 128)
+    return fail(STA_ERR_UNSUPPORTED, "forward: q_pos_base must be a multiple of 128 below n");
   if (a->dca_chunk_size > 0) {
     const int64_t L = (int64_t)a->dca_chunk_size - a->dca_local_window;
     if (a->dca_local_window <= 0 || L <= 0 || L % 256)
@@ -218,8 +221,9 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
   if (!ws || ws_len < L.total) return fail(STA_ERR_WORKSPACE, "forward: workspace too small");
   uint8_t* w = static_cast<uint8_t*>(ws);
   const int64_t H = a->n_heads, Hk = a->n_kv_heads, G = H / Hk, N = a->n;
+  const int64_t qbase = a->q_pos_base, Nq = N - qbase;
   const int T = (v == kShared || v == kChunk) ? a->tile : 32;
-  const int64_t nt = (N + T - 1) / T;
+  const int64_t nt = (Nq + T - 1) / T;
   const int64_t es = esize(a->dtype);
   const int64_t kmax = a->k_max;
   if (L.rtab_len > 0)
@@ -233,7 +237,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       const uint8_t* q = static_cast<const uint8_t*>(a->q) + h0 * a->q_stride_h * es;
       const uint8_t* k = static_cast<const uint8_t*>(a->k) + k0 * a->k_stride_h * es;
       const uint8_t* vv = static_cast<const uint8_t*>(a->v) + k0 * a->v_stride_h * es;
-      uint8_t* out = static_cast<uint8_t*>(a->out) + h0 * N * a->d * es;
+      uint8_t* out = static_cast<uint8_t*>(a->out) + h0 * Nq * a->d * es;
       const float* tau = a->tau + g0 * G;
       auto mark = [&](int i) {
         if (a->stage_events) cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), st);
@@ -242,19 +246,19 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       const bool dca = a->dca_chunk_size > 0;
       const int64_t dL = dca ? (int64_t)a->dca_chunk_size - a->dca_local_window : 0;
       if (!dca) {
-        STA_TRY(launch_rope_split(q, a->dtype, qn, N, a->d, a->q_stride_h, a->q_stride_n,
+        STA_TRY(launch_rope_split(q, a->dtype, qn, Nq, a->d, a->q_stride_h, a->q_stride_n,
                                   a->inv_freq_a, a->pos_scale_a, a->rope_scale_a, w + L.qh,
-                                  w + L.ql, st));
+                                  w + L.ql, st, 0, 0, 0, qbase));
         STA_TRY(launch_rope_split(k, a->dtype, c, N, a->d, a->k_stride_h, a->k_stride_n,
                                   a->inv_freq_a, a->pos_scale_a, a->rope_scale_a, w + L.kh,
                                   w + L.kl, st));
       } else {
-        const size_t plane = (size_t)qn * N * a->d * 2;
+        const size_t plane = (size_t)qn * Nq * a->d * 2;
         for (int role = 1; role <= 3; ++role)
-          STA_TRY(launch_rope_split(q, a->dtype, qn, N, a->d, a->q_stride_h, a->q_stride_n,
+          STA_TRY(launch_rope_split(q, a->dtype, qn, Nq, a->d, a->q_stride_h, a->q_stride_n,
                                     a->inv_freq_a, 1.0f, a->rope_scale_a,
                                     w + L.qh + (role - 1) * plane, w + L.ql + (role - 1) * plane,
-                                    st, role, dL, a->dca_chunk_size));
+                                    st, role, dL, a->dca_chunk_size, qbase));
         STA_TRY(launch_rope_split(k, a->dtype, c, N, a->d, a->k_stride_h, a->k_stride_n,
                                   a->inv_freq_a, 1.0f, a->rope_scale_a, w + L.kh, w + L.kl, st,
                                   1, dL, a->dca_chunk_size));
@@ -273,6 +277,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       s.sm_scale = a->sm_scale;
       s.tau = tau;
       s.dca_chunk_len = (int32_t)dL;
+      s.q_pos_base = qbase;
       mark(1);
       if (v == kPQStream) {
         s.max_only = 1;
@@ -305,7 +310,8 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
         pa.rope_table_R = L.rtab_R;
         pa.rope_table_len = L.rtab_len;
         pa.span = a->span + h0 * nt;
-        pa.kept = a->kept_rows + h0 * N;
+        pa.kept = a->kept_rows + h0 * Nq;
+        pa.q_pos_base = qbase;
         pa.blocks = a->blocks + h0 * nt;
         pa.skipped = a->skipped + h0 * nt;
         mark(3);
@@ -346,6 +352,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
         ba.overflow = a->overflow + h0 * nt;
         ba.kpct_meas = a->kpct_meas + h0 * nt;
         ba.overflow20 = a->overflow20 + h0 * nt;
+        ba.q_pos_base = qbase;
         STA_TRY(launch_build_sets(&ba, st));
       } else if (v == kChunk) {
         int32_t* cmask = a->mask_out ? a->mask_out + h0 * nt * kmax : nullptr;
@@ -368,6 +375,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
         ba.mask = cmask;
         ba.usize = a->shared_size + h0 * nt;
         ba.kept_size = a->kept_size + h0 * nt;
+        ba.q_pos_base = qbase;
         STA_TRY(launch_build_sets_chunk(&ba, st));
       } else {
         mask = a->mask_out ? a->mask_out + h0 * nt * kmax : reinterpret_cast<int32_t*>(w + L.mask);
@@ -389,6 +397,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
         ba.usize = a->shared_size + h0 * nt;
         ba.kept_size = a->kept_size + h0 * nt;
         ba.overflow = a->overflow + h0 * nt;
+        ba.q_pos_base = qbase;
         STA_TRY(launch_build_sets_pq(&ba, st));
       }
       mark(3);
@@ -422,6 +431,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       ca.rope_table = L.rtab_len > 0 ? w + L.rtab : nullptr;
       ca.rope_table_R = L.rtab_R;
       ca.rope_table_len = L.rtab_len;
+      ca.q_pos_base = qbase;
       STA_TRY(launch_gather_attend(&ca, st));
       mark(4);
     }
@@ -444,6 +454,10 @@ const char* sta_last_error(void) { return g_last_error; }
 int sta_version(void) { return 1; }
 
 int64_t sta_tri_head_stride(int64_t n, int32_t tile) { return tri_head_stride(n, tile); }
+
+int64_t sta_tri_head_stride_q(int64_t n, int32_t tile, int64_t q_pos_base) {
+  return tri_head_stride(n, tile, q_pos_base);
+}
 
 int sta_rope_split(const void* x, int32_t dtype, int64_t heads, int64_t n, int32_t d,
                    int64_t stride_h, int64_t stride_n, const float* inv_freq, float pos_scale,

@@ -31,6 +31,7 @@ struct AttendP {
   int64_t vsh, vsn;
   void* out;
   int64_t BH, N, nt;
+  int64_t qbase, Nq;  // queries: positions qbase .. N-1, held as rows 0 .. Nq-1
   int H, Hkv;
   int k_max;
   const int32_t* idx;
@@ -88,19 +89,20 @@ gather_attend_kernel(const AttendP p) {
   const bool direct = !F32 && p.direct;
   for (int it = tid; it < T * C8; it += NTH) {
     const int r = it / C8, f0 = (it % C8) * 8;
-    const int64_t qp = (int64_t)t * T + r;
+    const int64_t qp = p.qbase + (int64_t)t * T + r;  // absolute query position
+    const int64_t ql = qp - p.qbase;                    // row in the Q slab
     const float pos = npq_row[r];
     __nv_bfloat16* dst = sQ + r * LD;
     if (direct && qp < N && pos == __fmul_rn((float)qp, p.ps_sel)) {
-      copy_rotated<HALF>(p.qh + (bh * N + qp) * D, p.ql + (bh * N + qp) * D, f0, dst, T * LD);
+      copy_rotated<HALF>(p.qh + (bh * p.Nq + ql) * D, p.ql + (bh * p.Nq + ql) * D, f0, dst, T * LD);
     } else {
-      rotate8<NQ, HALF>(qg + qp * p.qsn, qp < N, f0, pos, p.inv_freq, p.rope_scale, dst, T * LD,
+      rotate8<NQ, HALF>(qg + ql * p.qsn, qp < N, f0, pos, p.inv_freq, p.rope_scale, dst, T * LD,
                         p.rtab, table_index(pos, p.rtab_R, p.rtab_len));
     }
   }
 
   const int ra = warp * 16 + g, rb = ra + 8;  // tile-local rows of this thread
-  const int64_t qpa = (int64_t)t * T + ra, qpb = (int64_t)t * T + rb;
+  const int64_t qpa = p.qbase + (int64_t)t * T + ra, qpb = p.qbase + (int64_t)t * T + rb;
   float o[D / 8][4];
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
@@ -274,23 +276,24 @@ gather_attend_kernel(const AttendP p) {
   }
 
   // ---- epilogue
-  TV* og = static_cast<TV*>(p.out) + bh * N * D;
+  TV* og = static_cast<TV*>(p.out) + bh * p.Nq * D;
+  const int64_t ora = qpa - p.qbase, orb = qpb - p.qbase;  // rows of the output slab
 #pragma unroll
   for (int dt = 0; dt < D / 8; ++dt) {
     const int col = dt * 8 + 2 * c4;
     if (qpa < N) {
       if (F32) {
-        reinterpret_cast<float2*>(og + qpa * D + col)[0] = make_float2(o[dt][0] / lA, o[dt][1] / lA);
+        reinterpret_cast<float2*>(og + ora * D + col)[0] = make_float2(o[dt][0] / lA, o[dt][1] / lA);
       } else {
-        reinterpret_cast<__nv_bfloat162*>(og + qpa * D + col)[0] =
+        reinterpret_cast<__nv_bfloat162*>(og + ora * D + col)[0] =
             __floats2bfloat162_rn(o[dt][0] / lA, o[dt][1] / lA);
       }
     }
     if (qpb < N) {
       if (F32) {
-        reinterpret_cast<float2*>(og + qpb * D + col)[0] = make_float2(o[dt][2] / lB, o[dt][3] / lB);
+        reinterpret_cast<float2*>(og + orb * D + col)[0] = make_float2(o[dt][2] / lB, o[dt][3] / lB);
       } else {
-        reinterpret_cast<__nv_bfloat162*>(og + qpb * D + col)[0] =
+        reinterpret_cast<__nv_bfloat162*>(og + orb * D + col)[0] =
             __floats2bfloat162_rn(o[dt][2] / lB, o[dt][3] / lB);
       }
     }
@@ -342,7 +345,11 @@ int launch_gather_attend(const sta_attend_args* a, cudaStream_t stream) {
   p.out = a->out;
   p.BH = a->batch * a->n_heads;
   p.N = a->n;
-  p.nt = (a->n + a->tile - 1) / a->tile;
+  if (a->q_pos_base < 0 || a->q_pos_base >= a->n)
+    return fail(STA_ERR_ARG, "sta_gather_attend: q_pos_base outside [0, n)");
+  p.qbase = a->q_pos_base;
+  p.Nq = a->n - a->q_pos_base;
+  p.nt = (p.Nq + a->tile - 1) / a->tile;
   p.H = (int)a->n_heads;
   p.Hkv = (int)a->n_kv_heads;
   p.k_max = a->k_max;

@@ -191,7 +191,7 @@ __device__ void radix_kth_largest(const SetRow& r, int64_t N, bool weighted, int
 struct BuildP {
   const uint8_t* votes;
   const float* wvotes;
-  int64_t BH, N, nt, head_stride;
+  int64_t BH, N, nt, head_stride, qbase;
   int T, k_max, n_global, n_local;
   int nsteps;
   int steps[3];
@@ -216,9 +216,9 @@ __global__ void __launch_bounds__(kBT) build_sets_kernel(const BuildP p) {
   const int tid = threadIdx.x;
   const int64_t N = p.N;
   const int T = p.T;
-  const int64_t tstart = t * T;
+  const int64_t tstart = p.qbase + t * T;  // absolute position of the tile's first query
   SetRow r;
-  const int64_t off = bh * p.head_stride + tri_tile_offset(t, T);
+  const int64_t off = bh * p.head_stride + tri_tile_offset(t, T, p.qbase);
   r.v = p.votes + off;
   r.w = p.weighted ? p.wvotes + off : nullptr;
   r.b = nullptr;
@@ -415,7 +415,7 @@ struct BuildPQP {
   const uint8_t* votes;
   const float* wvotes;
   const uint32_t* bits;
-  int64_t BH, N, nt, head_stride;
+  int64_t BH, N, nt, head_stride, qbase;
   int T, k_max, n_global, n_local;
   int weighted;
   int32_t* idx;
@@ -433,9 +433,9 @@ __global__ void __launch_bounds__(kBT) build_sets_pq_kernel(const BuildPQP p) {
   const int tid = threadIdx.x;
   const int64_t N = p.N;
   const int T = p.T;
-  const int64_t tstart = t * T;
+  const int64_t tstart = p.qbase + t * T;  // absolute position of the tile's first query
   SetRow r;
-  const int64_t off = bh * p.head_stride + tri_tile_offset(t, T);
+  const int64_t off = bh * p.head_stride + tri_tile_offset(t, T, p.qbase);
   r.v = p.votes + off;
   r.w = p.weighted ? p.wvotes + off : nullptr;
   r.b = p.bits + off;
@@ -553,7 +553,7 @@ __global__ void __launch_bounds__(kBT) build_sets_pq_kernel(const BuildPQP p) {
 struct BuildChunkP {
   const uint8_t* votes;
   const float* wvotes;
-  int64_t BH, N, nt, head_stride;
+  int64_t BH, N, nt, head_stride, qbase;
   int T, k_max, n_global, n_local, C, n_chunk, weighted, mean_agg;
   int32_t* idx;
   float* newpos_k;
@@ -571,11 +571,11 @@ __global__ void __launch_bounds__(kBT) build_sets_chunk_kernel(const BuildChunkP
   const int tid = threadIdx.x;
   const int64_t N = p.N;
   const int T = p.T, C = p.C;
-  const int64_t tstart = t * T;
+  const int64_t tstart = p.qbase + t * T;
   const int64_t nC = (N + C - 1) / C;
   float* mass = reinterpret_cast<float*>(dsm);
   uint8_t* flag = reinterpret_cast<uint8_t*>(mass + nC);
-  const int64_t off = bh * p.head_stride + tri_tile_offset(t, T);
+  const int64_t off = bh * p.head_stride + tri_tile_offset(t, T, p.qbase);
   const uint8_t* v = p.votes + off;
   const float* w = p.weighted ? p.wvotes + off : nullptr;
   const int64_t hi = min(tstart + T, N);      // causal keys of the tile (votes exist below)
@@ -750,8 +750,10 @@ int launch_build_sets_chunk(const sta_build_chunk_args* a, cudaStream_t stream) 
   p.BH = a->heads;
   p.N = a->n;
   p.T = a->tile;
-  p.nt = (a->n + a->tile - 1) / a->tile;
-  p.head_stride = tri_head_stride(a->n, a->tile);
+  if (a->q_pos_base < 0 || a->q_pos_base >= a->n) return fail(STA_ERR_ARG, "q_pos_base outside [0, n)");
+  p.qbase = a->q_pos_base;
+  p.nt = (a->n - a->q_pos_base + a->tile - 1) / a->tile;
+  p.head_stride = tri_head_stride(a->n, a->tile, a->q_pos_base);
   p.k_max = a->k_max;
   p.n_global = a->n_global;
   p.n_local = a->n_local;
@@ -793,8 +795,10 @@ int launch_build_sets(const sta_build_args* a, cudaStream_t stream) {
   p.BH = a->heads;
   p.N = a->n;
   p.T = a->tile;
-  p.nt = (a->n + a->tile - 1) / a->tile;
-  p.head_stride = tri_head_stride(a->n, a->tile);
+  if (a->q_pos_base < 0 || a->q_pos_base >= a->n) return fail(STA_ERR_ARG, "q_pos_base outside [0, n)");
+  p.qbase = a->q_pos_base;
+  p.nt = (a->n - a->q_pos_base + a->tile - 1) / a->tile;
+  p.head_stride = tri_head_stride(a->n, a->tile, a->q_pos_base);
   p.k_max = a->k_max;
   p.n_global = a->n_global;
   p.n_local = a->n_local;
@@ -839,8 +843,10 @@ int launch_build_sets_pq(const sta_build_pq_args* a, cudaStream_t stream) {
   p.BH = a->heads;
   p.N = a->n;
   p.T = a->tile;
-  p.nt = (a->n + a->tile - 1) / a->tile;
-  p.head_stride = tri_head_stride(a->n, a->tile);
+  if (a->q_pos_base < 0 || a->q_pos_base >= a->n) return fail(STA_ERR_ARG, "q_pos_base outside [0, n)");
+  p.qbase = a->q_pos_base;
+  p.nt = (a->n - a->q_pos_base + a->tile - 1) / a->tile;
+  p.head_stride = tri_head_stride(a->n, a->tile, a->q_pos_base);
   p.k_max = a->k_max;
   p.n_global = a->n_global;
   p.n_local = a->n_local;

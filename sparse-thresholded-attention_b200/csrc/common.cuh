@@ -221,14 +221,16 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
-// Compact (lower-triangular) layout of per-(head, tile, key) selection arrays: tile t of a
-// head only has entries for keys j < hi_t = min((t+1)*T, N).
-__host__ __device__ __forceinline__ int64_t tri_head_stride(int64_t N, int T) {
-  int64_t nt = (N + T - 1) / T;
-  return (int64_t)T * (nt - 1) * nt / 2 + N;
+// Compact (lower-triangular) layout of per-(head, tile, key) selection arrays.  The queries
+// are the positions [base, N) (base = q_pos_base, 0 for a whole-sequence prefill); local query
+// tile t only has entries for keys j < hi_t = min(base + (t+1)*T, N), so it starts at
+// sum_{u<t} (base + (u+1)*T) = t*base + T*t*(t+1)/2.
+__host__ __device__ __forceinline__ int64_t tri_tile_offset(int64_t t, int T, int64_t base = 0) {
+  return t * base + (int64_t)T * t * (t + 1) / 2;
 }
-__host__ __device__ __forceinline__ int64_t tri_tile_offset(int64_t t, int T) {
-  return (int64_t)T * t * (t + 1) / 2;
+__host__ __device__ __forceinline__ int64_t tri_head_stride(int64_t N, int T, int64_t base = 0) {
+  const int64_t nt = (N - base + T - 1) / T;
+  return nt > 0 ? tri_tile_offset(nt - 1, T, base) + N : 0;
 }
 
 }  // namespace sta

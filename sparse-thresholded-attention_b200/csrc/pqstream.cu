@@ -33,6 +33,7 @@ struct PQSP {
   int64_t vsh, vsn;
   void* out;
   int64_t BH, N, nt;
+  int64_t qbase, Nq;  // queries: positions qbase .. N-1, held as rows 0 .. Nq-1
   int H, Hkv;
   const __nv_bfloat16 *qh, *ql, *kh, *kl;
   const float* row_max;
@@ -114,12 +115,12 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   const TV* qg = static_cast<const TV*>(p.q) + bh * p.qsh;
   const TV* kg = static_cast<const TV*>(p.k) + kvh * p.ksh;
   const TV* vg = static_cast<const TV*>(p.v) + kvh * p.vsh;
-  const __nv_bfloat16* qhg = p.qh + bh * N * D;
-  const __nv_bfloat16* qlg = p.ql + bh * N * D;
+  const __nv_bfloat16* qhg = p.qh + bh * p.Nq * D;
+  const __nv_bfloat16* qlg = p.ql + bh * p.Nq * D;
   const __nv_bfloat16* khg = p.kh + kvh * N * D;
   const __nv_bfloat16* klg = p.kl + kvh * N * D;
 
-  const int64_t tstart = (int64_t)t * T;
+  const int64_t tstart = p.qbase + (int64_t)t * T;  // absolute position of the tile's first query
   const int64_t P_top = min(tstart + T - 1, N - 1);
   const int64_t hi = P_top + 1;
   const int nblk = (int)((hi + BN - 1) / BN);
@@ -130,17 +131,18 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   for (int it = tid; it < T * D; it += NTH) {
     const int r = it / D, d = it % D;
     const int64_t qp = tstart + r;
+    const int64_t ql = qp - p.qbase;
     __nv_bfloat16 zh = __float2bfloat16_rn(0.f);
-    sQs[r * LD + d] = qp < N ? qhg[qp * D + d] : zh;
-    sQs[(T + r) * LD + d] = qp < N ? qlg[qp * D + d] : zh;
+    sQs[r * LD + d] = qp < N ? qhg[ql * D + d] : zh;
+    sQs[(T + r) * LD + d] = qp < N ? qlg[ql * D + d] : zh;
   }
   for (int it = tid; it < T * HALF; it += NTH) {
     const int r = it / HALF, f = it % HALF;
     const int64_t qp = tstart + r;
     float x1 = 0.f, x2 = 0.f;
     if (qp < N) {
-      x1 = ldv(qg + qp * p.qsn + f);
-      x2 = ldv(qg + qp * p.qsn + f + HALF);
+      x1 = ldv(qg + (qp - p.qbase) * p.qsn + f);
+      x2 = ldv(qg + (qp - p.qbase) * p.qsn + f + HALF);
     }
     const float npq = (float)(qp - P_top);
     float r1, r2;
@@ -166,8 +168,9 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   const int ra = warp * 16 + g, rb = ra + 8;
   const int64_t qpa = tstart + ra, qpb = tstart + rb;
   const bool okA = qpa < N, okB = qpb < N;
-  const float thrA = okA ? __fsub_rn(p.row_max[bh * N + qpa], tau) : INFINITY;
-  const float thrB = okB ? __fsub_rn(p.row_max[bh * N + qpb], tau) : INFINITY;
+  const int64_t ra_l = qpa - p.qbase, rb_l = qpb - p.qbase;  // slab rows
+  const float thrA = okA ? __fsub_rn(p.row_max[bh * p.Nq + ra_l], tau) : INFINITY;
+  const float thrB = okB ? __fsub_rn(p.row_max[bh * p.Nq + rb_l], tau) : INFINITY;
 
   float o[D / 8][4];
 #pragma unroll
@@ -355,28 +358,28 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
     ++n_used;
   }
 
-  TV* og = static_cast<TV*>(p.out) + bh * N * D;
+  TV* og = static_cast<TV*>(p.out) + bh * p.Nq * D;
 #pragma unroll
   for (int dt = 0; dt < D / 8; ++dt) {
     const int col = dt * 8 + 2 * c4;
     if (okA) {
       if (F32)
-        reinterpret_cast<float2*>(og + qpa * D + col)[0] = make_float2(o[dt][0] / lA, o[dt][1] / lA);
+        reinterpret_cast<float2*>(og + ra_l * D + col)[0] = make_float2(o[dt][0] / lA, o[dt][1] / lA);
       else
-        reinterpret_cast<__nv_bfloat162*>(og + qpa * D + col)[0] =
+        reinterpret_cast<__nv_bfloat162*>(og + ra_l * D + col)[0] =
             __floats2bfloat162_rn(o[dt][0] / lA, o[dt][1] / lA);
     }
     if (okB) {
       if (F32)
-        reinterpret_cast<float2*>(og + qpb * D + col)[0] = make_float2(o[dt][2] / lB, o[dt][3] / lB);
+        reinterpret_cast<float2*>(og + rb_l * D + col)[0] = make_float2(o[dt][2] / lB, o[dt][3] / lB);
       else
-        reinterpret_cast<__nv_bfloat162*>(og + qpb * D + col)[0] =
+        reinterpret_cast<__nv_bfloat162*>(og + rb_l * D + col)[0] =
             __floats2bfloat162_rn(o[dt][2] / lB, o[dt][3] / lB);
     }
   }
   if (c4 == 0) {
-    if (okA) p.kept[bh * N + qpa] = keptA;
-    if (okB) p.kept[bh * N + qpb] = keptB;
+    if (okA) p.kept[bh * p.Nq + ra_l] = keptA;
+    if (okB) p.kept[bh * p.Nq + rb_l] = keptB;
   }
   if (tid == 0) {
     const int64_t o2 = bh * p.nt + t;
@@ -430,7 +433,11 @@ int launch_pqstream(const sta_pqstream_args* a, cudaStream_t stream) {
   p.out = a->out;
   p.BH = a->batch * a->n_heads;
   p.N = a->n;
-  p.nt = (a->n + T - 1) / T;
+  if (a->q_pos_base < 0 || a->q_pos_base >= a->n)
+    return fail(STA_ERR_ARG, "sta_pqstream_attend: q_pos_base outside [0, n)");
+  p.qbase = a->q_pos_base;
+  p.Nq = a->n - a->q_pos_base;
+  p.nt = (p.Nq + T - 1) / T;
   p.H = (int)a->n_heads;
   p.Hkv = (int)a->n_kv_heads;
   p.qh = static_cast<const __nv_bfloat16*>(a->q_hi);

@@ -32,14 +32,15 @@ __device__ __forceinline__ int64_t position_id(int64_t n, int mode, int64_t L, i
 }
 
 // One thread per (row, frequency pair).  x is (rows = heads*N, D) with element strides
-// (stride_h, stride_n); last dim contiguous.  Angle = (float(position_id) * pos_scale) * inv_freq.
+// (stride_h, stride_n); last dim contiguous; row n sits at position pos0 + n.
+// Angle = (float(position_id) * pos_scale) * inv_freq.
 template <typename T>
 __global__ void rope_split_kernel(const T* __restrict__ x, int64_t heads, int64_t N, int D,
                                   int64_t stride_h, int64_t stride_n,
                                   const float* __restrict__ inv_freq, float pos_scale,
                                   float rope_scale, __nv_bfloat16* __restrict__ hi,
                                   __nv_bfloat16* __restrict__ lo, int mode, int64_t dca_L,
-                                  int64_t dca_s) {
+                                  int64_t dca_s, int64_t pos0) {
   const int half = D >> 1;
   const int64_t total = heads * N * half;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -51,7 +52,7 @@ __global__ void rope_split_kernel(const T* __restrict__ x, int64_t heads, int64_
     const T* src = x + h * stride_h + n * stride_n;
     const float x1 = load_f(src + f);
     const float x2 = load_f(src + f + half);
-    const float pid = (float)position_id(n, mode, dca_L, dca_s);
+    const float pid = (float)position_id(pos0 + n, mode, dca_L, dca_s);
     const float ang = __fmul_rn(__fmul_rn(pid, pos_scale), __ldg(inv_freq + f));
     float r1, r2;
     rope_pair(x1, x2, ang, rope_scale, r1, r2);
@@ -69,7 +70,8 @@ __global__ void rope_split_kernel(const T* __restrict__ x, int64_t heads, int64_
 int launch_rope_split(const void* x, int dtype, int64_t heads, int64_t N, int D,
                       int64_t stride_h, int64_t stride_n, const float* inv_freq,
                       float pos_scale, float rope_scale, void* hi, void* lo,
-                      cudaStream_t stream, int mode, int64_t dca_L, int64_t dca_s) {
+                      cudaStream_t stream, int mode, int64_t dca_L, int64_t dca_s,
+                      int64_t pos0) {
   const int64_t total = heads * N * (D / 2);
   if (total == 0) return 0;
   const int threads = 256;
@@ -79,12 +81,12 @@ int launch_rope_split(const void* x, int dtype, int64_t heads, int64_t N, int D,
     rope_split_kernel<float><<<(unsigned)blocks, threads, 0, stream>>>(
         static_cast<const float*>(x), heads, N, D, stride_h, stride_n, inv_freq, pos_scale,
         rope_scale, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), mode, dca_L,
-        dca_s);
+        dca_s, pos0);
   } else {
     rope_split_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(x), heads, N, D, stride_h, stride_n, inv_freq,
         pos_scale, rope_scale, static_cast<__nv_bfloat16*>(hi),
-        static_cast<__nv_bfloat16*>(lo), mode, dca_L, dca_s);
+        static_cast<__nv_bfloat16*>(lo), mode, dca_L, dca_s, pos0);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : STA_ERR_CUDA;
 }

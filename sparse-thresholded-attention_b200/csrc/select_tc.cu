@@ -49,9 +49,12 @@ struct Cfg {
 struct Params {
   int64_t BH;
   int H, Hkv;
-  int64_t N;
+  int64_t N;            // keys (= last query position + 1)
+  int64_t Nq;           // query rows held by Q (positions qbase .. N-1)
+  int64_t qbase;        // absolute position of query row 0 (multiple of BM)
+  int qb0;              // qbase / BM
   int T;
-  int nqb;
+  int nqb;              // local query blocks
   int npass;
   int wmode;
   float sm_scale;
@@ -130,7 +133,7 @@ __device__ __forceinline__ float raw_threshold(float thr, float sm) {
 
 __device__ __forceinline__ void decode_item(int64_t w, const Params& p, int64_t& bh, int& qb,
                                             int64_t& kvh) {
-  qb = p.nqb - 1 - (int)(w / p.BH);
+  qb = p.nqb - 1 - (int)(w / p.BH) + p.qb0;  // absolute query block
   bh = w % p.BH;
   const int G = p.H / p.Hkv;
   kvh = (bh / p.H) * p.Hkv + (bh % p.H) / G;
@@ -219,8 +222,9 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
               mbar_arrive_expect_tx(q_full, C::Q_BYTES);
               const int z = (int)(plane * p.BH + bh);
               for (int c = 0; c < C::NC; ++c) {
-                tma_load_3d(sQ + c * kTileBytes, &tm_qhi, q_full, c * 64, qb * BM, z);
-                tma_load_3d(sQ + (C::NC + c) * kTileBytes, &tm_qlo, q_full, c * 64, qb * BM, z);
+                const int qrow = (qb - p.qb0) * BM;  // local row in the Q slab
+                tma_load_3d(sQ + c * kTileBytes, &tm_qhi, q_full, c * 64, qrow, z);
+                tma_load_3d(sQ + (C::NC + c) * kTileBytes, &tm_qlo, q_full, c * 64, qrow, z);
               }
               ++qloads;
               cur = plane;
@@ -422,7 +426,8 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
                 vs += s_vote[o];
                 wsum += s_w[o];
               }
-              const int64_t off = bh * p.head_stride + tri_tile_offset(tg, p.T) + kj;
+              const int64_t off =
+                  bh * p.head_stride + tri_tile_offset(tg - p.qbase / p.T, p.T, p.qbase) + kj;
               if (p.votes) p.votes[off] = (uint8_t)vs;
               if (p.wmode != 0 && p.wvotes) p.wvotes[off] = wsum;
               if (p.bits && p.T == 32) p.bits[off] = s_bits[rb * (4 * BN) + tt * BN + col];
@@ -446,8 +451,8 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
       cnt = s_rowc[row] + s_rowc[128 + row];
       named_bar_sync(3, kEpi);
       if (half == 0 && row_ok) {
-        if (p.row_max) p.row_max[bh * p.N + qp] = m;
-        if (p.row_count && p.npass == 2) p.row_count[bh * p.N + qp] = cnt;
+        if (p.row_max) p.row_max[bh * p.Nq + (qp - p.qbase)] = m;
+        if (p.row_count && p.npass == 2) p.row_count[bh * p.Nq + (qp - p.qbase)] = cnt;
       }
     }
   }
@@ -480,13 +485,16 @@ int launch_select(const sta_select_args* a, cudaStream_t stream) {
     return fail(STA_ERR_ARG, "sta_select: weighted mode needs wvotes");
   if (a->n <= 0 || a->batch <= 0) return 0;
   if (a->n > (int64_t)1 << 30) return fail(STA_ERR_UNSUPPORTED, "sta_select: n too large");
+  if (a->q_pos_base < 0 || a->q_pos_base >= a->n || a->q_pos_base % BM)
+    return fail(STA_ERR_UNSUPPORTED, "sta_select: q_pos_base must be a multiple of 128 below n");
+  const int64_t nq = a->n - a->q_pos_base;
 
   const int64_t BH = a->batch * a->n_heads;
   const int64_t BHk = a->batch * a->n_kv_heads;
   CUtensorMap m_qhi, m_qlo, m_khi, m_klo;
   const int64_t qplanes = a->dca_chunk_len > 0 ? 3 : 1;  // DCA: intra / previous / older chunk Q
-  bool okm = make_tmap_bf16_3d(&m_qhi, a->q_hi, a->d, a->n, qplanes * BH, 64, BM) &&
-             make_tmap_bf16_3d(&m_qlo, a->q_lo, a->d, a->n, qplanes * BH, 64, BM) &&
+  bool okm = make_tmap_bf16_3d(&m_qhi, a->q_hi, a->d, nq, qplanes * BH, 64, BM) &&
+             make_tmap_bf16_3d(&m_qlo, a->q_lo, a->d, nq, qplanes * BH, 64, BM) &&
              make_tmap_bf16_3d(&m_khi, a->k_hi, a->d, a->n, BHk, 64, BN) &&
              make_tmap_bf16_3d(&m_klo, a->k_lo, a->d, a->n, BHk, 64, BN);
   if (!okm) return fail(STA_ERR_CUDA, "sta_select: cuTensorMapEncodeTiled failed");
@@ -496,8 +504,11 @@ int launch_select(const sta_select_args* a, cudaStream_t stream) {
   p.H = (int)a->n_heads;
   p.Hkv = (int)a->n_kv_heads;
   p.N = a->n;
+  p.Nq = nq;
+  p.qbase = a->q_pos_base;
+  p.qb0 = (int)(a->q_pos_base / BM);
   p.T = a->tile;
-  p.nqb = (int)((a->n + BM - 1) / BM);
+  p.nqb = (int)((nq + BM - 1) / BM);
   p.npass = a->max_only ? 1 : 2;
   p.wmode = a->max_only ? 0 : a->wmode;
   p.sm_scale = a->sm_scale;
@@ -508,7 +519,7 @@ int launch_select(const sta_select_args* a, cudaStream_t stream) {
   p.row_max = a->row_max;
   p.row_count = a->row_count;
   p.err = device_error_word();
-  p.head_stride = tri_head_stride(a->n, a->tile);
+  p.head_stride = tri_head_stride(a->n, a->tile, a->q_pos_base);
   p.dca_L = a->dca_chunk_len;
   if (p.dca_L > 0 && (p.dca_L % BN)) return fail(STA_ERR_UNSUPPORTED, "sta_select: DCA chunk_len must be a multiple of 256");
 

@@ -29,7 +29,7 @@ class SelectArgs(ctypes.Structure):
                 ("d", c_i32), ("tile", c_i32), ("sm_scale", c_f32), ("wmode", c_i32),
                 ("tau", c_vp), ("max_only", c_i32), ("votes", c_vp), ("wvotes", c_vp),
                 ("bits", c_vp), ("row_max", c_vp), ("row_count", c_vp),
-                ("dca_chunk_len", c_i32)]
+                ("dca_chunk_len", c_i32), ("q_pos_base", c_i64)]
 
 
 class BuildArgs(ctypes.Structure):
@@ -38,7 +38,8 @@ class BuildArgs(ctypes.Structure):
                 ("pct", c_f32), ("pos_scale", c_f32), ("select_score", c_i32),
                 ("measure", c_i32), ("idx", c_vp), ("newpos_k", c_vp), ("newpos_q", c_vp),
                 ("shared_size", c_vp), ("kept_size", c_vp), ("chosen", c_vp),
-                ("overflow", c_vp), ("kpct_meas", c_vp), ("overflow20", c_vp)]
+                ("overflow", c_vp), ("kpct_meas", c_vp), ("overflow20", c_vp),
+                ("q_pos_base", c_i64)]
 
 
 class BuildPQArgs(ctypes.Structure):
@@ -46,7 +47,7 @@ class BuildPQArgs(ctypes.Structure):
                 ("n", c_i64), ("tile", c_i32), ("k_max", c_i32), ("n_global", c_i32),
                 ("n_local", c_i32), ("select_score", c_i32), ("idx", c_vp),
                 ("newpos_k", c_vp), ("newpos_q", c_vp), ("mask", c_vp), ("usize", c_vp),
-                ("kept_size", c_vp), ("overflow", c_vp)]
+                ("kept_size", c_vp), ("overflow", c_vp), ("q_pos_base", c_i64)]
 
 
 class BuildChunkArgs(ctypes.Structure):
@@ -54,7 +55,7 @@ class BuildChunkArgs(ctypes.Structure):
                 ("tile", c_i32), ("k_max", c_i32), ("n_global", c_i32), ("n_local", c_i32),
                 ("chunk_size", c_i32), ("n_chunk", c_i32), ("select_score", c_i32),
                 ("chunk_agg", c_i32), ("idx", c_vp), ("newpos_k", c_vp), ("newpos_q", c_vp),
-                ("mask", c_vp), ("usize", c_vp), ("kept_size", c_vp)]
+                ("mask", c_vp), ("usize", c_vp), ("kept_size", c_vp), ("q_pos_base", c_i64)]
 
 
 class AttendArgs(ctypes.Structure):
@@ -68,7 +69,7 @@ class AttendArgs(ctypes.Structure):
                 ("rope_scale", c_f32), ("sm_scale", c_f32), ("q_hi", c_vp), ("q_lo", c_vp),
                 ("k_hi", c_vp), ("k_lo", c_vp), ("pos_scale_sel", c_f32),
                 ("same_geometry", c_i32), ("rope_table", c_vp), ("rope_table_R", c_f32),
-                ("rope_table_len", c_i64)]
+                ("rope_table_len", c_i64), ("q_pos_base", c_i64)]
 
 
 class PQStreamArgs(ctypes.Structure):
@@ -82,7 +83,7 @@ class PQStreamArgs(ctypes.Structure):
                 ("n_local", c_i32), ("inv_freq_c", c_vp), ("sm_scale", c_f32),
                 ("pos_advance", c_i32), ("use_skip", c_i32), ("rope_table", c_vp),
                 ("rope_table_R", c_f32), ("rope_table_len", c_i64), ("span", c_vp), ("kept", c_vp),
-                ("blocks", c_vp), ("skipped", c_vp)]
+                ("blocks", c_vp), ("skipped", c_vp), ("q_pos_base", c_i64)]
 
 
 class ForwardArgs(ctypes.Structure):
@@ -103,7 +104,7 @@ class ForwardArgs(ctypes.Structure):
                 ("newpos_q_out", c_vp), ("mask_out", c_vp), ("max_workspace_bytes", c_i64),
                 ("stage_events", c_vp), ("same_geometry", c_i32), ("chunk_size", c_i32),
                 ("n_chunk", c_i32), ("chunk_agg", c_i32), ("dca_chunk_size", c_i32),
-                ("dca_local_window", c_i32)]
+                ("dca_local_window", c_i32), ("q_pos_base", c_i64)]
 
 
 # every symbol include/sta.h declares (checked by the CPU test suite)
@@ -113,7 +114,7 @@ EXPORTED = ["sta_last_error", "sta_version", "sta_tri_head_stride", "sta_rope_sp
             "sta_pq_union_workspace_bytes", "sta_pq_union_forward",
             "sta_pq_stream_workspace_bytes", "sta_pq_stream_forward", "sta_device_error",
             "sta_shared_forward_static", "sta_build_sets_chunk", "sta_chunk_workspace_bytes",
-            "sta_chunk_forward", "sta_rope_split_dca", "sta_rope_table"]
+            "sta_chunk_forward", "sta_rope_split_dca", "sta_rope_table", "sta_tri_head_stride_q"]
 
 _lib = None
 
@@ -131,6 +132,8 @@ def lib():
     L.sta_version.restype = ctypes.c_int
     L.sta_tri_head_stride.restype = c_i64
     L.sta_tri_head_stride.argtypes = [c_i64, c_i32]
+    L.sta_tri_head_stride_q.restype = c_i64
+    L.sta_tri_head_stride_q.argtypes = [c_i64, c_i32, c_i64]
     L.sta_rope_split.restype = ctypes.c_int
     L.sta_rope_split.argtypes = [c_vp, c_i32, c_i64, c_i64, c_i32, c_i64, c_i64, c_vp, c_f32,
                                  c_f32, c_vp, c_vp, c_vp]

@@ -51,13 +51,14 @@ def _dev_f32(x, device):
     return x.to(device=device, dtype=torch.float32).contiguous()
 
 
-def _check_inputs(q, k, v):
+def _check_inputs(q, k, v, q_pos_base=0):
     if not (q.is_cuda and k.is_cuda and v.is_cuda):
         raise ValueError("q, k, v must be CUDA tensors (there is no CPU path)")
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
         raise ValueError("q, k, v must be (Z, H, N, D)")
-    Z, H, N, D = q.shape
-    if k.shape[0] != Z or v.shape != k.shape or k.shape[2] != N or k.shape[3] != D:
+    Z, H, Nq, D = q.shape
+    N = k.shape[2]
+    if k.shape[0] != Z or v.shape != k.shape or Nq + q_pos_base != N or k.shape[3] != D:
         raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
     if H % k.shape[1]:
         raise ValueError("number of q heads must be a multiple of the number of kv heads")
@@ -71,16 +72,24 @@ def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=
             pct=30.0, n_global=32, n_local=32, tile=32, k_max=1024, select_score="freq",
             measure=False, block_n=32, pos_advance="max", use_skip=True, keep_sets=False,
             max_workspace_bytes=0, stage_events=None, chunk_size=16, n_chunk=0,
-            chunk_agg="sum"):
-    """Run one prefill op.  variant: 'shared' | 'pq_union' | 'pq_stream'.
+            chunk_agg="sum", q_pos_base=0):
+    """Run one prefill op.  variant: 'shared' | 'pq_union' | 'pq_stream' | 'chunk'.
     q (Z,H,N,D); k, v (Z,Hkv,N,D) with H % Hkv == 0 (Hkv == H for repeat_kv-expanded input).
-    Returns (out (Z,H,N,D), dict of per-(head, tile) statistics [+ sets when keep_sets])."""
-    Z, H, Hk, N, D = _check_inputs(q, k, v)
+    q_pos_base > 0 (a multiple of 128): q holds only the queries at positions
+    q_pos_base..N-1 (a query slab, (Z,H,N-q_pos_base,D)); k / v hold all N keys and the
+    statistics cover the slab's tiles.  Every query tile is independent of the others, so slabs
+    reproduce the whole-sequence call exactly.
+    Returns (out (Z,H,Nq,D), dict of per-(head, tile) statistics [+ sets when keep_sets])."""
+    q_pos_base = int(q_pos_base)
+    if q_pos_base < 0 or q_pos_base % 128:
+        raise ValueError("q_pos_base must be a non-negative multiple of 128")
+    Z, H, Hk, N, D = _check_inputs(q, k, v, q_pos_base)
+    Nq = N - q_pos_base
     dev = q.device
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     T = int(tile)
-    nt = (N + T - 1) // T
+    nt = (Nq + T - 1) // T
     tau_d = _dev_f32(tau, dev).reshape(-1)
     if tau_d.numel() != H:
         raise ValueError(f"tau must have one entry per q head ({H}), got {tau_d.numel()}")
@@ -91,7 +100,7 @@ def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=
                                              gc.inv_freq.detach().float().cpu())))
     if ia.numel() != D // 2 or ic.numel() != D // 2:
         raise ValueError("inv_freq must have head_dim/2 entries")
-    out = torch.empty((Z, H, N, D), dtype=q.dtype, device=dev)
+    out = torch.empty((Z, H, Nq, D), dtype=q.dtype, device=dev)
     i32 = dict(dtype=torch.int32, device=dev)
     st = {}
     if variant == "shared":
@@ -109,7 +118,7 @@ def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=
     elif variant == "pq_stream":
         f32 = dict(dtype=torch.float32, device=dev)
         st["span"] = torch.empty((Z, H, nt), **f32)
-        st["kept"] = torch.empty((Z, H, N), **i32)
+        st["kept"] = torch.empty((Z, H, Nq), **i32)
         st["blocks"] = torch.empty((Z, H, nt), **f32)
         st["skipped"] = torch.empty((Z, H, nt), **f32)
     else:
@@ -175,6 +184,7 @@ def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=
                 a.mask_out = sets["mask"][b].data_ptr()
         a.max_workspace_bytes = int(max_workspace_bytes)
         a.same_geometry = same_geometry
+        a.q_pos_base = q_pos_base
         if ga.dca is not None:
             a.dca_chunk_size, a.dca_local_window = int(ga.dca[0]), int(ga.dca[1])
         if stage_events is not None:

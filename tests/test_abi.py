@@ -34,7 +34,8 @@ def test_struct_layouts_match_header_order():
     src = open(HEADER).read()
     for cname, cls in (("sta_select_args", L.SelectArgs), ("sta_build_args", L.BuildArgs),
                        ("sta_build_pq_args", L.BuildPQArgs), ("sta_attend_args", L.AttendArgs),
-                       ("sta_pqstream_args", L.PQStreamArgs), ("sta_forward_args", L.ForwardArgs)):
+                       ("sta_pqstream_args", L.PQStreamArgs), ("sta_forward_args", L.ForwardArgs),
+                       ("sta_build_chunk_args", L.BuildChunkArgs)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), src, re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
         fields = re.findall(r"\**\s*([A-Za-z_0-9]+)\s*;", body)
@@ -46,6 +47,36 @@ def test_tri_head_stride():
     for n, t in ((300, 64), (1024, 32), (1, 32), (131072, 32), (65536, 64)):
         nt = (n + t - 1) // t
         assert lib.sta_tri_head_stride(n, t) == t * (nt - 1) * nt // 2 + n
+
+
+def test_tri_head_stride_of_query_slabs():
+    """Compact layout of a query slab [base, n): local tile t holds keys j < base + (t+1)*T."""
+    lib = L.lib()
+    for n, t, base in ((1000, 64, 384), (131072, 32, 43904), (300, 32, 0), (1100, 64, 1024)):
+        nt = (n - base + t - 1) // t
+        his = [min(base + (i + 1) * t, n) for i in range(nt)]
+        assert lib.sta_tri_head_stride_q(n, t, base) == sum(his)
+    assert lib.sta_tri_head_stride_q(32768, 64, 0) == lib.sta_tri_head_stride(32768, 64)
+
+
+def test_slab_partition_balanced_and_exact_cover():
+    from sta.partition import plan, slab_edges
+    for n, parts in ((131072, 8), (32768, 2), (65536, 4), (1000, 3)):
+        e = slab_edges(n, parts, attend_weight=4096.0 if n > 4096 else 128.0)
+        assert e[0] == 0 and e[-1] == n and all(a < b for a, b in zip(e, e[1:]))
+        assert all(x % 128 == 0 for x in e[:-1])
+        if n >= 32768:
+            cost = [(b * b - a * a) / 2 + 4096.0 * (b - a) for a, b in zip(e, e[1:])]
+            assert max(cost) / min(cost) < 1.05, cost
+    for world, mode in ((8, "heads"), (8, "slabs"), (16, "grid"), (4, "grid"), (6, "auto")):
+        cover = {}
+        for r in range(world):
+            u = plan(8 if world != 6 else 6, 4096, world, r, mode)
+            for h in range(*u["kv"]):
+                for pos in range(*u["slab"]):
+                    cover[(h, pos)] = cover.get((h, pos), 0) + 1
+        hk = 8 if world != 6 else 6
+        assert len(cover) == hk * 4096 and set(cover.values()) == {1}, (world, mode)
 
 
 def test_null_arguments_rejected_without_gpu():

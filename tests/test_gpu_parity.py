@@ -475,3 +475,55 @@ def test_cfg2_fallback_clusters_vs_oracle():
         got = out[0, :, t * T:(t + 1) * T].float().cpu().numpy()
         err = np.abs(got - ref[:, t * T:(t + 1) * T])
         assert err.mean() <= BF16_MEAN and err.max() <= BF16_MAX, (t, err.max(), err.mean())
+
+
+SLAB_CASES = [
+    # variant, H, Hkv, N, D, T, dtype, geometry, extra kwargs
+    ("shared", 4, 2, 1000, 128, 64, torch.bfloat16, "yarn", {}),
+    ("shared", 2, 2, 700, 64, 32, torch.float32, "pi", {"select_score": "expmass"}),
+    ("shared", 4, 2, 1100, 128, 64, torch.bfloat16, "dca", {}),
+    ("pq_union", 4, 2, 900, 128, 32, torch.bfloat16, "yarn", {"select_score": "expmass"}),
+    ("pq_stream", 4, 2, 900, 128, 32, torch.bfloat16, "yarn", {"select_score": "expmass"}),
+    ("chunk", 2, 2, 800, 64, 32, torch.float32, "pi", {"n_chunk": 8}),
+]
+
+
+@pytest.mark.parametrize("case", SLAB_CASES, ids=[f"slab_{c[0]}_{c[7]}" for c in SLAB_CASES])
+def test_query_slabs_reproduce_whole_sequence(case):
+    """The single-sequence multi-GPU unit: slabs of query positions [s, e), each called with
+    k / v truncated to e keys and q_pos_base = s, reproduce the whole-sequence call bit for bit
+    (every query tile's result depends only on its own queries and the keys before them)."""
+    from sta.partition import slab_edges
+    variant, H, Hk, N, D, T, dt, geom, extra = case
+    q, k, v = make_inputs(SynthSpec(n_heads=H, n_kv_heads=Hk, seq_len=N, head_dim=D,
+                                    n_planted=16, seed=80, dtype=dt))
+    tau = torch.full((H,), 5.0)
+    if geom == "yarn":
+        invf, rs = yarn_inv_freq(D, 5e5, 4.0, 256)
+        ga = Geometry(invf, 1.0, rs)
+    elif geom == "dca":
+        invf, rs = rope_inv_freq(D, 1e4), 1.0
+        ga = Geometry(invf, 1.0, 1.05, (320, 64))
+    else:
+        invf, rs = rope_inv_freq(D, 1e4), 1.0
+        ga = Geometry(invf, 0.5, 1.0)
+    gc = Geometry(invf, 0.5 if geom != "yarn" else 1.0, rs) if variant == "shared" else \
+        Geometry(rope_inv_freq(D, 5e5 if geom == "yarn" else 1e4))
+    kw = dict(tile=T, k_max=256, keep_sets=variant != "pq_stream", **extra)
+    qd, kd, vd = cu(q), cu(k), cu(v)
+    out, st, sets = core.forward(variant, qd, kd, vd, tau, ga, gc, **kw)
+    edges = slab_edges(N, 3, attend_weight=128.0)
+    assert len(set(edges)) == 4 and all(e % 128 == 0 for e in edges[:-1])
+    for s0, s1 in zip(edges, edges[1:]):
+        o2, st2, sets2 = core.forward(variant, qd[:, :, s0:s1].contiguous(), kd[:, :, :s1],
+                                      vd[:, :, :s1], tau, ga, gc, q_pos_base=s0, **kw)
+        assert torch.equal(o2, out[:, :, s0:s1]), (s0, s1)
+        t0, t1 = s0 // T, (s1 + T - 1) // T
+        for name, x in st2.items():
+            ref = st[name][..., s0:s1] if name == "kept" else st[name][..., t0:t1]
+            assert torch.equal(x, ref), (name, s0, s1)
+        for name, x in sets2.items():
+            if name == "idx":  # padding sentinel = the call's key count
+                x = torch.where(x == s1, torch.full_like(x, N), x)
+            assert torch.equal(x, sets[name][:, :, t0:t1]), (name, s0, s1)
+    assert core.device_error() == 0

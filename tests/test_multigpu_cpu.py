@@ -1,8 +1,9 @@
 """Host-side multi-rank logic on CPU with the gloo backend (world size 2).
 
-The B200 op partitions a layer's kv heads across ranks with no data-path collective; the only
-collectives are the barrier and the max-over-ranks reduction of step times.  These tests run
-that partition + timing protocol on CPU ranks, including a rank that fails between steps.
+The B200 op partitions a layer across ranks by kv-head range and/or query slab
+(sta.partition) with no data-path collective; the only collectives are the barrier and the
+max-over-ranks reduction of step times.  These tests run that partition + timing protocol on
+CPU ranks, including a rank that fails between steps.
 """
 import os
 import socket
@@ -22,8 +23,9 @@ def _free_port():
 
 
 def partition(Hkv, G, world, rank):
-    """kv heads [k0, k1) and q heads [k0*G, k1*G) of rank `rank` (bench.py's rule)."""
-    k0, k1 = rank * Hkv // world, (rank + 1) * Hkv // world
+    """kv heads [k0, k1) and q heads [k0*G, k1*G) of rank `rank` (bench.py's head rule)."""
+    from sta.partition import kv_head_range
+    k0, k1 = kv_head_range(Hkv, world, rank)
     return (k0, k1), (k0 * G, k1 * G)
 
 
@@ -37,6 +39,13 @@ def _worker(rank, world, port, result_q, fail_rank):
         mine = torch.zeros(Hkv * G, dtype=torch.int64)
         mine[h0:h1] = 1
         dist.all_reduce(mine)                      # every q head covered exactly once
+        from sta.partition import plan
+        N, T = 131072, 32
+        cov = torch.zeros((Hkv, N // T), dtype=torch.int64)
+        u = plan(Hkv, N, world, rank, "slabs")     # single-sequence query-slab unit
+        cov[u["kv"][0]:u["kv"][1], u["slab"][0] // T:u["slab"][1] // T] = 1
+        dist.all_reduce(cov)
+        assert int(cov.min()) == 1 and int(cov.max()) == 1
         t = torch.tensor([10.0 + rank], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)   # max-over-ranks step time
         if rank == fail_rank:
