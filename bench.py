@@ -296,11 +296,13 @@ def run_gpu(args):
         torch.cuda.synchronize()
         barrier()
     ms_total = start.elapsed_time(end)
-    # the op runs once per batch element and the events bracket the last one: scale by B
+    # the op runs once per batch element and per group of kv heads (scratch cap); the events
+    # bracket the last group of the last element: scale by both counts
+    ngroups = int(st.get("kv_head_groups", 1))
     stage_ms = [0.0] * 4
     for row in evs:
         for j in range(4):
-            stage_ms[j] += B * row[j].elapsed_time(row[j + 1]) / K
+            stage_ms[j] += B * ngroups * row[j].elapsed_time(row[j + 1]) / K
     t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -354,7 +356,9 @@ def run_gpu(args):
             "tensor_flops_issued_per_launch": 3 * flops_sel,
             "note": "3 bf16 products per fp32-accurate score (hi*hi + hi*lo + lo*hi)"}
 
-    launches_per_step = {"shared": 5, "pq_union": 5, "pq_stream": 4}[args.variant]
+    # per op call: the cos/sin table, then per kv-head group the RoPE prologue of q and k (q in
+    # 3 planes for DCA), Kernel A, the selection and the attend (PQ-Stream: pass 2 fused)
+    per_group = {"shared": 4, "pq_union": 4, "pq_stream": 3}[args.variant] + (2 if geo.get("dca") else 0)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import torch as _t
@@ -376,7 +380,8 @@ def run_gpu(args):
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic (seeded generator sta.synth, BASELINE config shapes)",
                 "config": workload_desc(c, args, world, unit), "clocks": clocks, "e2e": e2e,
-                "gpu_launches": launches_per_step * K,
+                "gpu_launches": K * B * (1 + per_group * ngroups),
+                "kv_head_groups": ngroups,
                 "stage_ms": {"rope_prologue": stage_ms[0], "select_tcgen05": stage_ms[1],
                              "build_sets": stage_ms[2], "attend": stage_ms[3]},
                 "roofline": roof, "cpu_baseline": cpu, "selection": stats}

@@ -386,13 +386,17 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
               cnt += __popc(word);
               const uint32_t colw = transpose32(word);  // lane j: keep bits of column j, bit r = row r
               float myw = 0.f;
-              if (p.wmode != 0) {
+              // weighted votes only where some row of the warp keeps a key of this chunk (the
+              // kept sets are sparse: most chunks have none, and their sums are exactly 0)
+              if (p.wmode != 0 && __any_sync(0xffffffffu, word != 0u)) {
                 float wv[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                  const float sc = __fmul_rn(v[j], p.sm_scale);
-                  const float c = p.wmode == 1 ? __fsub_rn(sc, thr) : expf(__fsub_rn(sc, m));
-                  wv[j] = ((word >> j) & 1u) ? c : 0.f;
+                  wv[j] = 0.f;
+                  if ((word >> j) & 1u) {
+                    const float sc = __fmul_rn(v[j], p.sm_scale);
+                    wv[j] = p.wmode == 1 ? __fsub_rn(sc, thr) : expf(__fsub_rn(sc, m));
+                  }
                 }
                 myw = transpose_reduce32(wv);
               }

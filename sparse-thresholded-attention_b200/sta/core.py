@@ -193,6 +193,16 @@ def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=
         nbytes = fn_ws(ctypes.byref(a))
         if nbytes == 0:
             L.check(1, f"sta_{variant}_workspace_bytes")
+        if b == 0 and stage_events is not None:
+            # the stage events bracket the last group of kv heads: report the group count
+            cap = a.max_workspace_bytes
+            a.max_workspace_bytes = 0
+            full = fn_ws(ctypes.byref(a))
+            a.max_workspace_bytes = cap
+            groups = max(1, round(full / nbytes))
+            while Hk % groups:
+                groups += 1
+            st["kv_head_groups"] = groups
         if ws is None or ws.numel() < nbytes:
             ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         L.check(fn(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel()),
