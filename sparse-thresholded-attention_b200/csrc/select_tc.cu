@@ -43,7 +43,7 @@ struct Cfg {
   static constexpr int STAGE_BYTES = NC * kKTileBytes;
   static constexpr int NSTAGE = (D == 64) ? 4 : 2;
   static constexpr int RED_WORDS = 2 * 4 * BN;   // [buffer][quadrant][column]
-  static constexpr int SMEM = 1024 + Q_BYTES + NSTAGE * STAGE_BYTES + 3 * RED_WORDS * 4 + 2 * kEpi * 4 + 512;
+  static constexpr int SMEM = 1024 + Q_BYTES + NSTAGE * STAGE_BYTES + 2 * RED_WORDS * 4 + 2 * kEpi * 4 + 512;
 };
 
 struct Params {
@@ -152,8 +152,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
   uint8_t* sK = base + C::Q_BYTES;
   uint32_t* s_vote = reinterpret_cast<uint32_t*>(sK + C::NSTAGE * C::STAGE_BYTES);
   float* s_w = reinterpret_cast<float*>(s_vote + C::RED_WORDS);
-  uint32_t* s_bits = reinterpret_cast<uint32_t*>(s_w + C::RED_WORDS);
-  float* s_rowx = reinterpret_cast<float*>(s_bits + C::RED_WORDS);     // [2 halves][128 rows]
+  float* s_rowx = s_w + C::RED_WORDS;     // [2 halves][128 rows]
   int* s_rowc = reinterpret_cast<int*>(s_rowx + kEpi);                  // [2 halves][128 rows]
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_rowc + kEpi);
   uint64_t* q_full = bars;
@@ -392,18 +391,29 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
                 float wv[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                  wv[j] = 0.f;
-                  if ((word >> j) & 1u) {
-                    const float sc = __fmul_rn(v[j], p.sm_scale);
-                    wv[j] = p.wmode == 1 ? __fsub_rn(sc, thr) : expf(__fsub_rn(sc, m));
-                  }
+                  const float sc = __fmul_rn(v[j], p.sm_scale);
+                  const float c = p.wmode == 1 ? __fsub_rn(sc, thr) : expf(__fsub_rn(sc, m));
+                  wv[j] = ((word >> j) & 1u) ? c : 0.f;
                 }
                 myw = transpose_reduce32(wv);
               }
-              const int o = rb * (4 * BN) + quad * BN + ch * 32 + lane;
-              s_vote[o] = __popc(colw);
-              s_bits[o] = colw;
-              s_w[o] = myw;
+              if (p.T == 32) {
+                // a 32-query tile is exactly this warp's 32 rows: lane j already holds the
+                // tile's votes / bits / weighted vote of key kbase + j -- store them directly
+                const int64_t tg = q0 / 32 + quad;
+                const int64_t kj = kbase + lane;
+                if (tg < nt && kj < min((tg + 1) * 32, p.N)) {
+                  const int64_t off =
+                      bh * p.head_stride + tri_tile_offset(tg - p.qbase / 32, 32, p.qbase) + kj;
+                  if (p.votes) p.votes[off] = (uint8_t)__popc(colw);
+                  if (p.wmode != 0 && p.wvotes) p.wvotes[off] = myw;
+                  if (p.bits) p.bits[off] = colw;
+                }
+              } else {
+                const int o = rb * (4 * BN) + quad * BN + ch * 32 + lane;
+                s_vote[o] = __popc(colw);
+                s_w[o] = myw;
+              }
             }
             if (cc + 1 < BN / 64) {
               tmem_wait_ld();
@@ -413,8 +423,8 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
           }
           tc_fence_before();
           mbar_arrive(acc_empty + slot);
-          if (pass == 1) {
-            // combine the quadrants of each query tile, store compact votes / bits / wvotes
+          if (pass == 1 && p.T != 32) {
+            // combine the quadrants of each query tile, store compact votes / wvotes
             named_bar_sync(2, kEpi);
             const int col = threadIdx.x;  // kEpi == BN: one column per epilogue thread
             const int64_t kj = (int64_t)kb * BN + col;
@@ -434,7 +444,6 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
                   bh * p.head_stride + tri_tile_offset(tg - p.qbase / p.T, p.T, p.qbase) + kj;
               if (p.votes) p.votes[off] = (uint8_t)vs;
               if (p.wmode != 0 && p.wvotes) p.wvotes[off] = wsum;
-              if (p.bits && p.T == 32) p.bits[off] = s_bits[rb * (4 * BN) + tt * BN + col];
             }
             rb ^= 1;
           }
