@@ -12,12 +12,12 @@
 // bf16 tcgen05 products (hi*hi + hi*lo + lo*hi, fp32 accumulation in TMEM); both passes issue
 // the identical instruction sequence, so pass 2 reproduces pass 1's scores bit for bit.
 //
-// Roles (320 threads, one CTA per SM, persistent over a longest-first static schedule):
-//   warps 0-7  epilogue: warps w and w+4 share TMEM lane quadrant w%4 (rows 32(w%4)..+31) and
-//              split each block's 128 columns; row max in pass 1;
+// Roles (576 threads, one CTA per SM, persistent over a longest-first static schedule):
+//   warps 0-15 epilogue: warps w, w+4, w+8, w+12 share TMEM lane quadrant w%4 (rows
+//              32(w%4)..+31) and split each block's 256 columns; row max in pass 1;
 //              keep / warp-ballot votes / per-query bits / weighted votes in pass 2;
-//   warp 8     TMA producer (Q tile once per item, K blocks through an NSTAGE smem ring);
-//   warp 9     MMA issuer (one thread), M=128 N=256 K=16, 2 TMEM accumulator slots of 256
+//   warp 16    TMA producer (Q tile once per item, K blocks through an NSTAGE smem ring);
+//   warp 17    MMA issuer (one thread), M=128 N=256 K=16, 2 TMEM accumulator slots of 256
 //              columns; the K ring holds one bf16 piece (hi or lo) of a key block per stage.
 // All waits are bounded; on expiry the kernel records STA_ERR_TIMEOUT and unwinds.
 #include "common.cuh"
@@ -30,7 +30,12 @@ namespace {
 constexpr int BM = 128;       // query rows per item == TMEM lanes
 constexpr int BN = 256;       // keys per block == MMA N
 constexpr int NACC = 2;       // accumulator slots (2 x 256 fp32 columns = all 512 TMEM columns)
-constexpr int kEpi = 256;     // 8 epilogue warps: two per TMEM lane quadrant, splitting columns
+#ifndef STA_SELECT_EPI_WARPS
+#define STA_SELECT_EPI_WARPS 16
+#endif
+constexpr int kEpi = STA_SELECT_EPI_WARPS * 32;  // epilogue threads: kParts warps per TMEM lane
+constexpr int kParts = kEpi / 128;               // quadrant, each taking BN / kParts columns
+constexpr int kChunks = BN / 32 / kParts;        // 32-column chunks per warp and key block
 constexpr int kThreads = kEpi + 64;
 constexpr int kTileBytes = BM * 128;   // 128 query rows x 64 bf16 (one 128-byte swizzle chunk)
 constexpr int kKTileBytes = BN * 128;  // 256 key rows x 64 bf16
@@ -152,8 +157,8 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
   uint8_t* sK = base + C::Q_BYTES;
   uint32_t* s_vote = reinterpret_cast<uint32_t*>(sK + C::NSTAGE * C::STAGE_BYTES);
   float* s_w = reinterpret_cast<float*>(s_vote + C::RED_WORDS);
-  float* s_rowx = s_w + C::RED_WORDS;     // [2 halves][128 rows]
-  int* s_rowc = reinterpret_cast<int*>(s_rowx + kEpi);                  // [2 halves][128 rows]
+  float* s_rowx = s_w + C::RED_WORDS;                                  // [kParts][128 rows]
+  int* s_rowc = reinterpret_cast<int*>(s_rowx + kEpi);                  // [kParts][128 rows]
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_rowc + kEpi);
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 1;
@@ -314,12 +319,12 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
       }
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 0-3)
+    // ---------------------------------------------------------------- epilogue
     // Thread r owns accumulator row r.  Scores are compared in raw accumulator units against a
     // per-row threshold derived exactly (see raw_threshold), so no per-element scaling is
     // needed for the keep decision; pass 1 keeps the raw row max and scales it once.
     const int quad = warp & 3;             // TMEM lane quadrant
-    const int half = warp >> 2;            // which two of the block's four 32-column chunks
+    const int part = warp >> 2;            // which kChunks of the block's eight 32-column chunks
     const int row = quad * 32 + lane;
     const int64_t nt = (p.N + p.T - 1) / p.T;
     const int tiles_per_item = BM / p.T;
@@ -354,13 +359,21 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
           }
           tc_fence_after();
           const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + slot * BN;
-          float v[32], vn[32];
-          tmem_ld32(taddr + half * (BN / 2), v);
+          // with 8 epilogue warps the next chunk's load is kept in flight (vn); with 16 the
+          // other warps of the quadrant hide its latency and the registers go to occupancy
+          constexpr bool kPrefetch = kParts <= 2;
+          float v[32], vn[32];  // vn unused (eliminated) without prefetch
+          tmem_ld32(taddr + part * (BN / kParts), v);
           tmem_wait_ld();
 #pragma unroll 1
-          for (int cc = 0; cc < BN / 64; ++cc) {
-            const int ch = half * (BN / 64) + cc;
-            if (cc + 1 < BN / 64) tmem_ld32(taddr + (ch + 1) * 32, vn);  // next chunk in flight
+          for (int cc = 0; cc < kChunks; ++cc) {
+            const int ch = part * kChunks + cc;
+            if constexpr (kPrefetch) {
+              if (cc + 1 < kChunks) tmem_ld32(taddr + (ch + 1) * 32, vn);  // next chunk in flight
+            } else if (cc > 0) {
+              tmem_ld32(taddr + ch * 32, v);
+              tmem_wait_ld();
+            }
             const int64_t kbase = (int64_t)kb * BN + ch * 32;
             // causal mask of this row over the chunk's 32 keys (all ones off the diagonal)
             const int64_t lim = qp - kbase;
@@ -388,14 +401,14 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
               // weighted votes only where some row of the warp keeps a key of this chunk (the
               // kept sets are sparse: most chunks have none, and their sums are exactly 0)
               if (p.wmode != 0 && __any_sync(0xffffffffu, word != 0u)) {
-                float wv[32];
+                // v is not read again for this chunk: reuse it for the per-key weights
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                   const float sc = __fmul_rn(v[j], p.sm_scale);
                   const float c = p.wmode == 1 ? __fsub_rn(sc, thr) : expf(__fsub_rn(sc, m));
-                  wv[j] = ((word >> j) & 1u) ? c : 0.f;
+                  v[j] = ((word >> j) & 1u) ? c : 0.f;
                 }
-                myw = transpose_reduce32(wv);
+                myw = transpose_reduce32(v);
               }
               if (p.T == 32) {
                 // a 32-query tile is exactly this warp's 32 rows: lane j already holds the
@@ -415,10 +428,12 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
                 s_w[o] = myw;
               }
             }
-            if (cc + 1 < BN / 64) {
-              tmem_wait_ld();
+            if constexpr (kPrefetch) {
+              if (cc + 1 < kChunks) {
+                tmem_wait_ld();
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = vn[j];
+                for (int j = 0; j < 32; ++j) v[j] = vn[j];
+              }
             }
           }
           tc_fence_before();
@@ -426,9 +441,9 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
           if (pass == 1 && p.T != 32) {
             // combine the quadrants of each query tile, store compact votes / wvotes
             named_bar_sync(2, kEpi);
-            const int col = threadIdx.x;  // kEpi == BN: one column per epilogue thread
+            const int col = threadIdx.x % BN;  // kEpi / BN threads per column split the tiles
             const int64_t kj = (int64_t)kb * BN + col;
-            for (int tt = 0; tt < tiles_per_item; ++tt) {
+            for (int tt = threadIdx.x / BN; tt < tiles_per_item; tt += kEpi / BN) {
               const int64_t tg = q0 / p.T + tt;
               if (tg >= nt) break;
               const int64_t hi_t = min((tg + 1) * (int64_t)p.T, p.N);
@@ -451,19 +466,22 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
         if (!ok) break;
         if (pass == 0) {
           // the two column halves of each row meet: exact row max, then scale once
-          s_rowx[half * 128 + row] = mraw;
+          s_rowx[part * 128 + row] = mraw;
           named_bar_sync(3, kEpi);
-          mraw = fmaxf(s_rowx[row], s_rowx[128 + row]);
+#pragma unroll
+          for (int q2 = 0; q2 < kParts; ++q2) mraw = fmaxf(mraw, s_rowx[q2 * 128 + row]);
           named_bar_sync(3, kEpi);
           m = __fmul_rn(mraw, p.sm_scale);  // scaling is monotone: max commutes with it
         }
       }
       if (!ok) break;
-      s_rowc[half * 128 + row] = cnt;
+      s_rowc[part * 128 + row] = cnt;
       named_bar_sync(3, kEpi);
-      cnt = s_rowc[row] + s_rowc[128 + row];
+      cnt = 0;
+#pragma unroll
+      for (int q2 = 0; q2 < kParts; ++q2) cnt += s_rowc[q2 * 128 + row];
       named_bar_sync(3, kEpi);
-      if (half == 0 && row_ok) {
+      if (part == 0 && row_ok) {
         if (p.row_max) p.row_max[bh * p.Nq + (qp - p.qbase)] = m;
         if (p.row_count && p.npass == 2) p.row_count[bh * p.Nq + (qp - p.qbase)] = cnt;
       }
