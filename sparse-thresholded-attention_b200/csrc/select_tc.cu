@@ -98,18 +98,6 @@ __device__ __forceinline__ float transpose_reduce32(float (&v)[32]) {
   return v[0];
 }
 
-// OR of `pred` over the `n` threads that arrive at named barrier `id` (a barrier itself)
-__device__ __forceinline__ int bar_red_or(int id, int n, int pred) {
-  int r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.b32 p, %1, 0;\n\t"
-      "barrier.cta.red.or.pred q, %2, %3, p;\n\t"
-      "selp.s32 %0, 1, 0, q;\n\t}"
-      : "=r"(r) : "r"(pred), "r"(id), "r"(n) : "memory");
-  return r;
-}
-
 // 32 x 32 bit-matrix transpose across the warp: on entry lane r holds row r (bit c = M[r][c]);
 // on exit lane c holds column c (bit r = M[r][c]).  Five block-swap rounds, one shuffle each.
 __device__ __forceinline__ uint32_t transpose32(uint32_t x) {
@@ -327,12 +315,13 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
     const int part = warp >> 2;            // which kChunks of the block's eight 32-column chunks
     const int row = quad * 32 + lane;
     const int64_t nt = (p.N + p.T - 1) / p.T;
-    const int tiles_per_item = BM / p.T;
     const int quads_per_tile = p.T / 32;
     uint32_t ac = 0;
     int rb = 0;
     bool ok = true;
-    for (int64_t w = blockIdx.x; w < total && ok; w += gridDim.x) {
+    // After a failed wait (ok == false) a warp keeps walking the same schedule without touching
+    // TMEM or memory, so every epilogue warp still reaches every named barrier.
+    for (int64_t w = blockIdx.x; w < total; w += gridDim.x) {
       int64_t bh, kvh;
       int qb;
       decode_item(w, p, bh, qb, kvh);
@@ -343,7 +332,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
       const int nb = qb / 2 + 1;
       float mraw = -INFINITY, m = -INFINITY, thr = -INFINITY, thr_raw = INFINITY;
       int cnt = 0;
-      for (int pass = 0; pass < p.npass && ok; ++pass) {
+      for (int pass = 0; pass < p.npass; ++pass) {
         if (pass == 1) {
           thr = __fsub_rn(m, tau_h);
           thr_raw = row_ok ? raw_threshold(thr, p.sm_scale) : INFINITY;
@@ -351,106 +340,103 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
         for (int kb = 0; kb < nb; ++kb, ++ac) {
           const uint32_t slot = ac % NACC, use = ac / NACC;
           int bad = 0;
-          if (lane == 0) bad = !mbar_wait(acc_full + slot, use & 1, s_abort, p.err, kErrTimeoutAcc);
-          // one collective decision for all epilogue warps, so none is left at a named barrier
-          if (bar_red_or(1, kEpi, bad)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + slot * BN;
-          // with 8 epilogue warps the next chunk's load is kept in flight (vn); with 16 the
-          // other warps of the quadrant hide its latency and the registers go to occupancy
-          constexpr bool kPrefetch = kParts <= 2;
-          float v[32], vn[32];  // vn unused (eliminated) without prefetch
-          tmem_ld32(taddr + part * (BN / kParts), v);
-          tmem_wait_ld();
+          if (ok && lane == 0) bad = !mbar_wait(acc_full + slot, use & 1, s_abort, p.err, kErrTimeoutAcc);
+          if (__shfl_sync(0xffffffffu, bad, 0)) ok = false;
+          if (ok) {
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + slot * BN;
+            // with 8 epilogue warps the next chunk's load is kept in flight (vn); with 16 the
+            // other warps of the quadrant hide its latency and the registers go to occupancy
+            constexpr bool kPrefetch = kParts <= 2;
+            float v[32], vn[32];  // vn unused (eliminated) without prefetch
+            tmem_ld32(taddr + part * (BN / kParts), v);
+            tmem_wait_ld();
 #pragma unroll 1
-          for (int cc = 0; cc < kChunks; ++cc) {
-            const int ch = part * kChunks + cc;
-            if constexpr (kPrefetch) {
-              if (cc + 1 < kChunks) tmem_ld32(taddr + (ch + 1) * 32, vn);  // next chunk in flight
-            } else if (cc > 0) {
-              tmem_ld32(taddr + ch * 32, v);
-              tmem_wait_ld();
-            }
-            const int64_t kbase = (int64_t)kb * BN + ch * 32;
-            // causal mask of this row over the chunk's 32 keys (all ones off the diagonal)
-            const int64_t lim = qp - kbase;
-            const uint32_t cmask = lim >= 31 ? 0xffffffffu : (lim < 0 ? 0u : ((2u << lim) - 1u));
-            if (pass == 0) {
-              float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-              if (cmask == 0xffffffffu) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) m4[j & 3] = fmaxf(m4[j & 3], v[j]);
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  m4[j & 3] = fmaxf(m4[j & 3], ((cmask >> j) & 1u) ? v[j] : -INFINITY);
-              }
-              mraw = fmaxf(mraw, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
-            } else {
-              uint32_t w4[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-              for (int j = 0; j < 32; ++j) w4[j & 3] |= (v[j] >= thr_raw ? 1u : 0u) << j;
-              uint32_t word = ((w4[0] | w4[1]) | (w4[2] | w4[3])) & cmask;
-              if (!row_ok) word = 0;
-              cnt += __popc(word);
-              const uint32_t colw = transpose32(word);  // lane j: keep bits of column j, bit r = row r
-              float myw = 0.f;
-              // weighted votes only where some row of the warp keeps a key of this chunk (the
-              // kept sets are sparse: most chunks have none, and their sums are exactly 0)
-              if (p.wmode != 0 && __any_sync(0xffffffffu, word != 0u)) {
-                // v is not read again for this chunk: reuse it for the per-key weights
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                  const float sc = __fmul_rn(v[j], p.sm_scale);
-                  const float c = p.wmode == 1 ? __fsub_rn(sc, thr) : expf(__fsub_rn(sc, m));
-                  v[j] = ((word >> j) & 1u) ? c : 0.f;
-                }
-                myw = transpose_reduce32(v);
-              }
-              if (p.T == 32) {
-                // a 32-query tile is exactly this warp's 32 rows: lane j already holds the
-                // tile's votes / bits / weighted vote of key kbase + j -- store them directly
-                const int64_t tg = q0 / 32 + quad;
-                const int64_t kj = kbase + lane;
-                if (tg < nt && kj < min((tg + 1) * 32, p.N)) {
-                  const int64_t off =
-                      bh * p.head_stride + tri_tile_offset(tg - p.qbase / 32, 32, p.qbase) + kj;
-                  if (p.votes) p.votes[off] = (uint8_t)__popc(colw);
-                  if (p.wmode != 0 && p.wvotes) p.wvotes[off] = myw;
-                  if (p.bits) p.bits[off] = colw;
-                }
-              } else {
-                const int o = rb * (4 * BN) + quad * BN + ch * 32 + lane;
-                s_vote[o] = __popc(colw);
-                s_w[o] = myw;
-              }
-            }
-            if constexpr (kPrefetch) {
-              if (cc + 1 < kChunks) {
+            for (int cc = 0; cc < kChunks; ++cc) {
+              const int ch = part * kChunks + cc;
+              if constexpr (kPrefetch) {
+                if (cc + 1 < kChunks) tmem_ld32(taddr + (ch + 1) * 32, vn);  // next chunk in flight
+              } else if (cc > 0) {
+                tmem_ld32(taddr + ch * 32, v);
                 tmem_wait_ld();
+              }
+              const int64_t kbase = (int64_t)kb * BN + ch * 32;
+              // causal mask of this row over the chunk's 32 keys (all ones off the diagonal)
+              const int64_t lim = qp - kbase;
+              const uint32_t cmask = lim >= 31 ? 0xffffffffu : (lim < 0 ? 0u : ((2u << lim) - 1u));
+              if (pass == 0) {
+                float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                if (cmask == 0xffffffffu) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = vn[j];
+                  for (int j = 0; j < 32; ++j) m4[j & 3] = fmaxf(m4[j & 3], v[j]);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    m4[j & 3] = fmaxf(m4[j & 3], ((cmask >> j) & 1u) ? v[j] : -INFINITY);
+                }
+                mraw = fmaxf(mraw, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+              } else {
+                uint32_t w4[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+                for (int j = 0; j < 32; ++j) w4[j & 3] |= (v[j] >= thr_raw ? 1u : 0u) << j;
+                uint32_t word = ((w4[0] | w4[1]) | (w4[2] | w4[3])) & cmask;
+                if (!row_ok) word = 0;
+                cnt += __popc(word);
+                const uint32_t colw = transpose32(word);  // lane j: keep bits of column j, bit r = row r
+                float myw = 0.f;
+                // weighted votes only where some row of the warp keeps a key of this chunk (the
+                // kept sets are sparse: most chunks have none, and their sums are exactly 0)
+                if (p.wmode != 0 && __any_sync(0xffffffffu, word != 0u)) {
+                  // v is not read again for this chunk: reuse it for the per-key weights
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) {
+                    const float sc = __fmul_rn(v[j], p.sm_scale);
+                    const float c = p.wmode == 1 ? __fsub_rn(sc, thr) : expf(__fsub_rn(sc, m));
+                    v[j] = ((word >> j) & 1u) ? c : 0.f;
+                  }
+                  myw = transpose_reduce32(v);
+                }
+                if (p.T == 32) {
+                  // a 32-query tile is exactly this warp's 32 rows: lane j already holds the
+                  // tile's votes / bits / weighted vote of key kbase + j -- store them directly
+                  const int64_t tg = q0 / 32 + quad;
+                  const int64_t kj = kbase + lane;
+                  if (tg < nt && kj < min((tg + 1) * 32, p.N)) {
+                    const int64_t off =
+                        bh * p.head_stride + tri_tile_offset(tg - p.qbase / 32, 32, p.qbase) + kj;
+                    if (p.votes) p.votes[off] = (uint8_t)__popc(colw);
+                    if (p.wmode != 0 && p.wvotes) p.wvotes[off] = myw;
+                    if (p.bits) p.bits[off] = colw;
+                  }
+                } else {
+                  const int o = rb * (4 * BN) + quad * BN + ch * 32 + lane;
+                  s_vote[o] = __popc(colw);
+                  s_w[o] = myw;
+                }
+              }
+              if constexpr (kPrefetch) {
+                if (cc + 1 < kChunks) {
+                  tmem_wait_ld();
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] = vn[j];
+                }
               }
             }
-          }
-          tc_fence_before();
-          mbar_arrive(acc_empty + slot);
+            tc_fence_before();
+            mbar_arrive(acc_empty + slot);
+          }  // ok
           if (pass == 1 && p.T != 32) {
-            // combine the quadrants of each query tile, store compact votes / wvotes
-            named_bar_sync(2, kEpi);
-            const int col = threadIdx.x % BN;  // kEpi / BN threads per column split the tiles
+            // combine the quadrants of each query tile and store compact votes / wvotes: the
+            // warps of one tile's quadrants meet at their own barrier (ids 4, 5)
+            const int g = quad / quads_per_tile;                 // == tile of the item
+            named_bar_sync(4 + g, quads_per_tile * kParts * 32);
+            const int col = (part * quads_per_tile + quad % quads_per_tile) * 32 + lane;
+            const int64_t tg = q0 / p.T + g;
             const int64_t kj = (int64_t)kb * BN + col;
-            for (int tt = threadIdx.x / BN; tt < tiles_per_item; tt += kEpi / BN) {
-              const int64_t tg = q0 / p.T + tt;
-              if (tg >= nt) break;
-              const int64_t hi_t = min((tg + 1) * (int64_t)p.T, p.N);
-              if (kj >= hi_t) continue;
+            if (ok && col < BN && tg < nt && kj < min((tg + 1) * (int64_t)p.T, p.N)) {
               uint32_t vs = 0;
               float wsum = 0.f;
-              for (int qq = tt * quads_per_tile; qq < (tt + 1) * quads_per_tile; ++qq) {
+              for (int qq = g * quads_per_tile; qq < (g + 1) * quads_per_tile; ++qq) {
                 const int o = rb * (4 * BN) + qq * BN + col;
                 vs += s_vote[o];
                 wsum += s_w[o];
@@ -463,7 +449,6 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             rb ^= 1;
           }
         }
-        if (!ok) break;
         if (pass == 0) {
           // the two column halves of each row meet: exact row max, then scale once
           s_rowx[part * 128 + row] = mraw;
@@ -474,14 +459,13 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
           m = __fmul_rn(mraw, p.sm_scale);  // scaling is monotone: max commutes with it
         }
       }
-      if (!ok) break;
       s_rowc[part * 128 + row] = cnt;
       named_bar_sync(3, kEpi);
       cnt = 0;
 #pragma unroll
       for (int q2 = 0; q2 < kParts; ++q2) cnt += s_rowc[q2 * 128 + row];
       named_bar_sync(3, kEpi);
-      if (part == 0 && row_ok) {
+      if (ok && part == 0 && row_ok) {
         if (p.row_max) p.row_max[bh * p.Nq + (qp - p.qbase)] = m;
         if (p.row_count && p.npass == 2) p.row_count[bh * p.Nq + (qp - p.qbase)] = cnt;
       }
