@@ -358,7 +358,7 @@ def run_gpu(args):
 
     # per op call: the cos/sin table, then per kv-head group the RoPE prologue of q and k (q in
     # 3 planes for DCA), Kernel A, the selection and the attend (PQ-Stream: pass 2 fused)
-    per_group = {"shared": 4, "pq_union": 4, "pq_stream": 3}[args.variant] + (2 if geo.get("dca") else 0)
+    per_group = {"shared": 5, "pq_union": 5, "pq_stream": 4}[args.variant] + (2 if geo.get("dca") else 0)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import torch as _t
@@ -373,6 +373,16 @@ def run_gpu(args):
                  "overflow_frac": float(st["overflow"].float().mean()),
                  "unresolved_frac": float(st["overflow20"].float().mean()),
                  "fallback_tiles": int(((st["chosen"] > 0) & (st["chosen"] < 30)).sum())}
+    elif args.variant == "pq_union":
+        stats = {"mean_usize": float(st["usize"].float().mean()),
+                 "mean_kept_size": float(st["kept_size"].float().mean()),
+                 "overflow_frac": float(st["overflow"].float().mean())}
+    else:
+        used = (st["blocks"] - st["skipped"]).float()
+        stats = {"mean_kept_per_query": float(st["kept"].float().mean()),
+                 "mean_blocks_per_tile": float(st["blocks"].float().mean()),
+                 "mean_advancing_blocks_per_tile": float(used.mean()),
+                 "mean_span": float(st["span"].float().mean())}
     clocks = clk.summary()
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,

@@ -113,6 +113,13 @@ typedef struct sta_select_args {
    * keys, and row_max / row_count are (batch*n_heads, n - q_pos_base); compact arrays use the
    * layout of sta_tri_head_stride_q */
   int64_t q_pos_base;
+  /* optional (tile 32, 2 passes): per (tile, key block) the maximum over the tile's queries of
+   * the number of kept keys in the block -- the PQ-Stream advance before forced keys.  Blocks
+   * of block_max_bn (32 or 64) keys; tile t holds ceil(hi_t / 32) bytes at offset
+   * t*(q_pos_base/32) + t*(t+1)/2, heads sta_tri_head_stride_q(ceil(n/32), 1, q_pos_base/32)
+   * apart; a 64-key block's entry sits at its first 32-key index. */
+  uint8_t* block_max;
+  int32_t block_max_bn;
 } sta_select_args;
 
 int sta_select(const sta_select_args* a, void* stream);
@@ -257,9 +264,9 @@ typedef struct sta_attend_args {
 int sta_gather_attend(const sta_attend_args* a, void* stream);
 
 /* ---------------------------------------------------------------------------------------
- * PQ-Stream pass 2 (fused select + streamed positions + attend, descending key blocks).
- * Together with sta_select(max_only=1) this replaces _pqstream_kernel
- * (pqstream_kernel.py:174-368).
+ * PQ-Stream pass 2 (streamed positions + attend over the kept keys, descending key blocks).
+ * Together with sta_select (2 passes, tile 32, bits + block_max + row_count) this replaces
+ * _pqstream_kernel (pqstream_kernel.py:174-368).
  * ------------------------------------------------------------------------------------- */
 typedef struct sta_pqstream_args {
   const void* q; int64_t q_stride_h; int64_t q_stride_n;
@@ -274,9 +281,10 @@ typedef struct sta_pqstream_args {
   int32_t d;
   int32_t tile;            /* 32 */
   int32_t block_n;         /* 32 or 64 */
-  const void* q_hi; const void* q_lo; const void* k_hi; const void* k_lo;  /* select geometry */
-  const float* row_max;    /* (batch*n_heads, n) from sta_select(max_only=1) */
-  const float* tau;        /* (n_heads,) */
+  /* keep decisions of the selection geometry, from sta_select (2 passes, tile 32): */
+  const uint32_t* bits;    /* compact per-query keep bits */
+  const uint8_t* block_max;/* block maxima with block_max_bn == block_n */
+  const int32_t* row_count;/* (batch*n_heads, n - q_pos_base) kept keys per query */
   int32_t n_global;
   int32_t n_local;
   const float* inv_freq_c; /* attend geometry: base RoPE, rope_scale 1 */
@@ -288,10 +296,10 @@ typedef struct sta_pqstream_args {
   float rope_table_R;
   int64_t rope_table_len;
   float* span;             /* (heads, nt) */
-  int32_t* kept;           /* (heads, n) */
+  int32_t* kept;           /* (heads, n - q_pos_base) */
   float* blocks;           /* (heads, nt) */
   float* skipped;          /* (heads, nt) */
-  int64_t q_pos_base;      /* as sta_attend_args; row_max / kept are (heads, n - q_pos_base) */
+  int64_t q_pos_base;      /* as sta_attend_args */
 } sta_pqstream_args;
 
 int sta_pqstream_attend(const sta_pqstream_args* a, void* stream);

@@ -92,7 +92,7 @@ inline size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
   int64_t c;          // kv heads per group
-  size_t qh, ql, kh, kl, votes, wvotes, bits, idx, npk, npq, mask, rowmax, rtab, total;
+  size_t qh, ql, kh, kl, votes, wvotes, bits, idx, npk, npq, mask, rowcnt, bmax, rtab, total;
   float rtab_R;
   int64_t rtab_len;
 };
@@ -121,7 +121,10 @@ Layout layout_for(const sta_forward_args* a, Variant v, int64_t c) {
   L.kh = take(c * N * D * 2);
   L.kl = take(c * N * D * 2);
   if (v == kPQStream) {
-    L.rowmax = take(qh * Nq * 4);
+    // Kernel A's keep bits, block maxima and per-query counts feed the streaming pass
+    L.bits = take(qh * HS * 4);
+    L.bmax = take(qh * tri_head_stride((N + 31) / 32, 1, a->q_pos_base / 32));
+    L.rowcnt = take(qh * Nq * 4);
   } else {
     L.votes = take(qh * HS);
     if (a->select_score != STA_SCORE_FREQ) L.wvotes = take(qh * HS * 4);
@@ -280,8 +283,10 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       s.q_pos_base = qbase;
       mark(1);
       if (v == kPQStream) {
-        s.max_only = 1;
-        s.row_max = reinterpret_cast<float*>(w + L.rowmax);
+        s.bits = reinterpret_cast<uint32_t*>(w + L.bits);
+        s.block_max = w + L.bmax;
+        s.block_max_bn = a->block_n;
+        s.row_count = reinterpret_cast<int32_t*>(w + L.rowcnt);
         STA_TRY(launch_select(&s, st));
         mark(2);
         sta_pqstream_args pa{};
@@ -297,9 +302,9 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
         pa.d = a->d;
         pa.tile = 32;
         pa.block_n = a->block_n;
-        pa.q_hi = w + L.qh; pa.q_lo = w + L.ql; pa.k_hi = w + L.kh; pa.k_lo = w + L.kl;
-        pa.row_max = reinterpret_cast<float*>(w + L.rowmax);
-        pa.tau = tau;
+        pa.bits = reinterpret_cast<uint32_t*>(w + L.bits);
+        pa.block_max = w + L.bmax;
+        pa.row_count = reinterpret_cast<int32_t*>(w + L.rowcnt);
         pa.n_global = a->n_global;
         pa.n_local = a->n_local;
         pa.inv_freq_c = a->inv_freq_c;

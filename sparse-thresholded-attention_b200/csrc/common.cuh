@@ -221,6 +221,21 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
+// 32 x 32 bit-matrix transpose across the warp: on entry lane r holds row r (bit c = M[r][c]);
+// on exit lane c holds column c (bit r = M[r][c]).  Five block-swap rounds, one shuffle each.
+__device__ __forceinline__ uint32_t transpose32(uint32_t x) {
+  const int l = lane_id();
+  const uint32_t lo_masks[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    const int s = 16 >> i;
+    const uint32_t lo = lo_masks[i], hi = ~lo;
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, x, s);
+    x = (l & s) ? ((x & hi) | ((y & hi) >> s)) : ((x & lo) | ((y & lo) << s));
+  }
+  return x;
+}
+
 // Compact (lower-triangular) layout of per-(head, tile, key) selection arrays.  The queries
 // are the positions [base, N) (base = q_pos_base, 0 for a whole-sequence prefill); local query
 // tile t only has entries for keys j < hi_t = min(base + (t+1)*T, N), so it starts at

@@ -1,15 +1,17 @@
-// PQ-Stream, pass 2: per-query threshold selection with streamed block positions, fused with
-// the attention over the kept keys.
+// PQ-Stream, pass 2: streamed block positions and the attention over the kept keys.
 //
-// Reference: _pqstream_kernel, pqstream_kernel.py:174-368 (pass 2 is :251-358).  Pass 1 (exact
-// row max under the selection geometry) is sta_select(max_only=1) on the tensor cores; this
-// kernel reads its row maxima.  Per (head, 32-query tile), key blocks of block_n are visited in
-// DESCENDING order; for each block:
-//   s_sel = (Qsel . Ksel) * sm_scale   (selection geometry, pre-rotated hi/lo operands)
-//   keep  = (s_sel >= m - tau | forced) & causal & row < N & key < N
+// Reference: _pqstream_kernel, pqstream_kernel.py:174-368 (pass 2 is :251-358).  The reference
+// rescores every causal key block of every 32-query tile inside the streaming loop.  Here the
+// keep decisions come from the tensor-core Kernel A (sta_select, 2 passes, per-query keep bits
+// of each (tile, key) -- the same exact-max threshold test), and this kernel only streams:
+// per (head, 32-query tile), key blocks of block_n are taken in DESCENDING order and
+//   keep  = (bit | forced) & causal & row < N & key < N
 //   c_i   = sum_j keep ; adv = max_i c_i (or the block's occupied slot count, ADV_FULL)
-//   if adv > 0 (or skipping disabled): keys rotated with base RoPE at npk = -(d + o_j),
-//     o_j = hi_t - j, queries at npq = qpos - P_top; online softmax + PV; d += adv.
+//   d_b   = sum of adv over the blocks above b (exact: integers in fp32)
+// then the blocks holding any kept key are attended in the same order: keys rotated with base
+// RoPE at npk = -(d_b + o_j), o_j = hi_t - j, queries at npq = qpos - P_top; online softmax +
+// PV.  Blocks without kept keys change no softmax state, so visiting only the blocks with keeps
+// is exact; the skip rule (adv == 0) only decides the `skipped` statistic and d.
 // Outputs: out, span (= final d), kept (per-query kept count), blocks, skipped.
 #include "common.cuh"
 #include "mma_frag.cuh"
@@ -35,9 +37,11 @@ struct PQSP {
   int64_t BH, N, nt;
   int64_t qbase, Nq;  // queries: positions qbase .. N-1, held as rows 0 .. Nq-1
   int H, Hkv;
-  const __nv_bfloat16 *qh, *ql, *kh, *kl;
-  const float* row_max;
-  const float* tau;
+  const uint32_t* bits;
+  int64_t head_stride;       // compact bits
+  const uint8_t* bmax;
+  int64_t bmax_stride;       // compact block maxima (entries of 32 keys)
+  const int32_t* row_count;
   int n_global, n_local;
   const float* inv_freq_c;
   float sm_scale;
@@ -91,6 +95,28 @@ __device__ __forceinline__ void score_tile(const __nv_bfloat16* sA, const __nv_b
   }
 }
 
+// exclusive prefix sum over the CTA's NTH threads (2 warps); total returned in `total`
+__device__ __forceinline__ int cta_excl_sum(int x, int* sh, int& total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int inc = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) sh[w] = inc;
+  __syncthreads();
+  int base = 0;
+  total = 0;
+#pragma unroll
+  for (int i = 0; i < NW; ++i) {
+    if (i < w) base += sh[i];
+    total += sh[i];
+  }
+  __syncthreads();
+  return base + inc - x;
+}
+
 template <int D, int BN, bool F32>
 __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   using TV = typename std::conditional<F32, float, __nv_bfloat16>::type;
@@ -99,12 +125,16 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   constexpr int NQ = F32 ? 3 : 2;  // pieces of the attend-geometry Q / K
   constexpr int NV = F32 ? 3 : 1;  // pieces of P / V
   extern __shared__ __align__(16) uint8_t smem[];
-  __nv_bfloat16* sQs = reinterpret_cast<__nv_bfloat16*>(smem);  // [2][T][LD] select geometry
-  __nv_bfloat16* sQa = sQs + 2 * T * LD;                         // [NQ][T][LD] attend geometry
-  __nv_bfloat16* sKs = sQa + NQ * T * LD;                        // [2][BN][LD]
-  __nv_bfloat16* sKa = sKs + 2 * BN * LD;                        // [NQ][BN][LD]
-  __nv_bfloat16* sV = sKa + NQ * BN * LD;                        // [NV][BN][LD]
-  __shared__ int s_cmax[NW];
+  __nv_bfloat16* sQa = reinterpret_cast<__nv_bfloat16*>(smem);   // [NQ][T][LD]
+  __nv_bfloat16* sKa = sQa + NQ * T * LD;                         // [NQ][BN][LD]
+  __nv_bfloat16* sV = sKa + NQ * BN * LD;                         // [NV][BN][LD]
+  const int64_t nblk_cap = (p.N + BN - 1) / BN;
+  int* s_list = reinterpret_cast<int*>(sV + NV * BN * LD);        // [nblk_cap] attended blocks
+  float* s_dl = reinterpret_cast<float*>(s_list + nblk_cap);       // [nblk_cap] their d
+  uint8_t* s_cm = reinterpret_cast<uint8_t*>(s_dl + nblk_cap);     // [nblk_cap] max_i c_i
+  __shared__ uint32_t s_cw[BN];
+  __shared__ int s_extra[T];
+  __shared__ int s_red[NW];
 
   const int t = blockIdx.x;
   const int64_t bh = blockIdx.y;
@@ -115,27 +145,88 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   const TV* qg = static_cast<const TV*>(p.q) + bh * p.qsh;
   const TV* kg = static_cast<const TV*>(p.k) + kvh * p.ksh;
   const TV* vg = static_cast<const TV*>(p.v) + kvh * p.vsh;
-  const __nv_bfloat16* qhg = p.qh + bh * p.Nq * D;
-  const __nv_bfloat16* qlg = p.ql + bh * p.Nq * D;
-  const __nv_bfloat16* khg = p.kh + kvh * N * D;
-  const __nv_bfloat16* klg = p.kl + kvh * N * D;
 
   const int64_t tstart = p.qbase + (int64_t)t * T;  // absolute position of the tile's first query
   const int64_t P_top = min(tstart + T - 1, N - 1);
   const int64_t hi = P_top + 1;
   const int nblk = (int)((hi + BN - 1) / BN);
-  const float tau = __ldg(p.tau + (bh % p.H));
+  const int nrows = (int)(hi - tstart);
+  const uint32_t rowvalid = nrows >= 32 ? 0xffffffffu : ((1u << nrows) - 1u);
   const int64_t loc_lo = tstart - p.n_local + 1, loc_hi = tstart + T - 1;
+  const uint32_t* bits_row = p.bits + bh * p.head_stride + tri_tile_offset(t, T, p.qbase);
+  const uint8_t* bmax_row = p.bmax + bh * p.bmax_stride + tri_tile_offset(t, 1, p.qbase / 32);
 
-  // ---- prologue: Q in both geometries
-  for (int it = tid; it < T * D; it += NTH) {
-    const int r = it / D, d = it % D;
-    const int64_t qp = tstart + r;
-    const int64_t ql = qp - p.qbase;
-    __nv_bfloat16 zh = __float2bfloat16_rn(0.f);
-    sQs[r * LD + d] = qp < N ? qhg[ql * D + d] : zh;
-    sQs[(T + r) * LD + d] = qp < N ? qlg[ql * D + d] : zh;
+  // keep bits (bit r = query row r) of key j: Kernel A's threshold decisions OR the forced keys
+  // (global prefix and the tile's local window), restricted to causal, real rows
+  auto forced_rows = [&](int64_t j) -> uint32_t {
+    if (!(j < p.n_global || (j >= loc_lo && j <= loc_hi))) return 0u;
+    const int64_t dl = j - tstart;
+    const uint32_t causal = dl <= 0 ? 0xffffffffu : (dl >= 32 ? 0u : ~((1u << dl) - 1u));
+    return causal & rowvalid;
+  };
+
+  // ---- phase 1: max_i c_i of every block (Kernel A's maxima; exact recount where forced)
+  for (int b = tid; b < nblk; b += NTH) s_cm[b] = __ldg(bmax_row + (int64_t)b * (BN / 32));
+  for (int i = tid; i < T; i += NTH) s_extra[i] = 0;
+  __syncthreads();
+  const int ng_blk = (int)min((int64_t)nblk, ((int64_t)max(p.n_global, 0) + BN - 1) / BN);
+  const int lb0 = (int)min((int64_t)nblk, (loc_lo > 0 ? loc_lo : 0) / BN);
+  const int nf_g = min(ng_blk, lb0);
+  const int nfs = nf_g + (nblk - lb0);
+  int extra = 0;  // lane r: forced keys of row r that Kernel A's threshold did not keep
+  for (int f = warp; f < nfs; f += NW) {
+    const int b = f < nf_g ? f : lb0 + (f - nf_g);
+    int cf = 0, cn = 0;
+#pragma unroll
+    for (int h = 0; h < BN / 32; ++h) {
+      const int64_t j = (int64_t)b * BN + h * 32 + lane;
+      const uint32_t w = j <= P_top ? bits_row[j] : 0u;
+      cn += __popc(transpose32(w));
+      cf += __popc(transpose32(w | forced_rows(j)));
+    }
+    extra += cf - cn;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) cf = max(cf, __shfl_xor_sync(0xffffffffu, cf, o));
+    if (lane == 0) s_cm[b] = (uint8_t)cf;
   }
+  atomicAdd(&s_extra[lane], extra);
+  __syncthreads();
+
+  // ---- phase 2: streamed offsets in descending block order, list of blocks with keeps
+  int carry_d = 0, carry_u = 0, n_pos = 0;
+  for (int c0 = 0; c0 < nblk; c0 += NTH) {
+    const int tb = c0 + tid;
+    int adv = 0, use = 0;
+    int b = 0;
+    if (tb < nblk) {
+      b = nblk - 1 - tb;
+      const int cm = s_cm[b];
+      const int64_t sn = (int64_t)b * BN;
+      const int64_t hi_t = min(P_top, sn + BN - 1);
+      adv = p.adv_full ? (int)(hi_t - sn + 1) : cm;
+      use = cm > 0;
+      n_pos += adv > 0;
+    }
+    int tot_d, tot_u;
+    const int ed = cta_excl_sum(adv, s_red, tot_d);
+    const int eu = cta_excl_sum(use, s_red, tot_u);
+    if (use) {
+      s_list[carry_u + eu] = b;
+      s_dl[carry_u + eu] = (float)(carry_d + ed);
+    }
+    carry_d += tot_d;
+    carry_u += tot_u;
+  }
+  int n_adv;
+  {
+    int tot;
+    cta_excl_sum(n_pos, s_red, tot);
+    n_adv = tot;
+  }
+  const int n_list = carry_u;
+  __syncthreads();
+
+  // ---- Q at the streamed query positions (attend geometry)
   for (int it = tid; it < T * HALF; it += NTH) {
     const int r = it / HALF, f = it % HALF;
     const int64_t qp = tstart + r;
@@ -155,13 +246,13 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
       const float ang = __fmul_rn(npq, __ldg(p.inv_freq_c + f));
       rope_pair(x1, x2, ang, 1.f, r1, r2);
     }
-    __nv_bfloat16 a[NQ], b[NQ];
+    __nv_bfloat16 a[NQ], b2[NQ];
     split_pieces<NQ>(r1, a);
-    split_pieces<NQ>(r2, b);
+    split_pieces<NQ>(r2, b2);
 #pragma unroll
     for (int j = 0; j < NQ; ++j) {
       sQa[(j * T + r) * LD + f] = a[j];
-      sQa[(j * T + r) * LD + f + HALF] = b[j];
+      sQa[(j * T + r) * LD + f + HALF] = b2[j];
     }
   }
 
@@ -169,76 +260,24 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   const int64_t qpa = tstart + ra, qpb = tstart + rb;
   const bool okA = qpa < N, okB = qpb < N;
   const int64_t ra_l = qpa - p.qbase, rb_l = qpb - p.qbase;  // slab rows
-  const float thrA = okA ? __fsub_rn(p.row_max[bh * p.Nq + ra_l], tau) : INFINITY;
-  const float thrB = okB ? __fsub_rn(p.row_max[bh * p.Nq + rb_l], tau) : INFINITY;
 
   float o[D / 8][4];
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
-  int keptA = 0, keptB = 0;
-  float dpos = 0.f;
-  int n_used = 0;
 
-  for (int tb = 0; tb < nblk; ++tb) {
-    const int64_t sn = (int64_t)(nblk - 1 - tb) * BN;
+  // ---- phase 3: attend the blocks with keeps, in descending block order
+  for (int li = 0; li < n_list; ++li) {
+    const int b = s_list[li];
+    const float dpos = s_dl[li];
+    const int64_t sn = (int64_t)b * BN;
     const int64_t hi_t = min(P_top, sn + BN - 1);
     __syncthreads();
-    // phase 1: selection-geometry K (hi/lo) of the block
-    for (int it = tid; it < BN * (D / 8); it += NTH) {
-      const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
+    for (int i = tid; i < BN; i += NTH) {
       const int64_t j = sn + i;
-      uint4 h = make_uint4(0u, 0u, 0u, 0u), l = h;
-      if (j < N) {
-        h = *reinterpret_cast<const uint4*>(khg + j * D + d0);
-        l = *reinterpret_cast<const uint4*>(klg + j * D + d0);
-      }
-      *reinterpret_cast<uint4*>(sKs + i * LD + d0) = h;
-      *reinterpret_cast<uint4*>(sKs + (BN + i) * LD + d0) = l;
+      s_cw[i] = (j <= P_top ? bits_row[j] : 0u) | forced_rows(j);
     }
-    __syncthreads();
-
-    // selection scores and keep mask
-    float s[BN / 8][4];
-    score_tile<D, BN, 2>(sQs, sKs, s);
-    uint32_t keepbits[BN / 8];
-    int cA = 0, cB = 0;
-#pragma unroll
-    for (int nt = 0; nt < BN / 8; ++nt) {
-      uint32_t kb = 0;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int64_t j = sn + nt * 8 + 2 * c4 + (e & 1);
-        const int64_t qp = e < 2 ? qpa : qpb;
-        const bool rok = e < 2 ? okA : okB;
-        const float thr = e < 2 ? thrA : thrB;
-        const bool forced = j < p.n_global || (j >= loc_lo && j <= loc_hi);
-        const float sc = __fmul_rn(s[nt][e], p.sm_scale);
-        const bool keep = (sc >= thr || forced) && qp >= j && rok && j < N;
-        kb |= (keep ? 1u : 0u) << e;
-        if (keep) {
-          if (e < 2) ++cA;
-          else ++cB;
-        }
-      }
-      keepbits[nt] = kb;
-    }
-    cA += __shfl_xor_sync(0xffffffffu, cA, 1);
-    cA += __shfl_xor_sync(0xffffffffu, cA, 2);
-    cB += __shfl_xor_sync(0xffffffffu, cB, 1);
-    cB += __shfl_xor_sync(0xffffffffu, cB, 2);
-    int cm = max(cA, cB);
-#pragma unroll
-    for (int o2 = 4; o2 < 32; o2 <<= 1) cm = max(cm, __shfl_xor_sync(0xffffffffu, cm, o2));
-    if (lane == 0) s_cmax[warp] = cm;
-    __syncthreads();
-    int cmax = 0;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) cmax = max(cmax, s_cmax[w]);
-    const float adv = p.adv_full ? (float)(hi_t - sn + 1) : (float)cmax;
-    if (p.use_skip && !(adv > 0.f)) continue;
-
-    // phase 2 (used blocks only): raw K rotated at the streamed positions, and V
+    // raw K rotated at the streamed positions, and V
     for (int it = tid; it < BN * (HALF / 8); it += NTH) {
       const int i = it / (HALF / 8), f0 = (it % (HALF / 8)) * 8;
       const int64_t j = sn + i;
@@ -273,14 +312,16 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
     }
     __syncthreads();
 
-    // attend scores at the streamed positions
+    float s[BN / 8][4];
     score_tile<D, BN, NQ>(sQa, sKa, s);
     float mxA = -INFINITY, mxB = -INFINITY;
 #pragma unroll
     for (int nt = 0; nt < BN / 8; ++nt) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const bool keep = (keepbits[nt] >> e) & 1u;
+        const int col = nt * 8 + 2 * c4 + (e & 1);
+        const int row = e < 2 ? ra : rb;
+        const bool keep = (s_cw[col] >> row) & 1u;
         const float v = keep ? __fmul_rn(s[nt][e], p.sm_scale) : -INFINITY;
         s[nt][e] = v;
         if (e < 2) mxA = fmaxf(mxA, v);
@@ -352,10 +393,6 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
         }
       }
     }
-    keptA += cA;
-    keptB += cB;
-    dpos = __fadd_rn(dpos, adv);
-    ++n_used;
   }
 
   TV* og = static_cast<TV*>(p.out) + bh * p.Nq * D;
@@ -377,15 +414,16 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
             __floats2bfloat162_rn(o[dt][2] / lB, o[dt][3] / lB);
     }
   }
+  // kept keys per query: Kernel A's count plus the forced keys its threshold did not keep
   if (c4 == 0) {
-    if (okA) p.kept[bh * p.Nq + ra_l] = keptA;
-    if (okB) p.kept[bh * p.Nq + rb_l] = keptB;
+    if (okA) p.kept[bh * p.Nq + ra_l] = p.row_count[bh * p.Nq + ra_l] + s_extra[ra];
+    if (okB) p.kept[bh * p.Nq + rb_l] = p.row_count[bh * p.Nq + rb_l] + s_extra[rb];
   }
   if (tid == 0) {
     const int64_t o2 = bh * p.nt + t;
-    p.span[o2] = dpos;
+    p.span[o2] = (float)carry_d;
     p.blocks[o2] = (float)nblk;
-    p.skipped[o2] = (float)(nblk - n_used);
+    p.skipped[o2] = (float)(p.use_skip ? nblk - n_adv : 0);
   }
 }
 
@@ -393,7 +431,10 @@ template <int D, int BN, bool F32>
 int launch_one(const PQSP& p, cudaStream_t stream) {
   constexpr int LD = D + 8;
   constexpr int NQ = F32 ? 3 : 2, NV = F32 ? 3 : 1;
-  const size_t smem = (size_t)((2 + NQ) * T * LD + (2 + NQ + NV) * BN * LD) * 2;
+  const int64_t nblk_cap = (p.N + BN - 1) / BN;
+  const size_t smem = (size_t)(NQ * T * LD + (NQ + NV) * BN * LD) * 2 + (size_t)nblk_cap * 9 + 16;
+  if (smem > 200 * 1024)
+    return fail(STA_ERR_UNSUPPORTED, "sta_pqstream_attend: too many key blocks per tile (n / block_n)");
   auto kern = pqstream_kernel<D, BN, F32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return fail(STA_ERR_CUDA, cudaGetErrorString(e));
@@ -406,8 +447,8 @@ int launch_one(const PQSP& p, cudaStream_t stream) {
 }  // namespace
 
 int launch_pqstream(const sta_pqstream_args* a, cudaStream_t stream) {
-  if (!a || !a->q || !a->k || !a->v || !a->out || !a->q_hi || !a->q_lo || !a->k_hi || !a->k_lo ||
-      !a->row_max || !a->tau || !a->inv_freq_c || !a->span || !a->kept || !a->blocks || !a->skipped)
+  if (!a || !a->q || !a->k || !a->v || !a->out || !a->bits || !a->block_max || !a->row_count ||
+      !a->inv_freq_c || !a->span || !a->kept || !a->blocks || !a->skipped)
     return fail(STA_ERR_ARG, "sta_pqstream_attend: null pointer");
   if (a->tile != 32) return fail(STA_ERR_UNSUPPORTED, "sta_pqstream_attend: tile must be 32");
   if (a->block_n != 32 && a->block_n != 64)
@@ -416,6 +457,8 @@ int launch_pqstream(const sta_pqstream_args* a, cudaStream_t stream) {
   if (a->n_heads <= 0 || a->n_kv_heads <= 0 || a->n_heads % a->n_kv_heads)
     return fail(STA_ERR_ARG, "sta_pqstream_attend: bad head counts");
   if (a->n <= 0 || a->batch <= 0) return STA_OK;
+  if (a->q_pos_base < 0 || a->q_pos_base >= a->n || a->q_pos_base % 32)
+    return fail(STA_ERR_ARG, "sta_pqstream_attend: q_pos_base must be a multiple of 32 in [0, n)");
   {
     const int64_t es = a->dtype == STA_DTYPE_F32 ? 4 : 2;
     const uintptr_t al = reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->k) |
@@ -433,19 +476,16 @@ int launch_pqstream(const sta_pqstream_args* a, cudaStream_t stream) {
   p.out = a->out;
   p.BH = a->batch * a->n_heads;
   p.N = a->n;
-  if (a->q_pos_base < 0 || a->q_pos_base >= a->n)
-    return fail(STA_ERR_ARG, "sta_pqstream_attend: q_pos_base outside [0, n)");
   p.qbase = a->q_pos_base;
   p.Nq = a->n - a->q_pos_base;
   p.nt = (p.Nq + T - 1) / T;
   p.H = (int)a->n_heads;
   p.Hkv = (int)a->n_kv_heads;
-  p.qh = static_cast<const __nv_bfloat16*>(a->q_hi);
-  p.ql = static_cast<const __nv_bfloat16*>(a->q_lo);
-  p.kh = static_cast<const __nv_bfloat16*>(a->k_hi);
-  p.kl = static_cast<const __nv_bfloat16*>(a->k_lo);
-  p.row_max = a->row_max;
-  p.tau = a->tau;
+  p.bits = a->bits;
+  p.head_stride = tri_head_stride(a->n, T, a->q_pos_base);
+  p.bmax = a->block_max;
+  p.bmax_stride = tri_head_stride((a->n + 31) / 32, 1, a->q_pos_base / 32);
+  p.row_count = a->row_count;
   p.n_global = a->n_global;
   p.n_local = a->n_local;
   p.inv_freq_c = a->inv_freq_c;

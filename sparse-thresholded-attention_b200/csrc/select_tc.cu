@@ -72,6 +72,9 @@ struct Params {
   int* err;
   int64_t head_stride;  // compact per-head stride
   int64_t dca_L;        // > 0: Dual Chunk Attention selection geometry, chunk_len (multiple of 256)
+  uint8_t* block_max;   // PQ-Stream block maxima (tile 32) or null
+  int bmax_bn;
+  int64_t bmax_head_stride;
 };
 
 // Which rotated Q plane scores key block kb of query block qb: 0 = plain (or same DCA chunk),
@@ -96,21 +99,6 @@ __device__ __forceinline__ float transpose_reduce32(float (&v)[32]) {
     }
   }
   return v[0];
-}
-
-// 32 x 32 bit-matrix transpose across the warp: on entry lane r holds row r (bit c = M[r][c]);
-// on exit lane c holds column c (bit r = M[r][c]).  Five block-swap rounds, one shuffle each.
-__device__ __forceinline__ uint32_t transpose32(uint32_t x) {
-  const int l = lane_id();
-  const uint32_t lo_masks[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
-#pragma unroll
-  for (int i = 0; i < 5; ++i) {
-    const int s = 16 >> i;
-    const uint32_t lo = lo_masks[i], hi = ~lo;
-    const uint32_t y = __shfl_xor_sync(0xffffffffu, x, s);
-    x = (l & s) ? ((x & hi) | ((y & hi) >> s)) : ((x & lo) | ((y & lo) << s));
-  }
-  return x;
 }
 
 // Smallest fp32 x with fl(x * sm) >= thr (sm > 0).  fl(x * sm) is non-decreasing in x, so
@@ -351,6 +339,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             float v[32], vn[32];  // vn unused (eliminated) without prefetch
             tmem_ld32(taddr + part * (BN / kParts), v);
             tmem_wait_ld();
+            int rc_even = 0;  // kept count of the previous (even) chunk, for 64-key blocks
 #pragma unroll 1
             for (int cc = 0; cc < kChunks; ++cc) {
               const int ch = part * kChunks + cc;
@@ -407,6 +396,24 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
                     if (p.votes) p.votes[off] = (uint8_t)__popc(colw);
                     if (p.wmode != 0 && p.wvotes) p.wvotes[off] = myw;
                     if (p.bits) p.bits[off] = colw;
+                  }
+                  if (p.block_max) {
+                    // PQ-Stream: max over the tile's rows of the kept count of each key block
+                    // (32 keys, or 64 = this chunk and the previous one of the same warp)
+                    int c = __popc(word);
+                    const bool wide = p.bmax_bn == 64;
+                    if (wide && !(cc & 1)) {
+                      rc_even = c;
+                    } else {
+                      if (wide) c += rc_even;
+#pragma unroll
+                      for (int o = 16; o >= 1; o >>= 1) c = max(c, __shfl_xor_sync(0xffffffffu, c, o));
+                      const int64_t kb0 = wide ? kbase - 32 : kbase;
+                      if (lane == 0 && tg < nt && kb0 < min((tg + 1) * 32, p.N))
+                        p.block_max[bh * p.bmax_head_stride +
+                                    tri_tile_offset(tg - p.qbase / 32, 1, p.qbase / 32) + kb0 / 32] =
+                            (uint8_t)c;
+                    }
                   }
                 } else {
                   const int o = rb * (4 * BN) + quad * BN + ch * 32 + lane;
@@ -536,6 +543,11 @@ int launch_select(const sta_select_args* a, cudaStream_t stream) {
   p.err = device_error_word();
   p.head_stride = tri_head_stride(a->n, a->tile, a->q_pos_base);
   p.dca_L = a->dca_chunk_len;
+  p.block_max = a->max_only ? nullptr : a->block_max;
+  p.bmax_bn = a->block_max_bn;
+  p.bmax_head_stride = tri_head_stride((a->n + 31) / 32, 1, a->q_pos_base / 32);
+  if (p.block_max && (a->tile != 32 || (p.bmax_bn != 32 && p.bmax_bn != 64)))
+    return fail(STA_ERR_UNSUPPORTED, "sta_select: block_max needs tile 32 and block_max_bn 32 or 64");
   if (p.dca_L > 0 && (p.dca_L % BN)) return fail(STA_ERR_UNSUPPORTED, "sta_select: DCA chunk_len must be a multiple of 256");
 
   int dev = 0, nsm = 148;

@@ -29,7 +29,8 @@ class SelectArgs(ctypes.Structure):
                 ("d", c_i32), ("tile", c_i32), ("sm_scale", c_f32), ("wmode", c_i32),
                 ("tau", c_vp), ("max_only", c_i32), ("votes", c_vp), ("wvotes", c_vp),
                 ("bits", c_vp), ("row_max", c_vp), ("row_count", c_vp),
-                ("dca_chunk_len", c_i32), ("q_pos_base", c_i64)]
+                ("dca_chunk_len", c_i32), ("q_pos_base", c_i64),
+                ("block_max", c_vp), ("block_max_bn", c_i32)]
 
 
 class BuildArgs(ctypes.Structure):
@@ -78,12 +79,12 @@ class PQStreamArgs(ctypes.Structure):
                 ("v", c_vp), ("v_stride_h", c_i64), ("v_stride_n", c_i64),
                 ("out", c_vp), ("dtype", c_i32), ("batch", c_i64), ("n_heads", c_i64),
                 ("n_kv_heads", c_i64), ("n", c_i64), ("d", c_i32), ("tile", c_i32),
-                ("block_n", c_i32), ("q_hi", c_vp), ("q_lo", c_vp), ("k_hi", c_vp),
-                ("k_lo", c_vp), ("row_max", c_vp), ("tau", c_vp), ("n_global", c_i32),
-                ("n_local", c_i32), ("inv_freq_c", c_vp), ("sm_scale", c_f32),
-                ("pos_advance", c_i32), ("use_skip", c_i32), ("rope_table", c_vp),
-                ("rope_table_R", c_f32), ("rope_table_len", c_i64), ("span", c_vp), ("kept", c_vp),
-                ("blocks", c_vp), ("skipped", c_vp), ("q_pos_base", c_i64)]
+                ("block_n", c_i32), ("bits", c_vp), ("block_max", c_vp), ("row_count", c_vp),
+                ("n_global", c_i32), ("n_local", c_i32), ("inv_freq_c", c_vp),
+                ("sm_scale", c_f32), ("pos_advance", c_i32), ("use_skip", c_i32),
+                ("rope_table", c_vp), ("rope_table_R", c_f32), ("rope_table_len", c_i64),
+                ("span", c_vp), ("kept", c_vp), ("blocks", c_vp), ("skipped", c_vp),
+                ("q_pos_base", c_i64)]
 
 
 class ForwardArgs(ctypes.Structure):
