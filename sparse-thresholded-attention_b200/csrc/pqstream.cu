@@ -23,8 +23,8 @@ namespace sta {
 namespace {
 
 constexpr int T = 32;      // query tile (fixed by the reference's bit packing convention)
-constexpr int NW = 2;      // warps (16 query rows each)
-constexpr int NTH = 64;
+constexpr int NW = 4;      // warps: two pairs, each pair covers the tile's 32 rows (16 per warp)
+constexpr int NTH = NW * 32;
 
 struct PQSP {
   const void* q;
@@ -67,9 +67,9 @@ __device__ __forceinline__ float ldv<__nv_bfloat16>(const __nv_bfloat16* p) {
 // s (16 rows of this warp x BN keys) = sum of piece products of A [NP][T][LD] and B [NP][BN][LD]
 template <int D, int BN, int NP>
 __device__ __forceinline__ void score_tile(const __nv_bfloat16* sA, const __nv_bfloat16* sB,
-                                           float (&s)[BN / 8][4]) {
+                                           float (&s)[BN / 8][4], int warp) {
   constexpr int LD = D + 8;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
   const int mi = lane >> 3, rr = lane & 7;
 #pragma unroll
   for (int i = 0; i < BN / 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
@@ -124,21 +124,23 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   constexpr int HALF = D / 2;
   constexpr int NQ = F32 ? 3 : 2;  // pieces of the attend-geometry Q / K
   constexpr int NV = F32 ? 3 : 1;  // pieces of P / V
+  constexpr int KBUF = NQ * BN * LD, VBUF = NV * BN * LD;
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* sQa = reinterpret_cast<__nv_bfloat16*>(smem);   // [NQ][T][LD]
-  __nv_bfloat16* sKa = sQa + NQ * T * LD;                         // [NQ][BN][LD]
-  __nv_bfloat16* sV = sKa + NQ * BN * LD;                         // [NV][BN][LD]
-  const int64_t nblk_cap = (p.N + BN - 1) / BN;
-  int* s_list = reinterpret_cast<int*>(sV + NV * BN * LD);        // [nblk_cap] attended blocks
-  float* s_dl = reinterpret_cast<float*>(s_list + nblk_cap);       // [nblk_cap] their d
-  uint8_t* s_cm = reinterpret_cast<uint8_t*>(s_dl + nblk_cap);     // [nblk_cap] max_i c_i
-  __shared__ uint32_t s_cw[BN];
+  __nv_bfloat16* sKa = sQa + NQ * T * LD;                         // [2 pairs][NQ][BN][LD]
+  __nv_bfloat16* sV = sKa + 2 * KBUF;                             // [2 pairs][NV][BN][LD]
+  int* s_fcm = reinterpret_cast<int*>(sV + 2 * VBUF);             // forced blocks' max_i c_i
+  __shared__ uint32_t s_cw[2][BN];
+  __shared__ int s_list[NTH];
+  __shared__ float s_dl[NTH];
   __shared__ int s_extra[T];
   __shared__ int s_red[NW];
+  __shared__ float s_ml[32][4];
 
   const int t = blockIdx.x;
   const int64_t bh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int pair = warp >> 1, rw = warp & 1, ptid = tid & 63;
   const int g = lane >> 2, c4 = lane & 3;
   const int64_t N = p.N;
   const int64_t kvh = (bh / p.H) * p.Hkv + (bh % p.H) / (p.H / p.Hkv);
@@ -156,23 +158,23 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   const uint32_t* bits_row = p.bits + bh * p.head_stride + tri_tile_offset(t, T, p.qbase);
   const uint8_t* bmax_row = p.bmax + bh * p.bmax_stride + tri_tile_offset(t, 1, p.qbase / 32);
 
-  // keep bits (bit r = query row r) of key j: Kernel A's threshold decisions OR the forced keys
-  // (global prefix and the tile's local window), restricted to causal, real rows
+  // keep bits (bit r = query row r) of the forced key j (global prefix, local window),
+  // restricted to causal, real rows
   auto forced_rows = [&](int64_t j) -> uint32_t {
     if (!(j < p.n_global || (j >= loc_lo && j <= loc_hi))) return 0u;
     const int64_t dl = j - tstart;
     const uint32_t causal = dl <= 0 ? 0xffffffffu : (dl >= 32 ? 0u : ~((1u << dl) - 1u));
     return causal & rowvalid;
   };
-
-  // ---- phase 1: max_i c_i of every block (Kernel A's maxima; exact recount where forced)
-  for (int b = tid; b < nblk; b += NTH) s_cm[b] = __ldg(bmax_row + (int64_t)b * (BN / 32));
-  for (int i = tid; i < T; i += NTH) s_extra[i] = 0;
-  __syncthreads();
+  // forced blocks: [0, ng_blk) and [lb0, nblk); slot f of s_fcm
   const int ng_blk = (int)min((int64_t)nblk, ((int64_t)max(p.n_global, 0) + BN - 1) / BN);
   const int lb0 = (int)min((int64_t)nblk, (loc_lo > 0 ? loc_lo : 0) / BN);
   const int nf_g = min(ng_blk, lb0);
   const int nfs = nf_g + (nblk - lb0);
+
+  // ---- phase 1: exact max_i c_i of the forced blocks (Kernel A's keeps OR the forced keys)
+  for (int i = tid; i < T; i += NTH) s_extra[i] = 0;
+  __syncthreads();
   int extra = 0;  // lane r: forced keys of row r that Kernel A's threshold did not keep
   for (int f = warp; f < nfs; f += NW) {
     const int b = f < nf_g ? f : lb0 + (f - nf_g);
@@ -187,44 +189,9 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
     extra += cf - cn;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) cf = max(cf, __shfl_xor_sync(0xffffffffu, cf, o));
-    if (lane == 0) s_cm[b] = (uint8_t)cf;
+    if (lane == 0) s_fcm[f] = cf;
   }
   atomicAdd(&s_extra[lane], extra);
-  __syncthreads();
-
-  // ---- phase 2: streamed offsets in descending block order, list of blocks with keeps
-  int carry_d = 0, carry_u = 0, n_pos = 0;
-  for (int c0 = 0; c0 < nblk; c0 += NTH) {
-    const int tb = c0 + tid;
-    int adv = 0, use = 0;
-    int b = 0;
-    if (tb < nblk) {
-      b = nblk - 1 - tb;
-      const int cm = s_cm[b];
-      const int64_t sn = (int64_t)b * BN;
-      const int64_t hi_t = min(P_top, sn + BN - 1);
-      adv = p.adv_full ? (int)(hi_t - sn + 1) : cm;
-      use = cm > 0;
-      n_pos += adv > 0;
-    }
-    int tot_d, tot_u;
-    const int ed = cta_excl_sum(adv, s_red, tot_d);
-    const int eu = cta_excl_sum(use, s_red, tot_u);
-    if (use) {
-      s_list[carry_u + eu] = b;
-      s_dl[carry_u + eu] = (float)(carry_d + ed);
-    }
-    carry_d += tot_d;
-    carry_u += tot_u;
-  }
-  int n_adv;
-  {
-    int tot;
-    cta_excl_sum(n_pos, s_red, tot);
-    n_adv = tot;
-  }
-  const int n_list = carry_u;
-  __syncthreads();
 
   // ---- Q at the streamed query positions (attend geometry)
   for (int it = tid; it < T * HALF; it += NTH) {
@@ -255,146 +222,222 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
       sQa[(j * T + r) * LD + f + HALF] = b2[j];
     }
   }
+  __syncthreads();
 
-  const int ra = warp * 16 + g, rb = ra + 8;
-  const int64_t qpa = tstart + ra, qpb = tstart + rb;
-  const bool okA = qpa < N, okB = qpb < N;
-  const int64_t ra_l = qpa - p.qbase, rb_l = qpb - p.qbase;  // slab rows
-
+  const int ra = rw * 16 + g, rb = ra + 8;  // tile rows of this thread's fragments
   float o[D / 8][4];
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+  __nv_bfloat16* myK = sKa + pair * KBUF;
+  __nv_bfloat16* myV = sV + pair * VBUF;
 
-  // ---- phase 3: attend the blocks with keeps, in descending block order
-  for (int li = 0; li < n_list; ++li) {
-    const int b = s_list[li];
-    const float dpos = s_dl[li];
-    const int64_t sn = (int64_t)b * BN;
-    const int64_t hi_t = min(P_top, sn + BN - 1);
-    __syncthreads();
-    for (int i = tid; i < BN; i += NTH) {
-      const int64_t j = sn + i;
-      s_cw[i] = (j <= P_top ? bits_row[j] : 0u) | forced_rows(j);
+  // ---- phase 2: descending blocks, NTH at a time: offsets d, then attend the blocks with keeps
+  // (the two warp pairs take alternate blocks and merge their softmax states at the end)
+  int carry_d = 0, n_pos = 0;
+  for (int c0 = 0; c0 < nblk; c0 += NTH) {
+    const int tb = c0 + tid;
+    int adv = 0, use = 0, b = 0;
+    if (tb < nblk) {
+      b = nblk - 1 - tb;
+      int cm;
+      if (b < nf_g) cm = s_fcm[b];
+      else if (b >= lb0) cm = s_fcm[nf_g + (b - lb0)];
+      else cm = __ldg(bmax_row + (int64_t)b * (BN / 32));
+      const int64_t sn = (int64_t)b * BN;
+      const int64_t hi_t = min(P_top, sn + BN - 1);
+      adv = p.adv_full ? (int)(hi_t - sn + 1) : cm;
+      use = cm > 0;
+      n_pos += adv > 0;
     }
-    // raw K rotated at the streamed positions, and V
-    for (int it = tid; it < BN * (HALF / 8); it += NTH) {
-      const int i = it / (HALF / 8), f0 = (it % (HALF / 8)) * 8;
-      const int64_t j = sn + i;
-      const float npk = -__fadd_rn(dpos, (float)(hi_t - j));
-      rotate8<NQ, HALF>(kg + (j < N ? j : 0) * p.ksn, j < N, f0, npk, p.inv_freq_c, 1.f,
-                        sKa + i * LD, BN * LD, p.rtab, table_index(npk, p.rtab_R, p.rtab_len));
+    int tot_d, n_use;
+    const int ed = cta_excl_sum(adv, s_red, tot_d);
+    const int eu = cta_excl_sum(use, s_red, n_use);
+    if (use) {
+      s_list[eu] = b;
+      s_dl[eu] = (float)(carry_d + ed);
     }
-    for (int it = tid; it < BN * (D / 8); it += NTH) {
-      const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
-      const int64_t j = sn + i;
-      __nv_bfloat16* dst = sV + i * LD + d0;
-      if (!F32) {
-        uint4 u = make_uint4(0u, 0u, 0u, 0u);
-        if (j < N) u = *reinterpret_cast<const uint4*>(vg + j * p.vsn + d0);
-        *reinterpret_cast<uint4*>(dst) = u;
-      } else {
-        float x[8];
-        if (j < N) {
-          load8(vg + j * p.vsn + d0, x);
-        } else {
-#pragma unroll
-          for (int u = 0; u < 8; ++u) x[u] = 0.f;
+    carry_d += tot_d;
+    for (int li0 = 0; li0 < n_use; li0 += 2) {
+      const int li = li0 + pair;
+      const bool active = li < n_use;
+      __syncthreads();  // list written / the pair's buffers free
+      int64_t sn = 0, hi_t = 0;
+      if (active) {
+        const int bb = s_list[li];
+        const float dpos = s_dl[li];
+        sn = (int64_t)bb * BN;
+        hi_t = min(P_top, sn + BN - 1);
+        for (int i = ptid; i < BN; i += 64) {
+          const int64_t j = sn + i;
+          s_cw[pair][i] = (j <= P_top ? bits_row[j] : 0u) | forced_rows(j);
         }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          __nv_bfloat16 pc[NV];
-          split_pieces<NV>(x[u], pc);
-#pragma unroll
-          for (int q2 = 0; q2 < NV; ++q2) dst[q2 * BN * LD + u] = pc[q2];
+        // raw K rotated at the streamed positions, and V
+        for (int it = ptid; it < BN * (HALF / 8); it += 64) {
+          const int i = it / (HALF / 8), f0 = (it % (HALF / 8)) * 8;
+          const int64_t j = sn + i;
+          const float npk = -__fadd_rn(dpos, (float)(hi_t - j));
+          rotate8<NQ, HALF>(kg + (j < N ? j : 0) * p.ksn, j < N, f0, npk, p.inv_freq_c, 1.f,
+                            myK + i * LD, BN * LD, p.rtab, table_index(npk, p.rtab_R, p.rtab_len));
         }
-      }
-    }
-    __syncthreads();
-
-    float s[BN / 8][4];
-    score_tile<D, BN, NQ>(sQa, sKa, s);
-    float mxA = -INFINITY, mxB = -INFINITY;
+        for (int it = ptid; it < BN * (D / 8); it += 64) {
+          const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
+          const int64_t j = sn + i;
+          __nv_bfloat16* dst = myV + i * LD + d0;
+          if (!F32) {
+            uint4 u = make_uint4(0u, 0u, 0u, 0u);
+            if (j < N) u = *reinterpret_cast<const uint4*>(vg + j * p.vsn + d0);
+            *reinterpret_cast<uint4*>(dst) = u;
+          } else {
+            float x[8];
+            if (j < N) {
+              load8(vg + j * p.vsn + d0, x);
+            } else {
 #pragma unroll
-    for (int nt = 0; nt < BN / 8; ++nt) {
+              for (int u = 0; u < 8; ++u) x[u] = 0.f;
+            }
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int col = nt * 8 + 2 * c4 + (e & 1);
-        const int row = e < 2 ? ra : rb;
-        const bool keep = (s_cw[col] >> row) & 1u;
-        const float v = keep ? __fmul_rn(s[nt][e], p.sm_scale) : -INFINITY;
-        s[nt][e] = v;
-        if (e < 2) mxA = fmaxf(mxA, v);
-        else mxB = fmaxf(mxB, v);
-      }
-    }
-    mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
-    mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
-    mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
-    mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
-    const float mnA = fmaxf(mA, mxA), mnB = fmaxf(mB, mxB);
-    const float msA = mnA == -INFINITY ? 0.f : mnA;
-    const float msB = mnB == -INFINITY ? 0.f : mnB;
-    float sumA = 0.f, sumB = 0.f;
+            for (int u = 0; u < 8; ++u) {
+              __nv_bfloat16 pc[NV];
+              split_pieces<NV>(x[u], pc);
 #pragma unroll
-    for (int nt = 0; nt < BN / 8; ++nt) {
-      s[nt][0] = expf(__fsub_rn(s[nt][0], msA));
-      s[nt][1] = expf(__fsub_rn(s[nt][1], msA));
-      s[nt][2] = expf(__fsub_rn(s[nt][2], msB));
-      s[nt][3] = expf(__fsub_rn(s[nt][3], msB));
-      sumA += s[nt][0] + s[nt][1];
-      sumB += s[nt][2] + s[nt][3];
-    }
-    sumA += __shfl_xor_sync(0xffffffffu, sumA, 1);
-    sumA += __shfl_xor_sync(0xffffffffu, sumA, 2);
-    sumB += __shfl_xor_sync(0xffffffffu, sumB, 1);
-    sumB += __shfl_xor_sync(0xffffffffu, sumB, 2);
-    const float alA = expf(__fsub_rn(mA, msA)), alB = expf(__fsub_rn(mB, msB));
-    lA = lA * alA + sumA;
-    lB = lB * alB + sumB;
-#pragma unroll
-    for (int i = 0; i < D / 8; ++i) {
-      o[i][0] *= alA;
-      o[i][1] *= alA;
-      o[i][2] *= alB;
-      o[i][3] *= alB;
-    }
-    mA = mnA;
-    mB = mnB;
-    {
-      const int mi = lane >> 3, rr = lane & 7;
-#pragma unroll
-      for (int kk = 0; kk < BN / 16; ++kk) {
-        uint32_t pp[NV][4];
-        {
-          uint32_t x0[NV], x1[NV], x2[NV], x3[NV];
-          pack_pieces<NV>(s[2 * kk][0], s[2 * kk][1], x0);
-          pack_pieces<NV>(s[2 * kk][2], s[2 * kk][3], x1);
-          pack_pieces<NV>(s[2 * kk + 1][0], s[2 * kk + 1][1], x2);
-          pack_pieces<NV>(s[2 * kk + 1][2], s[2 * kk + 1][3], x3);
-#pragma unroll
-          for (int j = 0; j < NV; ++j) {
-            pp[j][0] = x0[j];
-            pp[j][1] = x1[j];
-            pp[j][2] = x2[j];
-            pp[j][3] = x3[j];
+              for (int q2 = 0; q2 < NV; ++q2) dst[q2 * BN * LD + u] = pc[q2];
+            }
           }
         }
-        const int row = kk * 16 + rr + (mi & 1) * 8;
+      }
+      __syncthreads();
+      if (!active) continue;
+
+      float s[BN / 8][4];
+      score_tile<D, BN, NQ>(sQa, myK, s, rw);
+      float mxA = -INFINITY, mxB = -INFINITY;
 #pragma unroll
-        for (int dp = 0; dp < D / 16; ++dp) {
-          const int col = (2 * dp + (mi >> 1)) * 8;
-          uint32_t v0[NV][2], v1[NV][2];
+      for (int nt = 0; nt < BN / 8; ++nt) {
 #pragma unroll
-          for (int j = 0; j < NV; ++j)
-            ldsm_x4_t(smem_u32(sV + (j * BN + row) * LD + col), v0[j][0], v0[j][1], v1[j][0], v1[j][1]);
-          mma_pieces<NV>(o[2 * dp], pp, v0);
-          mma_pieces<NV>(o[2 * dp + 1], pp, v1);
+        for (int e = 0; e < 4; ++e) {
+          const int col = nt * 8 + 2 * c4 + (e & 1);
+          const int row = e < 2 ? ra : rb;
+          const bool keep = (s_cw[pair][col] >> row) & 1u;
+          const float v = keep ? __fmul_rn(s[nt][e], p.sm_scale) : -INFINITY;
+          s[nt][e] = v;
+          if (e < 2) mxA = fmaxf(mxA, v);
+          else mxB = fmaxf(mxB, v);
+        }
+      }
+      mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
+      mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
+      mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
+      mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
+      const float mnA = fmaxf(mA, mxA), mnB = fmaxf(mB, mxB);
+      const float msA = mnA == -INFINITY ? 0.f : mnA;
+      const float msB = mnB == -INFINITY ? 0.f : mnB;
+      float sumA = 0.f, sumB = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < BN / 8; ++nt) {
+        s[nt][0] = expf(__fsub_rn(s[nt][0], msA));
+        s[nt][1] = expf(__fsub_rn(s[nt][1], msA));
+        s[nt][2] = expf(__fsub_rn(s[nt][2], msB));
+        s[nt][3] = expf(__fsub_rn(s[nt][3], msB));
+        sumA += s[nt][0] + s[nt][1];
+        sumB += s[nt][2] + s[nt][3];
+      }
+      sumA += __shfl_xor_sync(0xffffffffu, sumA, 1);
+      sumA += __shfl_xor_sync(0xffffffffu, sumA, 2);
+      sumB += __shfl_xor_sync(0xffffffffu, sumB, 1);
+      sumB += __shfl_xor_sync(0xffffffffu, sumB, 2);
+      const float alA = expf(__fsub_rn(mA, msA)), alB = expf(__fsub_rn(mB, msB));
+      lA = lA * alA + sumA;
+      lB = lB * alB + sumB;
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        o[i][0] *= alA;
+        o[i][1] *= alA;
+        o[i][2] *= alB;
+        o[i][3] *= alB;
+      }
+      mA = mnA;
+      mB = mnB;
+      {
+        const int mi = lane >> 3, rr = lane & 7;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          uint32_t pp[NV][4];
+          {
+            uint32_t x0[NV], x1[NV], x2[NV], x3[NV];
+            pack_pieces<NV>(s[2 * kk][0], s[2 * kk][1], x0);
+            pack_pieces<NV>(s[2 * kk][2], s[2 * kk][3], x1);
+            pack_pieces<NV>(s[2 * kk + 1][0], s[2 * kk + 1][1], x2);
+            pack_pieces<NV>(s[2 * kk + 1][2], s[2 * kk + 1][3], x3);
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+              pp[j][0] = x0[j];
+              pp[j][1] = x1[j];
+              pp[j][2] = x2[j];
+              pp[j][3] = x3[j];
+            }
+          }
+          const int row = kk * 16 + rr + (mi & 1) * 8;
+#pragma unroll
+          for (int dp = 0; dp < D / 16; ++dp) {
+            const int col = (2 * dp + (mi >> 1)) * 8;
+            uint32_t v0[NV][2], v1[NV][2];
+#pragma unroll
+            for (int j = 0; j < NV; ++j)
+              ldsm_x4_t(smem_u32(myV + (j * BN + row) * LD + col), v0[j][0], v0[j][1], v1[j][0], v1[j][1]);
+            mma_pieces<NV>(o[2 * dp], pp, v0);
+            mma_pieces<NV>(o[2 * dp + 1], pp, v1);
+          }
         }
       }
     }
   }
+  int n_adv;
+  {
+    int tot;
+    cta_excl_sum(n_pos, s_red, tot);
+    n_adv = tot;
+  }
 
+  // ---- merge the two pairs' softmax states (pair 1 -> shared memory -> pair 0)
+  float* s_o = reinterpret_cast<float*>(sKa);  // the K buffers are free now
+  __syncthreads();
+  if (pair == 1) {
+    float* dst = s_o + (size_t)(rw * 32 + lane) * (D / 2);
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dst[i * 4 + e] = o[i][e];
+  }
+  __syncthreads();
+  if (pair == 1 && c4 == 0) {
+    s_ml[ra][0] = mA;
+    s_ml[ra][1] = lA;
+    s_ml[rb][0] = mB;
+    s_ml[rb][1] = lB;
+  }
+  __syncthreads();
+  if (pair == 0) {
+    const float* src = s_o + (size_t)(rw * 32 + lane) * (D / 2);
+    const float m1A = s_ml[ra][0], l1A = s_ml[ra][1], m1B = s_ml[rb][0], l1B = s_ml[rb][1];
+    const float MA = fmaxf(mA, m1A), MB = fmaxf(mB, m1B);
+    const float a0A = mA == -INFINITY ? 0.f : expf(__fsub_rn(mA, MA));
+    const float a1A = m1A == -INFINITY ? 0.f : expf(__fsub_rn(m1A, MA));
+    const float a0B = mB == -INFINITY ? 0.f : expf(__fsub_rn(mB, MB));
+    const float a1B = m1B == -INFINITY ? 0.f : expf(__fsub_rn(m1B, MB));
+    lA = lA * a0A + l1A * a1A;
+    lB = lB * a0B + l1B * a1B;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] = o[i][0] * a0A + src[i * 4 + 0] * a1A;
+      o[i][1] = o[i][1] * a0A + src[i * 4 + 1] * a1A;
+      o[i][2] = o[i][2] * a0B + src[i * 4 + 2] * a1B;
+      o[i][3] = o[i][3] * a0B + src[i * 4 + 3] * a1B;
+    }
+  }
+  const int64_t qpa = tstart + ra, qpb = tstart + rb;
+  const bool okA = qpa < N && pair == 0, okB = qpb < N && pair == 0;
+  const int64_t ra_l = qpa - p.qbase, rb_l = qpb - p.qbase;  // slab rows
   TV* og = static_cast<TV*>(p.out) + bh * p.Nq * D;
 #pragma unroll
   for (int dt = 0; dt < D / 8; ++dt) {
@@ -431,10 +474,13 @@ template <int D, int BN, bool F32>
 int launch_one(const PQSP& p, cudaStream_t stream) {
   constexpr int LD = D + 8;
   constexpr int NQ = F32 ? 3 : 2, NV = F32 ? 3 : 1;
-  const int64_t nblk_cap = (p.N + BN - 1) / BN;
-  const size_t smem = (size_t)(NQ * T * LD + (NQ + NV) * BN * LD) * 2 + (size_t)nblk_cap * 9 + 16;
+  // forced blocks per tile: the global prefix and the local window (+ its partial blocks)
+  const int64_t ng = (int64_t)(p.n_global > 0 ? p.n_global : 0);
+  const int64_t nl = (int64_t)(p.n_local > 0 ? p.n_local : 0);
+  const int64_t nfs_cap = (ng + BN - 1) / BN + (nl + T + BN - 1) / BN + 2;
+  const size_t smem = (size_t)(NQ * T + 2 * (NQ + NV) * BN) * LD * 2 + (size_t)nfs_cap * 4;
   if (smem > 200 * 1024)
-    return fail(STA_ERR_UNSUPPORTED, "sta_pqstream_attend: too many key blocks per tile (n / block_n)");
+    return fail(STA_ERR_UNSUPPORTED, "sta_pqstream_attend: n_global / n_local too large");
   auto kern = pqstream_kernel<D, BN, F32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return fail(STA_ERR_CUDA, cudaGetErrorString(e));
