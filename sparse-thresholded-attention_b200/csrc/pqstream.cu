@@ -25,6 +25,8 @@ namespace {
 constexpr int T = 32;      // query tile (fixed by the reference's bit packing convention)
 constexpr int NW = 4;      // warps: two pairs, each pair covers the tile's 32 rows (16 per warp)
 constexpr int NTH = NW * 32;
+constexpr int SP = 32;     // key slots a warp pair scores per batch
+constexpr int SB = 2 * SP; // key slots per batch
 
 struct PQSP {
   const void* q;
@@ -124,23 +126,28 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   constexpr int HALF = D / 2;
   constexpr int NQ = F32 ? 3 : 2;  // pieces of the attend-geometry Q / K
   constexpr int NV = F32 ? 3 : 1;  // pieces of P / V
-  constexpr int KBUF = NQ * BN * LD, VBUF = NV * BN * LD;
+  constexpr int KBUF = NQ * SP * LD, VBUF = NV * SP * LD;
+  constexpr int NH = BN / 32;      // 32-key words per block
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* sQa = reinterpret_cast<__nv_bfloat16*>(smem);   // [NQ][T][LD]
-  __nv_bfloat16* sKa = sQa + NQ * T * LD;                         // [2 pairs][NQ][BN][LD]
-  __nv_bfloat16* sV = sKa + 2 * KBUF;                             // [2 pairs][NV][BN][LD]
+  __nv_bfloat16* sKa = sQa + NQ * T * LD;                         // [2 pairs][NQ][SP][LD]
+  __nv_bfloat16* sV = sKa + 2 * KBUF;                             // [2 pairs][NV][SP][LD]
   int* s_fcm = reinterpret_cast<int*>(sV + 2 * VBUF);             // forced blocks' max_i c_i
-  __shared__ uint32_t s_cw[2][BN];
-  __shared__ int s_list[NTH];
-  __shared__ float s_dl[NTH];
+  __shared__ int s_list[NTH];            // blocks with keeps of the current chunk (descending)
+  __shared__ float s_dl[NTH];            // their streamed offset d
+  __shared__ uint32_t s_bm[NTH][NH];     // their keys kept by some query (bit per key)
+  __shared__ int s_bo[NTH];              // exclusive prefix of their kept-key counts
+  __shared__ int s_sj[SB];               // pending slots: key, position, per-query keep bits
+  __shared__ float s_sp[SB];
+  __shared__ uint32_t s_scw[SB];
   __shared__ int s_extra[T];
   __shared__ int s_red[NW];
-  __shared__ float s_ml[32][4];
+  __shared__ float s_ml[T][2];
 
   const int t = blockIdx.x;
   const int64_t bh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int pair = warp >> 1, rw = warp & 1, ptid = tid & 63;
+  const int pair = warp >> 1, rw = warp & 1;
   const int g = lane >> 2, c4 = lane & 3;
   const int64_t N = p.N;
   const int64_t kvh = (bh / p.H) * p.Hkv + (bh % p.H) / (p.H / p.Hkv);
@@ -158,13 +165,16 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   const uint32_t* bits_row = p.bits + bh * p.head_stride + tri_tile_offset(t, T, p.qbase);
   const uint8_t* bmax_row = p.bmax + bh * p.bmax_stride + tri_tile_offset(t, 1, p.qbase / 32);
 
-  // keep bits (bit r = query row r) of the forced key j (global prefix, local window),
-  // restricted to causal, real rows
+  // keep bits (bit r = query row r) of key j: Kernel A's threshold decisions OR the forced keys
+  // (global prefix, local window), restricted to causal, real rows
   auto forced_rows = [&](int64_t j) -> uint32_t {
     if (!(j < p.n_global || (j >= loc_lo && j <= loc_hi))) return 0u;
     const int64_t dl = j - tstart;
     const uint32_t causal = dl <= 0 ? 0xffffffffu : (dl >= 32 ? 0u : ~((1u << dl) - 1u));
     return causal & rowvalid;
+  };
+  auto keep_word = [&](int64_t j) -> uint32_t {
+    return (j <= P_top ? __ldg(bits_row + j) : 0u) | forced_rows(j);
   };
   // forced blocks: [0, ng_blk) and [lb0, nblk); slot f of s_fcm
   const int ng_blk = (int)min((int64_t)nblk, ((int64_t)max(p.n_global, 0) + BN - 1) / BN);
@@ -180,7 +190,7 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
     const int b = f < nf_g ? f : lb0 + (f - nf_g);
     int cf = 0, cn = 0;
 #pragma unroll
-    for (int h = 0; h < BN / 32; ++h) {
+    for (int h = 0; h < NH; ++h) {
       const int64_t j = (int64_t)b * BN + h * 32 + lane;
       const uint32_t w = j <= P_top ? bits_row[j] : 0u;
       cn += __popc(transpose32(w));
@@ -232,9 +242,132 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   __nv_bfloat16* myK = sKa + pair * KBUF;
   __nv_bfloat16* myV = sV + pair * VBUF;
 
-  // ---- phase 2: descending blocks, NTH at a time: offsets d, then attend the blocks with keeps
-  // (the two warp pairs take alternate blocks and merge their softmax states at the end)
-  int carry_d = 0, n_pos = 0;
+  // attend one batch of SB pending slots (fewer at the end: the rest are padding, masked):
+  // every thread stages rotated K / V, then pair p scores slots [SP*p, SP*p + SP) for all rows
+  auto attend_batch = [&](int nb) {
+    for (int it = tid; it < SB * (HALF / 8); it += NTH) {
+      const int i = it / (HALF / 8), f0 = (it % (HALF / 8)) * 8;
+      const int64_t j = i < nb ? s_sj[i] : 0;
+      const float npk = i < nb ? s_sp[i] : 0.f;
+      __nv_bfloat16* dst = sKa + (i / SP) * KBUF + (i % SP) * LD;
+      rotate8<NQ, HALF>(kg + j * p.ksn, i < nb, f0, npk, p.inv_freq_c, 1.f, dst, SP * LD, p.rtab,
+                        table_index(npk, p.rtab_R, p.rtab_len));
+    }
+    for (int it = tid; it < SB * (D / 8); it += NTH) {
+      const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
+      const int64_t j = i < nb ? s_sj[i] : 0;
+      __nv_bfloat16* dst = sV + (i / SP) * VBUF + (i % SP) * LD + d0;
+      if (!F32) {
+        uint4 u = make_uint4(0u, 0u, 0u, 0u);
+        if (i < nb) u = *reinterpret_cast<const uint4*>(vg + j * p.vsn + d0);
+        *reinterpret_cast<uint4*>(dst) = u;
+      } else {
+        float x[8];
+        if (i < nb) {
+          load8(vg + j * p.vsn + d0, x);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) x[u] = 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          __nv_bfloat16 pc[NV];
+          split_pieces<NV>(x[u], pc);
+#pragma unroll
+          for (int q2 = 0; q2 < NV; ++q2) dst[q2 * SP * LD + u] = pc[q2];
+        }
+      }
+    }
+    __syncthreads();
+    float s[SP / 8][4];
+    score_tile<D, SP, NQ>(sQa, myK, s, rw);
+    float mxA = -INFINITY, mxB = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < SP / 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = nt * 8 + 2 * c4 + (e & 1);
+        const int row = e < 2 ? ra : rb;
+        const int si = pair * SP + col;
+        const bool keep = si < nb && ((s_scw[si] >> row) & 1u);
+        const float v = keep ? __fmul_rn(s[nt][e], p.sm_scale) : -INFINITY;
+        s[nt][e] = v;
+        if (e < 2) mxA = fmaxf(mxA, v);
+        else mxB = fmaxf(mxB, v);
+      }
+    }
+    mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
+    mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
+    mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
+    mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
+    const float mnA = fmaxf(mA, mxA), mnB = fmaxf(mB, mxB);
+    const float msA = mnA == -INFINITY ? 0.f : mnA;
+    const float msB = mnB == -INFINITY ? 0.f : mnB;
+    float sumA = 0.f, sumB = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < SP / 8; ++nt) {
+      s[nt][0] = expf(__fsub_rn(s[nt][0], msA));
+      s[nt][1] = expf(__fsub_rn(s[nt][1], msA));
+      s[nt][2] = expf(__fsub_rn(s[nt][2], msB));
+      s[nt][3] = expf(__fsub_rn(s[nt][3], msB));
+      sumA += s[nt][0] + s[nt][1];
+      sumB += s[nt][2] + s[nt][3];
+    }
+    sumA += __shfl_xor_sync(0xffffffffu, sumA, 1);
+    sumA += __shfl_xor_sync(0xffffffffu, sumA, 2);
+    sumB += __shfl_xor_sync(0xffffffffu, sumB, 1);
+    sumB += __shfl_xor_sync(0xffffffffu, sumB, 2);
+    const float alA = expf(__fsub_rn(mA, msA)), alB = expf(__fsub_rn(mB, msB));
+    lA = lA * alA + sumA;
+    lB = lB * alB + sumB;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= alA;
+      o[i][1] *= alA;
+      o[i][2] *= alB;
+      o[i][3] *= alB;
+    }
+    mA = mnA;
+    mB = mnB;
+    {
+      const int mi = lane >> 3, rr = lane & 7;
+#pragma unroll
+      for (int kk = 0; kk < SP / 16; ++kk) {
+        uint32_t pp[NV][4];
+        {
+          uint32_t x0[NV], x1[NV], x2[NV], x3[NV];
+          pack_pieces<NV>(s[2 * kk][0], s[2 * kk][1], x0);
+          pack_pieces<NV>(s[2 * kk][2], s[2 * kk][3], x1);
+          pack_pieces<NV>(s[2 * kk + 1][0], s[2 * kk + 1][1], x2);
+          pack_pieces<NV>(s[2 * kk + 1][2], s[2 * kk + 1][3], x3);
+#pragma unroll
+          for (int j = 0; j < NV; ++j) {
+            pp[j][0] = x0[j];
+            pp[j][1] = x1[j];
+            pp[j][2] = x2[j];
+            pp[j][3] = x3[j];
+          }
+        }
+        const int row = kk * 16 + rr + (mi & 1) * 8;
+#pragma unroll
+        for (int dp = 0; dp < D / 16; ++dp) {
+          const int col = (2 * dp + (mi >> 1)) * 8;
+          uint32_t v0[NV][2], v1[NV][2];
+#pragma unroll
+          for (int j = 0; j < NV; ++j)
+            ldsm_x4_t(smem_u32(myV + (j * SP + row) * LD + col), v0[j][0], v0[j][1], v1[j][0], v1[j][1]);
+          mma_pieces<NV>(o[2 * dp], pp, v0);
+          mma_pieces<NV>(o[2 * dp + 1], pp, v1);
+        }
+      }
+    }
+    __syncthreads();  // buffers and pending slots free again
+  };
+
+  // ---- phase 2: descending blocks, NTH per chunk: streamed offsets d, the blocks with keeps,
+  // their kept keys in (block, key) order appended to the pending slots, SB slots attended at a
+  // time
+  int carry_d = 0, n_pos = 0, n_pend = 0;
   for (int c0 = 0; c0 < nblk; c0 += NTH) {
     const int tb = c0 + tid;
     int adv = 0, use = 0, b = 0;
@@ -258,140 +391,61 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
       s_dl[eu] = (float)(carry_d + ed);
     }
     carry_d += tot_d;
-    for (int li0 = 0; li0 < n_use; li0 += 2) {
-      const int li = li0 + pair;
-      const bool active = li < n_use;
-      __syncthreads();  // list written / the pair's buffers free
-      int64_t sn = 0, hi_t = 0;
-      if (active) {
-        const int bb = s_list[li];
-        const float dpos = s_dl[li];
-        sn = (int64_t)bb * BN;
-        hi_t = min(P_top, sn + BN - 1);
-        for (int i = ptid; i < BN; i += 64) {
-          const int64_t j = sn + i;
-          s_cw[pair][i] = (j <= P_top ? bits_row[j] : 0u) | forced_rows(j);
-        }
-        // raw K rotated at the streamed positions, and V
-        for (int it = ptid; it < BN * (HALF / 8); it += 64) {
-          const int i = it / (HALF / 8), f0 = (it % (HALF / 8)) * 8;
-          const int64_t j = sn + i;
-          const float npk = -__fadd_rn(dpos, (float)(hi_t - j));
-          rotate8<NQ, HALF>(kg + (j < N ? j : 0) * p.ksn, j < N, f0, npk, p.inv_freq_c, 1.f,
-                            myK + i * LD, BN * LD, p.rtab, table_index(npk, p.rtab_R, p.rtab_len));
-        }
-        for (int it = ptid; it < BN * (D / 8); it += 64) {
-          const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
-          const int64_t j = sn + i;
-          __nv_bfloat16* dst = myV + i * LD + d0;
-          if (!F32) {
-            uint4 u = make_uint4(0u, 0u, 0u, 0u);
-            if (j < N) u = *reinterpret_cast<const uint4*>(vg + j * p.vsn + d0);
-            *reinterpret_cast<uint4*>(dst) = u;
-          } else {
-            float x[8];
-            if (j < N) {
-              load8(vg + j * p.vsn + d0, x);
-            } else {
+    __syncthreads();
+    // keys of each listed block kept by some query
+    for (int li = warp; li < n_use; li += NW) {
+      const int64_t sn = (int64_t)s_list[li] * BN;
 #pragma unroll
-              for (int u = 0; u < 8; ++u) x[u] = 0.f;
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              __nv_bfloat16 pc[NV];
-              split_pieces<NV>(x[u], pc);
-#pragma unroll
-              for (int q2 = 0; q2 < NV; ++q2) dst[q2 * BN * LD + u] = pc[q2];
-            }
-          }
-        }
+      for (int h = 0; h < NH; ++h) {
+        const uint32_t m = __ballot_sync(0xffffffffu, keep_word(sn + h * 32 + lane) != 0u);
+        if (lane == 0) s_bm[li][h] = m;
       }
+    }
+    __syncthreads();
+    int cnt = 0;
+    if (tid < n_use) {
+#pragma unroll
+      for (int h = 0; h < NH; ++h) cnt += __popc(s_bm[tid][h]);
+    }
+    int n_slots;
+    const int off = cta_excl_sum(cnt, s_red, n_slots);
+    if (tid < n_use) s_bo[tid] = off;
+    __syncthreads();
+    for (int s0 = 0; s0 < n_slots;) {
+      const int take = min(SB - n_pend, n_slots - s0);
+      for (int i = tid; i < take; i += NTH) {
+        const int gi = s0 + i;
+        int lo = 0, hi2 = n_use - 1;  // last listed block with s_bo <= gi
+        while (lo < hi2) {
+          const int mid = (lo + hi2 + 1) >> 1;
+          if (s_bo[mid] <= gi) lo = mid;
+          else hi2 = mid - 1;
+        }
+        int k = gi - s_bo[lo], kb = 0;
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          const uint32_t m = s_bm[lo][h];
+          const int c = __popc(m);
+          if (k >= 0 && k < c) kb = h * 32 + (int)__fns(m, 0, k + 1);
+          k -= c;
+        }
+        const int64_t sn = (int64_t)s_list[lo] * BN;
+        const int64_t j = sn + kb;
+        const int64_t hi_t = min(P_top, sn + BN - 1);
+        s_sj[n_pend + i] = (int)j;
+        s_sp[n_pend + i] = -__fadd_rn(s_dl[lo], (float)(hi_t - j));
+        s_scw[n_pend + i] = keep_word(j);
+      }
+      n_pend += take;
+      s0 += take;
       __syncthreads();
-      if (!active) continue;
-
-      float s[BN / 8][4];
-      score_tile<D, BN, NQ>(sQa, myK, s, rw);
-      float mxA = -INFINITY, mxB = -INFINITY;
-#pragma unroll
-      for (int nt = 0; nt < BN / 8; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int col = nt * 8 + 2 * c4 + (e & 1);
-          const int row = e < 2 ? ra : rb;
-          const bool keep = (s_cw[pair][col] >> row) & 1u;
-          const float v = keep ? __fmul_rn(s[nt][e], p.sm_scale) : -INFINITY;
-          s[nt][e] = v;
-          if (e < 2) mxA = fmaxf(mxA, v);
-          else mxB = fmaxf(mxB, v);
-        }
-      }
-      mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
-      mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
-      mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
-      mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
-      const float mnA = fmaxf(mA, mxA), mnB = fmaxf(mB, mxB);
-      const float msA = mnA == -INFINITY ? 0.f : mnA;
-      const float msB = mnB == -INFINITY ? 0.f : mnB;
-      float sumA = 0.f, sumB = 0.f;
-#pragma unroll
-      for (int nt = 0; nt < BN / 8; ++nt) {
-        s[nt][0] = expf(__fsub_rn(s[nt][0], msA));
-        s[nt][1] = expf(__fsub_rn(s[nt][1], msA));
-        s[nt][2] = expf(__fsub_rn(s[nt][2], msB));
-        s[nt][3] = expf(__fsub_rn(s[nt][3], msB));
-        sumA += s[nt][0] + s[nt][1];
-        sumB += s[nt][2] + s[nt][3];
-      }
-      sumA += __shfl_xor_sync(0xffffffffu, sumA, 1);
-      sumA += __shfl_xor_sync(0xffffffffu, sumA, 2);
-      sumB += __shfl_xor_sync(0xffffffffu, sumB, 1);
-      sumB += __shfl_xor_sync(0xffffffffu, sumB, 2);
-      const float alA = expf(__fsub_rn(mA, msA)), alB = expf(__fsub_rn(mB, msB));
-      lA = lA * alA + sumA;
-      lB = lB * alB + sumB;
-#pragma unroll
-      for (int i = 0; i < D / 8; ++i) {
-        o[i][0] *= alA;
-        o[i][1] *= alA;
-        o[i][2] *= alB;
-        o[i][3] *= alB;
-      }
-      mA = mnA;
-      mB = mnB;
-      {
-        const int mi = lane >> 3, rr = lane & 7;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          uint32_t pp[NV][4];
-          {
-            uint32_t x0[NV], x1[NV], x2[NV], x3[NV];
-            pack_pieces<NV>(s[2 * kk][0], s[2 * kk][1], x0);
-            pack_pieces<NV>(s[2 * kk][2], s[2 * kk][3], x1);
-            pack_pieces<NV>(s[2 * kk + 1][0], s[2 * kk + 1][1], x2);
-            pack_pieces<NV>(s[2 * kk + 1][2], s[2 * kk + 1][3], x3);
-#pragma unroll
-            for (int j = 0; j < NV; ++j) {
-              pp[j][0] = x0[j];
-              pp[j][1] = x1[j];
-              pp[j][2] = x2[j];
-              pp[j][3] = x3[j];
-            }
-          }
-          const int row = kk * 16 + rr + (mi & 1) * 8;
-#pragma unroll
-          for (int dp = 0; dp < D / 16; ++dp) {
-            const int col = (2 * dp + (mi >> 1)) * 8;
-            uint32_t v0[NV][2], v1[NV][2];
-#pragma unroll
-            for (int j = 0; j < NV; ++j)
-              ldsm_x4_t(smem_u32(myV + (j * BN + row) * LD + col), v0[j][0], v0[j][1], v1[j][0], v1[j][1]);
-            mma_pieces<NV>(o[2 * dp], pp, v0);
-            mma_pieces<NV>(o[2 * dp + 1], pp, v1);
-          }
-        }
+      if (n_pend == SB) {
+        attend_batch(SB);
+        n_pend = 0;
       }
     }
   }
+  if (n_pend > 0) attend_batch(n_pend);
   int n_adv;
   {
     int tot;
@@ -478,7 +532,7 @@ int launch_one(const PQSP& p, cudaStream_t stream) {
   const int64_t ng = (int64_t)(p.n_global > 0 ? p.n_global : 0);
   const int64_t nl = (int64_t)(p.n_local > 0 ? p.n_local : 0);
   const int64_t nfs_cap = (ng + BN - 1) / BN + (nl + T + BN - 1) / BN + 2;
-  const size_t smem = (size_t)(NQ * T + 2 * (NQ + NV) * BN) * LD * 2 + (size_t)nfs_cap * 4;
+  const size_t smem = (size_t)(NQ * T + 2 * (NQ + NV) * SP) * LD * 2 + (size_t)nfs_cap * 4;
   if (smem > 200 * 1024)
     return fail(STA_ERR_UNSUPPORTED, "sta_pqstream_attend: n_global / n_local too large");
   auto kern = pqstream_kernel<D, BN, F32>;
