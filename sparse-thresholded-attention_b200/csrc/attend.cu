@@ -20,7 +20,6 @@ namespace sta {
 
 namespace {
 
-constexpr int BK = 64;
 
 struct AttendP {
   const void* q;
@@ -49,29 +48,45 @@ struct AttendP {
   int64_t rtab_len;
 };
 
+// Roles: warps 0 .. T/16-1 consume (16 query rows each: QK, online softmax, PV); NPW producer
+// warps gather the next slot block (idx / positions / mask, K rotated at its position or copied
+// pre-rotated, V) into the other of two shared-memory stages, so loads and rotations overlap the
+// tensor-core work.  Stage hand-off: named barriers FULL(s) (producers arrive, consumers wait)
+// and EMPTY(s) (consumers arrive, producers wait).
+constexpr int NPW = 4;
+constexpr int kBarFull = 1, kBarEmpty = 3, kBarProd = 5;
+
 template <int D, int T, bool F32>
-__global__ void __launch_bounds__(T * 2)
+struct AttCfg {
+  static constexpr int BK = 32;              // slots per block (64 measured slower: 1 CTA / SM)
+  static constexpr int LD = D + 8;           // padded smem row (bf16 elements)
+  static constexpr int NQ = F32 ? 3 : 2;     // bf16 pieces of the rotated Q / K rows
+  static constexpr int NV = F32 ? 3 : 1;     // pieces of P and V (1: P rounded to bf16)
+  static constexpr int NCW = T / 16;         // consumer warps
+  static constexpr int NTH = (NCW + NPW) * 32;
+  static constexpr int KST = NQ * BK * LD;   // bf16 elements of one K stage
+  static constexpr int VST = NV * BK * LD;
+  static constexpr size_t SMEM = (size_t)(NQ * T * LD + 2 * (KST + VST)) * 2 + 2 * 3 * BK * 4;
+};
+
+template <int D, int T, bool F32>
+__global__ void __launch_bounds__(AttCfg<D, T, F32>::NTH)
 gather_attend_kernel(const AttendP p) {
+  using C = AttCfg<D, T, F32>;
   using TV = typename std::conditional<F32, float, __nv_bfloat16>::type;
-  constexpr int NW = T / 16;
-  constexpr int NTH = NW * 32;
-  constexpr int LD = D + 8;  // padded smem row (bf16 elements)
+  constexpr int BK = C::BK, LD = C::LD, NQ = C::NQ, NV = C::NV, NCW = C::NCW, NTH = C::NTH;
   constexpr int HALF = D / 2;
-  constexpr int NQ = F32 ? 3 : 2;  // bf16 pieces of the rotated Q / K rows
-  constexpr int NV = F32 ? 3 : 1;  // pieces of P and V (1: P rounded to bf16 like the reference)
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem);   // [NQ][T][LD]
-  __nv_bfloat16* sK = sQ + NQ * T * LD;                           // [NQ][BK][LD]
-  __nv_bfloat16* sV = sK + NQ * BK * LD;                          // [NV][BK][LD]
-  int* sIdx = reinterpret_cast<int*>(sV + NV * BK * LD);
-  float* sNpk = reinterpret_cast<float*>(sIdx + BK);
-  int* sMask = reinterpret_cast<int*>(sNpk + BK);
+  __nv_bfloat16* sK = sQ + NQ * T * LD;                           // [2][NQ][BK][LD]
+  __nv_bfloat16* sV = sK + 2 * C::KST;                            // [2][NV][BK][LD]
+  int* sIdx = reinterpret_cast<int*>(sV + 2 * C::VST);            // [2][BK]
+  float* sNpk = reinterpret_cast<float*>(sIdx + 2 * BK);          // [2][BK]
+  int* sMask = reinterpret_cast<int*>(sNpk + 2 * BK);             // [2][BK]
 
   const int t = blockIdx.x;
   const int64_t bh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, c4 = lane & 3;
-  const int mi = lane >> 3, rr = lane & 7;
   const int64_t N = p.N;
   const int64_t kvh = (bh / p.H) * p.Hkv + (bh % p.H) / (p.H / p.Hkv);
   const TV* qg = static_cast<const TV*>(p.q) + bh * p.qsh;
@@ -83,10 +98,10 @@ gather_attend_kernel(const AttendP p) {
   const float* npq_row = p.npq + row_base * T;
   const int32_t* mask_row = p.mask ? p.mask + row_base * p.k_max : nullptr;
   const bool use_mask = mask_row != nullptr;
-
-  // ---- Q prologue: rotate at newpos_q (or reuse the pre-rotated row), split, stage in smem
-  constexpr int C8 = HALF / 8;
   const bool direct = !F32 && p.direct;
+  constexpr int C8 = HALF / 8;
+
+  // ---- Q prologue (all warps): rotate at newpos_q (or reuse the pre-rotated row), split
   for (int it = tid; it < T * C8; it += NTH) {
     const int r = it / C8, f0 = (it % C8) * 8;
     const int64_t qp = p.qbase + (int64_t)t * T + r;  // absolute query position
@@ -100,7 +115,85 @@ gather_attend_kernel(const AttendP p) {
                         p.rtab, table_index(pos, p.rtab_R, p.rtab_len));
     }
   }
+  int nslots = p.k_max;
+  if (p.kept) {
+    const int ks = p.kept[row_base];
+    nslots = ks < p.k_max ? ks : p.k_max;
+  }
+  const int nblocks = (nslots + BK - 1) / BK;
+  __syncthreads();
 
+  if (warp >= NCW) {
+    // ================================================================ producers
+    const int ptid = tid - NCW * 32;
+    for (int ib = 0; ib < nblocks; ++ib) {
+      const int st = ib & 1;
+      if (ib >= 2) named_bar_sync(kBarEmpty + st, NTH);
+      int* mIdx = sIdx + st * BK;
+      float* mNpk = sNpk + st * BK;
+      int* mMask = sMask + st * BK;
+      for (int i = ptid; i < BK; i += NPW * 32) {
+        const int slot = ib * BK + i;
+        int id = (int)N;
+        float np = 0.f;
+        int mk = -1;
+        if (slot < p.k_max) {
+          id = idx_row[slot];
+          if (id < N) np = npk_row[slot];
+          if (use_mask) mk = mask_row[slot];
+        }
+        mIdx[i] = id;
+        mNpk[i] = np;
+        mMask[i] = mk;
+      }
+      named_bar_sync(kBarProd, NPW * 32);
+      __nv_bfloat16* kdst = sK + st * C::KST;
+      __nv_bfloat16* vdst = sV + st * C::VST;
+      for (int it = ptid; it < BK * C8; it += NPW * 32) {
+        const int i = it / C8, f0 = (it % C8) * 8;
+        const int id = mIdx[i];
+        const float pos = mNpk[i];
+        __nv_bfloat16* dst = kdst + i * LD;
+        if (direct && id < N && pos == __fmul_rn((float)id, p.ps_sel)) {
+          copy_rotated<HALF>(p.kh + (kvh * N + id) * D, p.kl + (kvh * N + id) * D, f0, dst, BK * LD);
+        } else {
+          rotate8<NQ, HALF>(kg + (int64_t)(id < N ? id : 0) * p.ksn, id < N, f0, pos, p.inv_freq,
+                            p.rope_scale, dst, BK * LD, p.rtab, table_index(pos, p.rtab_R, p.rtab_len));
+        }
+      }
+      for (int it = ptid; it < BK * (D / 8); it += NPW * 32) {
+        const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
+        const int id = mIdx[i];
+        __nv_bfloat16* dst = vdst + i * LD + d0;
+        if (!F32) {
+          uint4 u = make_uint4(0u, 0u, 0u, 0u);
+          if (id < N) u = *reinterpret_cast<const uint4*>(vg + (int64_t)id * p.vsn + d0);
+          *reinterpret_cast<uint4*>(dst) = u;
+        } else {
+          float x[8];
+          if (id < N) {
+            load8(vg + (int64_t)id * p.vsn + d0, x);
+          } else {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) x[u] = 0.f;
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            __nv_bfloat16 a[NV];
+            split_pieces<NV>(x[u], a);
+#pragma unroll
+            for (int j = 0; j < NV; ++j) dst[j * BK * LD + u] = a[j];
+          }
+        }
+      }
+      named_bar_arrive(kBarFull + st, NTH);
+    }
+    return;
+  }
+
+  // ================================================================== consumers
+  const int g = lane >> 2, c4 = lane & 3;
+  const int mi = lane >> 3, rr = lane & 7;
   const int ra = warp * 16 + g, rb = ra + 8;  // tile-local rows of this thread
   const int64_t qpa = p.qbase + (int64_t)t * T + ra, qpb = p.qbase + (int64_t)t * T + rb;
   float o[D / 8][4];
@@ -108,67 +201,13 @@ gather_attend_kernel(const AttendP p) {
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
 
-  int nslots = p.k_max;
-  if (p.kept) {
-    const int ks = p.kept[row_base];
-    nslots = ks < p.k_max ? ks : p.k_max;
-  }
-  for (int s0 = 0; s0 < nslots; s0 += BK) {
-    __syncthreads();
-    for (int i = tid; i < BK; i += NTH) {
-      const int slot = s0 + i;
-      int id = (int)N;
-      float np = 0.f;
-      int mk = -1;
-      if (slot < p.k_max) {
-        id = idx_row[slot];
-        if (id < N) np = npk_row[slot];
-        if (use_mask) mk = mask_row[slot];
-      }
-      sIdx[i] = id;
-      sNpk[i] = np;
-      sMask[i] = mk;
-    }
-    __syncthreads();
-    // gather K slots (pre-rotated rows where bit-identical, else rotate at newpos), gather V
-    for (int it = tid; it < BK * C8; it += NTH) {
-      const int i = it / C8, f0 = (it % C8) * 8;
-      const int id = sIdx[i];
-      const float pos = sNpk[i];
-      __nv_bfloat16* dst = sK + i * LD;
-      if (direct && id < N && pos == __fmul_rn((float)id, p.ps_sel)) {
-        copy_rotated<HALF>(p.kh + (kvh * N + id) * D, p.kl + (kvh * N + id) * D, f0, dst, BK * LD);
-      } else {
-        rotate8<NQ, HALF>(kg + (int64_t)(id < N ? id : 0) * p.ksn, id < N, f0, pos, p.inv_freq,
-                          p.rope_scale, dst, BK * LD, p.rtab, table_index(pos, p.rtab_R, p.rtab_len));
-      }
-    }
-    for (int it = tid; it < BK * (D / 8); it += NTH) {
-      const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
-      const int id = sIdx[i];
-      __nv_bfloat16* dst = sV + i * LD + d0;
-      if (!F32) {
-        uint4 u = make_uint4(0u, 0u, 0u, 0u);
-        if (id < N) u = *reinterpret_cast<const uint4*>(vg + (int64_t)id * p.vsn + d0);
-        *reinterpret_cast<uint4*>(dst) = u;
-      } else {
-        float x[8];
-        if (id < N) {
-          load8(vg + (int64_t)id * p.vsn + d0, x);
-        } else {
-#pragma unroll
-          for (int u = 0; u < 8; ++u) x[u] = 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          __nv_bfloat16 a[NV];
-          split_pieces<NV>(x[u], a);
-#pragma unroll
-          for (int j = 0; j < NV; ++j) dst[j * BK * LD + u] = a[j];
-        }
-      }
-    }
-    __syncthreads();
+  for (int ib = 0; ib < nblocks; ++ib) {
+    const int st = ib & 1;
+    named_bar_sync(kBarFull + st, NTH);
+    const __nv_bfloat16* cK = sK + st * C::KST;
+    const __nv_bfloat16* cV = sV + st * C::VST;
+    const int* cIdx = sIdx + st * BK;
+    const int* cMask = sMask + st * BK;
 
     float s[BK / 8][4];
 #pragma unroll
@@ -188,7 +227,7 @@ gather_attend_kernel(const AttendP p) {
         uint32_t b0[NQ][2], b1[NQ][2];
 #pragma unroll
         for (int j = 0; j < NQ; ++j)
-          ldsm_x4(smem_u32(sK + (j * BK + row) * LD + col), b0[j][0], b0[j][1], b1[j][0], b1[j][1]);
+          ldsm_x4(smem_u32(cK + (j * BK + row) * LD + col), b0[j][0], b0[j][1], b1[j][0], b1[j][1]);
         mma_pieces<NQ>(s[2 * np2], a, b0);
         mma_pieces<NQ>(s[2 * np2 + 1], a, b1);
       }
@@ -202,8 +241,8 @@ gather_attend_kernel(const AttendP p) {
         const int col = nt * 8 + 2 * c4 + (e & 1);
         const int row = e < 2 ? ra : rb;
         const int64_t qp = e < 2 ? qpa : qpb;
-        const int id = sIdx[col];
-        const bool keep = id < N && qp >= id && (!use_mask || ((sMask[col] >> row) & 1));
+        const int id = cIdx[col];
+        const bool keep = id < N && qp >= id && (!use_mask || ((cMask[col] >> row) & 1));
         const float v = keep ? __fmul_rn(s[nt][e], p.sm_scale) : -INFINITY;
         s[nt][e] = v;
         if (e < 2) mxA = fmaxf(mxA, v);
@@ -268,11 +307,12 @@ gather_attend_kernel(const AttendP p) {
         uint32_t v0[NV][2], v1[NV][2];
 #pragma unroll
         for (int j = 0; j < NV; ++j)
-          ldsm_x4_t(smem_u32(sV + (j * BK + row) * LD + col), v0[j][0], v0[j][1], v1[j][0], v1[j][1]);
+          ldsm_x4_t(smem_u32(cV + (j * BK + row) * LD + col), v0[j][0], v0[j][1], v1[j][0], v1[j][1]);
         mma_pieces<NV>(o[2 * dp], pp, v0);
         mma_pieces<NV>(o[2 * dp + 1], pp, v1);
       }
     }
+    if (ib + 2 < nblocks) named_bar_arrive(kBarEmpty + st, NTH);
   }
 
   // ---- epilogue
@@ -302,14 +342,12 @@ gather_attend_kernel(const AttendP p) {
 
 template <int D, int T, bool F32>
 int launch_one(const AttendP& p, cudaStream_t stream) {
-  constexpr int LD = D + 8;
-  constexpr int NQ = F32 ? 3 : 2, NV = F32 ? 3 : 1;
-  const size_t smem = (size_t)(NQ * T * LD + NQ * BK * LD + NV * BK * LD) * 2 + 3 * BK * 4;
+  using C = AttCfg<D, T, F32>;
   auto kern = gather_attend_kernel<D, T, F32>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
   if (e != cudaSuccess) return fail(STA_ERR_CUDA, cudaGetErrorString(e));
   dim3 grid((unsigned)p.nt, (unsigned)p.BH);
-  kern<<<grid, T * 2, smem, stream>>>(p);
+  kern<<<grid, C::NTH, C::SMEM, stream>>>(p);
   e = cudaGetLastError();
   return e == cudaSuccess ? STA_OK : fail(STA_ERR_CUDA, cudaGetErrorString(e));
 }
