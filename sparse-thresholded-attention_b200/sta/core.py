@@ -213,6 +213,71 @@ def forward(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, sm_scale=
 # -------------------------------------------------------------------------------------------
 # stage-level access (used by the parity tests to compare intermediates with the oracle)
 # -------------------------------------------------------------------------------------------
+def forward_host(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, groups=4,
+                 device=None, **kw):
+    """The op on HOST tensors, with the transfers overlapped with the compute.
+
+    q (Z,H,N,D), k / v (Z,Hkv,N,D) in pinned host memory (a copy is made otherwise).  The kv
+    heads are cut into ``groups`` equal groups (the largest divisor of Hkv not above it): group
+    g+1 is copied host -> device on one stream while group g computes on the current stream,
+    and each group's output is copied back on a third stream as soon as it is done.  Every
+    stage is independent per kv head, so the result equals one device call on the whole input.
+    Returns (out (Z,H,Nq,D) pinned host tensor, statistics on the device); the caller
+    synchronises (e.g. ``torch.cuda.current_stream().synchronize()``) before reading ``out``."""
+    for x in (q, k, v):
+        if x.is_cuda:
+            raise ValueError("forward_host takes host tensors; use forward for device tensors")
+    q, k, v = (x if x.is_pinned() else x.pin_memory() for x in (q, k, v))
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    Z, H, Nq, D = q.shape
+    Hk = k.shape[1]
+    if H % Hk:
+        raise ValueError("number of q heads must be a multiple of the number of kv heads")
+    G = H // Hk
+    ng = max(1, min(int(groups), Hk))
+    while Hk % ng:
+        ng -= 1
+    c = Hk // ng
+    qd = torch.empty(q.shape, dtype=q.dtype, device=dev)
+    kd = torch.empty(k.shape, dtype=k.dtype, device=dev)
+    vd = torch.empty(v.shape, dtype=v.dtype, device=dev)
+    out_h = torch.empty((Z, H, Nq, D), dtype=q.dtype, pin_memory=True)
+    comp = torch.cuda.current_stream(dev)
+    s_in = torch.cuda.Stream(dev)
+    s_out = torch.cuda.Stream(dev)
+    s_in.wait_stream(comp)   # device buffers were allocated on the current stream
+    s_out.wait_stream(comp)
+    ev_in = []
+    with torch.cuda.stream(s_in):
+        for g in range(ng):
+            hs, ks = slice(g * c * G, (g + 1) * c * G), slice(g * c, (g + 1) * c)
+            qd[:, hs].copy_(q[:, hs], non_blocking=True)
+            kd[:, ks].copy_(k[:, ks], non_blocking=True)
+            vd[:, ks].copy_(v[:, ks], non_blocking=True)
+            e = torch.cuda.Event()
+            e.record(s_in)
+            ev_in.append(e)
+    tau_h = torch.as_tensor(tau, dtype=torch.float32).reshape(-1)
+    stats = []
+    for g in range(ng):
+        hs, ks = slice(g * c * G, (g + 1) * c * G), slice(g * c, (g + 1) * c)
+        comp.wait_event(ev_in[g])
+        o, st, _ = forward(variant, qd[:, hs], kd[:, ks], vd[:, ks], tau_h[hs], ga, gc, **kw)
+        stats.append(st)
+        done = torch.cuda.Event()
+        done.record(comp)
+        s_out.wait_event(done)
+        with torch.cuda.stream(s_out):
+            out_h[:, hs].copy_(o, non_blocking=True)
+        o.record_stream(s_out)
+    for x in (qd, kd, vd):
+        x.record_stream(s_in)
+    comp.wait_stream(s_out)  # the caller's stream orders after the last copy back
+    st = {name: torch.cat([sg[name] for sg in stats], dim=1) for name in stats[0]
+          if torch.is_tensor(stats[0][name])}
+    return out_h, st
+
+
 def rope_split(x: torch.Tensor, g: Geometry):
     """x (heads, n, d) -> (hi, lo) bf16 rotated at the selection geometry."""
     x = _rows(x)

@@ -527,3 +527,26 @@ def test_query_slabs_reproduce_whole_sequence(case):
                 x = torch.where(x == s1, torch.full_like(x, N), x)
             assert torch.equal(x, sets[name][:, :, t0:t1]), (name, s0, s1)
     assert core.device_error() == 0
+
+
+@pytest.mark.parametrize("variant", ["shared", "pq_union", "pq_stream"])
+def test_forward_host_pipeline_equals_device_call(variant):
+    """Host buffers in, host output back, transfers overlapped by kv-head group: the result is
+    the device call's, bit for bit (every stage is independent per kv head)."""
+    H, Hk, N, D = 8, 4, 640, 128
+    q, k, v = make_inputs(SynthSpec(n_heads=H, n_kv_heads=Hk, seq_len=N, head_dim=D, seed=90,
+                                    n_planted=16, dtype=torch.bfloat16))
+    tau = torch.full((H,), 5.0)
+    invf, rs = yarn_inv_freq(D, 5e5, 4.0, 256)
+    ga = Geometry(invf, 1.0, rs)
+    gc = ga if variant == "shared" else Geometry(rope_inv_freq(D, 5e5))
+    T = 64 if variant == "shared" else 32
+    kw = dict(tile=T, k_max=256, select_score="freq" if variant == "shared" else "expmass")
+    ref, st_ref, _ = core.forward(variant, cu(q), cu(k), cu(v), tau, ga, gc, **kw)
+    out_h, st = core.forward_host(variant, q, k, v, tau, ga, gc, groups=2, **kw)
+    torch.cuda.synchronize()
+    assert not out_h.is_cuda
+    assert torch.equal(out_h, ref.cpu())
+    for name, x in st_ref.items():
+        if torch.is_tensor(x):
+            assert torch.equal(st[name], x), name
