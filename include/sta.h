@@ -414,6 +414,61 @@ int sta_pq_stream_forward(const sta_forward_args* a, void* workspace, size_t wor
 int sta_shared_forward_static(const sta_forward_args* a, void* stream);
 
 /* Error flag of the last bounded device wait on this device: 0 = none. */
+/* ---------------------------------------------------------------------------------------
+ * Decode: one query per head against the KV cache (keys 0 .. m-1, the query at position m-1).
+ * Replaces the per-query selection + attend of the reference's decode paths:
+ *   STA_DECODE_PI     _decode_build_sets + _decode_attend_torch
+ *                     (shared_selection_triton_exact.py:464-560): threshold keep, optional
+ *                     top-pct_decode of the passers, forced global / local / self, k_max cap by
+ *                     score (tie-inclusive cut), PI reposition with pos_scale_c;
+ *   STA_DECODE_RANK   _decode_build_sets_pq + _decode_attend_torch_pq
+ *                     (shared_selection_triton_perquery.py:652-740): full set, exact-budget cap
+ *                     by score (ties: lowest key index), dense-rank positions;
+ *   STA_DECODE_STREAM _decode_build_sets_pqs + _decode_attend_torch (pqstream_kernel.py:694-795):
+ *                     full set, no cap, streamed positions over block_n blocks, query at 0.
+ * Scores use the selection geometry (inv_freq_a, pos_scale_a, rope_scale_a); the attention uses
+ * (inv_freq_c, rope_scale_c) at the new positions; softmax and PV in fp32.
+ * ------------------------------------------------------------------------------------- */
+#define STA_DECODE_PI 0
+#define STA_DECODE_RANK 1
+#define STA_DECODE_STREAM 2
+
+typedef struct sta_decode_args {
+  const void* q; int64_t q_stride_h;                        /* (batch*n_heads, d) */
+  const void* k; int64_t k_stride_h; int64_t k_stride_n;    /* raw cache (batch*n_kv_heads, m, d) */
+  const void* v; int64_t v_stride_h; int64_t v_stride_n;
+  void* out;               /* (batch*n_heads, d), dtype */
+  int32_t dtype;
+  int64_t batch;
+  int64_t n_heads;
+  int64_t n_kv_heads;
+  int64_t m;               /* keys in the cache, the query's own included */
+  int32_t d;               /* 64 or 128 */
+  const float* tau;        /* (n_heads,) */
+  const float* inv_freq_a; float pos_scale_a; float rope_scale_a;
+  const float* inv_freq_c; float pos_scale_c; float rope_scale_c;
+  float sm_scale;
+  int32_t mode;            /* STA_DECODE_* */
+  int32_t n_global;
+  int32_t n_local;
+  int32_t k_max;           /* slot cap (PI, RANK); ignored by STREAM (every kept key) */
+  float pct_decode;        /* PI only: < 100 keeps the top pct of the threshold passers */
+  int32_t block_n;         /* STREAM: key block */
+  /* optional cos/sin tables (sta_rope_table) of the selection and attend geometries */
+  const void* rope_table_a; float rope_table_a_R; int64_t rope_table_a_len;
+  const void* rope_table_c; float rope_table_c_R; int64_t rope_table_c_len;
+  /* optional outputs: the slot set (heads, cap) with cap = k_max (PI, RANK) or m (STREAM) */
+  int32_t* idx_out;
+  float* newpos_k_out;
+  float* newpos_q_out;     /* (heads,) */
+  int32_t* kept_out;       /* (heads,) size of the final set */
+  int32_t* usize_out;      /* (heads,) threshold passers */
+} sta_decode_args;
+
+size_t sta_decode_workspace_bytes(const sta_decode_args* a);
+int sta_decode_forward(const sta_decode_args* a, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
 int sta_device_error(void* stream, int32_t* code_out);
 
 #ifdef __cplusplus

@@ -547,6 +547,13 @@ int sta_pq_stream_forward(const sta_forward_args* a, void* workspace, size_t wor
   return run_forward(a, kPQStream, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
+size_t sta_decode_workspace_bytes(const sta_decode_args* a) { return decode_workspace_bytes(a); }
+
+int sta_decode_forward(const sta_decode_args* a, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  return decode_forward(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
 int sta_device_error(void* stream, int32_t* code_out) {
   int* p = device_error_word();
   if (!p) return fail(STA_ERR_CUDA, "sta_device_error: symbol lookup failed");

@@ -30,6 +30,8 @@ int launch_build_sets_pq(const sta_build_pq_args* a, cudaStream_t stream);
 int launch_build_sets_chunk(const sta_build_chunk_args* a, cudaStream_t stream);
 int launch_gather_attend(const sta_attend_args* a, cudaStream_t stream);
 int launch_pqstream(const sta_pqstream_args* a, cudaStream_t stream);
+size_t decode_workspace_bytes(const sta_decode_args* a);
+int decode_forward(const sta_decode_args* a, void* ws, size_t ws_len, cudaStream_t stream);
 
 // cuTensorMapEncodeTiled obtained through the runtime's driver entry point
 bool make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t d, uint64_t n,

@@ -108,6 +108,25 @@ class ForwardArgs(ctypes.Structure):
                 ("dca_local_window", c_i32), ("q_pos_base", c_i64)]
 
 
+class DecodeArgs(ctypes.Structure):
+    _fields_ = [("q", c_vp), ("q_stride_h", c_i64),
+                ("k", c_vp), ("k_stride_h", c_i64), ("k_stride_n", c_i64),
+                ("v", c_vp), ("v_stride_h", c_i64), ("v_stride_n", c_i64),
+                ("out", c_vp), ("dtype", c_i32), ("batch", c_i64), ("n_heads", c_i64),
+                ("n_kv_heads", c_i64), ("m", c_i64), ("d", c_i32), ("tau", c_vp),
+                ("inv_freq_a", c_vp), ("pos_scale_a", c_f32), ("rope_scale_a", c_f32),
+                ("inv_freq_c", c_vp), ("pos_scale_c", c_f32), ("rope_scale_c", c_f32),
+                ("sm_scale", c_f32), ("mode", c_i32), ("n_global", c_i32), ("n_local", c_i32),
+                ("k_max", c_i32), ("pct_decode", c_f32), ("block_n", c_i32),
+                ("rope_table_a", c_vp), ("rope_table_a_R", c_f32), ("rope_table_a_len", c_i64),
+                ("rope_table_c", c_vp), ("rope_table_c_R", c_f32), ("rope_table_c_len", c_i64),
+                ("idx_out", c_vp), ("newpos_k_out", c_vp), ("newpos_q_out", c_vp),
+                ("kept_out", c_vp), ("usize_out", c_vp)]
+
+
+DECODE = {"pi": 0, "rank": 1, "stream": 2}
+
+
 # every symbol include/sta.h declares (checked by the CPU test suite)
 EXPORTED = ["sta_last_error", "sta_version", "sta_tri_head_stride", "sta_rope_split",
             "sta_select", "sta_build_sets", "sta_build_sets_pq", "sta_gather_attend",
@@ -115,7 +134,8 @@ EXPORTED = ["sta_last_error", "sta_version", "sta_tri_head_stride", "sta_rope_sp
             "sta_pq_union_workspace_bytes", "sta_pq_union_forward",
             "sta_pq_stream_workspace_bytes", "sta_pq_stream_forward", "sta_device_error",
             "sta_shared_forward_static", "sta_build_sets_chunk", "sta_chunk_workspace_bytes",
-            "sta_chunk_forward", "sta_rope_split_dca", "sta_rope_table", "sta_tri_head_stride_q"]
+            "sta_chunk_forward", "sta_rope_split_dca", "sta_rope_table", "sta_tri_head_stride_q",
+            "sta_decode_workspace_bytes", "sta_decode_forward"]
 
 _lib = None
 
@@ -157,6 +177,10 @@ def lib():
                                      c_i32, c_i32, c_i32, c_vp, c_vp, c_vp]
     L.sta_rope_table.restype = ctypes.c_int
     L.sta_rope_table.argtypes = [c_vp, c_i32, c_f32, c_f32, c_i64, c_vp, c_vp]
+    L.sta_decode_workspace_bytes.restype = ctypes.c_size_t
+    L.sta_decode_workspace_bytes.argtypes = [ctypes.POINTER(DecodeArgs)]
+    L.sta_decode_forward.restype = ctypes.c_int
+    L.sta_decode_forward.argtypes = [ctypes.POINTER(DecodeArgs), c_vp, ctypes.c_size_t, c_vp]
     L.sta_shared_forward_static.restype = ctypes.c_int
     L.sta_shared_forward_static.argtypes = [ctypes.POINTER(ForwardArgs), c_vp]
     L.sta_device_error.restype = ctypes.c_int

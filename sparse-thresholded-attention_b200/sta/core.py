@@ -278,6 +278,110 @@ def forward_host(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, grou
     return out_h, st
 
 
+_TABLES = {}
+
+
+def _rope_table(inv_freq: torch.Tensor, rope_scale: float, R: float, length: int):
+    """Cached (cos, sin) * rope_scale table at positions i / R, 0 <= i < length (sta_rope_table);
+    grown by doubling so that a decode loop builds it O(log n) times."""
+    key = (inv_freq.device, inv_freq.data_ptr(), inv_freq.numel(), float(rope_scale), float(R))
+    t = _TABLES.get(key)
+    if t is None or t[1] < length:
+        cap = max(length, 2 * (t[1] if t else 0), 1024)
+        half = inv_freq.numel()
+        buf = torch.empty((cap, half, 2), dtype=torch.float32, device=inv_freq.device)
+        L.check(L.lib().sta_rope_table(_p(inv_freq), 2 * half, float(rope_scale), float(R), cap,
+                                       _p(buf), _stream()), "sta_rope_table")
+        t = (buf, cap, inv_freq)  # keep inv_freq alive: its address is part of the key
+        _TABLES[key] = t
+    return t[0], t[1]
+
+
+def _table_R(pos_scale):
+    for r in (1, 2, 4):
+        if float(pos_scale) * r == 1.0:
+            return float(r)
+    return 0.0
+
+
+def decode(mode: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, n_global=32, n_local=32,
+           k_max=1024, pct_decode=100.0, block_n=32, sm_scale=None, keep_sets=False):
+    """One decode step: the query at position m-1 of every head against the cache.
+
+    mode: 'pi' (shared hooks: threshold + optional top-pct + forced + tie-inclusive k_max cap by
+    score + PI reposition, shared_selection_triton_exact.py:464-560), 'rank' (PQ-Union:
+    exact-budget cap, dense ranks, perquery.py:652-740) or 'stream' (PQ-Stream: no cap, streamed
+    positions, pqstream_kernel.py:694-795).  q (Z,H,D); k, v (Z,Hkv,m,D) raw cache (GQA-native).
+    ga: selection geometry; gc: attend geometry (pos_scale_c repositions in 'pi').
+    Returns (out (Z,H,D), stats {kept, usize} (Z,H) [+ sets idx / newpos_k / newpos_q])."""
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise ValueError("q, k, v must be CUDA tensors (there is no CPU path)")
+    if q.dim() != 3 or k.dim() != 4 or v.shape != k.shape:
+        raise ValueError("decode expects q (Z,H,D) and k, v (Z,Hkv,m,D)")
+    Z, H, D = q.shape
+    Hk, M = k.shape[1], k.shape[2]
+    if H % Hk or k.shape[0] != Z or k.shape[3] != D:
+        raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)}")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError("q, k, v must share one dtype")
+    dev = q.device
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    md = L.DECODE[mode]
+    tau_d = _dev_f32(tau, dev).reshape(-1)
+    if tau_d.numel() != H:
+        raise ValueError(f"tau must have one entry per q head ({H})")
+    ia, ic = _dev_f32(ga.inv_freq, dev), _dev_f32(gc.inv_freq, dev)
+    rs_c = float(gc.rope_scale) if mode == "pi" else 1.0
+    qr = q if q.stride(-1) == 1 and q.stride(0) == H * q.stride(1) else q.contiguous()
+    kr = k if k.stride(-1) == 1 else k.contiguous()
+    vr = v if v.stride(-1) == 1 else v.contiguous()
+    if kr.stride(0) != Hk * kr.stride(1) or vr.stride(0) != Hk * vr.stride(1):
+        kr, vr = kr.contiguous(), vr.contiguous()
+    out = torch.empty((Z, H, D), dtype=q.dtype, device=dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    st = {"kept": torch.empty((Z, H), **i32), "usize": torch.empty((Z, H), **i32)}
+    cap = M if mode == "stream" else int(k_max)
+    sets = {}
+    if keep_sets:
+        sets = {"idx": torch.empty((Z, H, cap), **i32),
+                "newpos_k": torch.empty((Z, H, cap), dtype=torch.float32, device=dev),
+                "newpos_q": torch.empty((Z, H), dtype=torch.float32, device=dev)}
+    a = L.DecodeArgs()
+    a.q, a.q_stride_h = qr.data_ptr(), qr.stride(1)
+    a.k, a.k_stride_h, a.k_stride_n = kr.data_ptr(), kr.stride(1), kr.stride(2)
+    a.v, a.v_stride_h, a.v_stride_n = vr.data_ptr(), vr.stride(1), vr.stride(2)
+    a.out = out.data_ptr()
+    a.dtype = dtype_code(q.dtype)
+    a.batch, a.n_heads, a.n_kv_heads, a.m, a.d = Z, H, Hk, M, D
+    a.tau = tau_d.data_ptr()
+    a.inv_freq_a, a.pos_scale_a, a.rope_scale_a = ia.data_ptr(), float(ga.pos_scale), float(ga.rope_scale)
+    a.inv_freq_c, a.pos_scale_c, a.rope_scale_c = ic.data_ptr(), float(gc.pos_scale), rs_c
+    a.sm_scale = float(sm_scale)
+    a.mode = md
+    a.n_global, a.n_local, a.k_max = int(n_global), int(n_local), int(k_max or 0)
+    a.pct_decode, a.block_n = float(pct_decode), int(block_n)
+    Ra = _table_R(ga.pos_scale)
+    if Ra:
+        ta, la = _rope_table(ia, float(ga.rope_scale), Ra, int(M * Ra) + 1)
+        a.rope_table_a, a.rope_table_a_R, a.rope_table_a_len = ta.data_ptr(), Ra, la
+    Rc = {"pi": _table_R(gc.pos_scale), "rank": 1.0, "stream": -1.0}[mode]
+    if Rc:
+        tc, lc = _rope_table(ic, rs_c, Rc, int(M * abs(Rc)) + 1)
+        a.rope_table_c, a.rope_table_c_R, a.rope_table_c_len = tc.data_ptr(), Rc, lc
+    a.kept_out, a.usize_out = st["kept"].data_ptr(), st["usize"].data_ptr()
+    if sets:
+        a.idx_out, a.newpos_k_out = sets["idx"].data_ptr(), sets["newpos_k"].data_ptr()
+        a.newpos_q_out = sets["newpos_q"].data_ptr()
+    nbytes = L.lib().sta_decode_workspace_bytes(ctypes.byref(a))
+    if nbytes == 0:
+        L.check(1, "sta_decode_workspace_bytes")
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    L.check(L.lib().sta_decode_forward(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()),
+                                       ctypes.c_size_t(nbytes), _stream()), "sta_decode_forward")
+    return out, st, sets
+
+
 def rope_split(x: torch.Tensor, g: Geometry):
     """x (heads, n, d) -> (hi, lo) bf16 rotated at the selection geometry."""
     x = _rows(x)

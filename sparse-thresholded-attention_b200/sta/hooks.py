@@ -5,78 +5,16 @@ perquery / pqstream variants): the patched ``LlamaAttention.forward`` projects q
 k/v in the KV cache, freezes the PI position scale at prefill and routes the prefill through
 the B200 op.  Differences: k/v are passed GQA-native (no ``repeat_kv`` copy).
 
-Decode (past_len > 0) is not on the accelerated path: it runs the reference's per-query torch
-rule (threshold + forced global/local/self + k_max cap by score + reposition) in torch, exactly
-as the reference's default ``decode_backend="torch"`` does.
+Decode (past_len > 0) and the per-query prefill mode run the reference's per-query rule
+(threshold + optional top-pct + forced global/local/self + k_max cap by score + PI reposition,
+shared_selection_triton_exact.py:464-560) on the device: ``sta.core.decode``, one launch sequence
+per query position, GQA-native.
 """
 from __future__ import annotations
 
 import math
 
 import torch
-
-
-def _rope(x, pos, inv_freq, rope_scale):
-    half = x.shape[-1] // 2
-    ang = pos[..., None].to(torch.float32) * inv_freq.to(torch.float32)
-    c = torch.cos(ang) * rope_scale
-    s = torch.sin(ang) * rope_scale
-    x1, x2 = x[..., :half].float(), x[..., half:].float()
-    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
-
-
-@torch.no_grad()
-def decode_step(q, K, V, tau, q_pos, sel, att, n_global, n_local, k_max, pct_decode=100.0,
-                reposition="pi", sm_scale=None):
-    """One decode query per head (torch).  q (H,D); K, V (H,M,D) (GQA already expanded).
-    sel / att: (inv_freq, pos_scale, rope_scale) of the selection and attend geometries.
-    reposition: "pi" (newpos = rank + cummax(pos*pos_scale_c - rank)) or "rank" (dense ranks)."""
-    H, M, D = K.shape
-    dev = K.device
-    if sm_scale is None:
-        sm_scale = 1.0 / math.sqrt(D)
-    ia, psa, rsa = sel
-    ic, psc, rsc = att
-    pos = torch.arange(M, device=dev)
-    qs = _rope(q, torch.tensor(float(q_pos) * psa, device=dev), ia.to(dev), rsa)
-    ks = _rope(K, pos.float() * psa, ia.to(dev), rsa)
-    score = torch.einsum("hd,hmd->hm", qs, ks) * sm_scale
-    m = score.max(-1).values
-    keep = score >= (m - tau.to(dev).float())[:, None]
-    forced = torch.zeros(M, dtype=torch.bool, device=dev)
-    forced[:min(n_global, M)] = True
-    forced[max(0, q_pos - n_local + 1):q_pos + 1] = True
-    forced[q_pos] = True
-    if pct_decode < 100.0:
-        n_pass = keep.sum(-1)
-        b = torch.ceil(pct_decode / 100.0 * n_pass).clamp(min=1).long()
-        sp = torch.where(keep, score, torch.full_like(score, -math.inf))
-        cut = torch.gather(torch.sort(sp, -1, descending=True).values, -1,
-                           (b - 1).clamp(0, M - 1)[:, None])
-        keep = keep & (score >= cut)
-    kp = keep | forced[None]
-    nf = int(forced.sum())
-    bud = k_max - nf
-    nonf = kp & ~forced[None]
-    snf = torch.where(nonf, score, torch.full_like(score, -math.inf))
-    ci = min(max(bud - 1, 0), M - 1)
-    cutc = torch.sort(snf, -1, descending=True).values[:, ci:ci + 1]
-    kept_nf = nonf & (score >= cutc) if bud > 0 else torch.zeros_like(nonf)
-    final = torch.where((kp.sum(-1) > k_max)[:, None], forced[None] | kept_nf, kp)
-    rank0 = (final.int().cumsum(-1) - 1).float()
-    if reposition == "pi":
-        cr = torch.where(final, pos.float()[None] * psc - rank0, torch.full_like(rank0, -math.inf))
-        newpos = rank0 + torch.cummax(cr, -1).values
-    else:
-        newpos = rank0
-    out = torch.empty((H, D), dtype=q.dtype, device=dev)
-    for h in range(H):
-        kk = final[h].nonzero().squeeze(-1)
-        qr = _rope(q[h], newpos[h, q_pos], ic.to(dev), rsc)
-        kr = _rope(K[h, kk], newpos[h, kk], ic.to(dev), rsc)
-        a = torch.softmax((kr @ qr) * sm_scale, -1)
-        out[h] = (a[:, None] * V[h, kk].float()).sum(0).to(q.dtype)
-    return out
 
 
 def _rope_theta(cfg):
@@ -172,17 +110,16 @@ def make_shared_installer(geom, attention_fn, select_score=False, hybrid=False):
                  self.spi_last_overflow, self.spi_last_kpct_meas,
                  self.spi_last_overflow20) = res[1:]
             else:
-                G = q.shape[1] // k.shape[1]
-                Kf = k[0].repeat_interleave(G, 0)
-                Vf = v[0].repeat_interleave(G, 0)
+                from .core import Geometry, decode
                 outs = []
                 for i in range(N):
                     P = past_len + i
-                    outs.append(decode_step(q[0, :, i], Kf[:, :P + 1], Vf[:, :P + 1],
-                                            self.tau_head_vec, P, (inv_a, psa, rsa),
-                                            (inv_c, psc, rsc), self.spi_ng, self.spi_nl,
-                                            self.spi_kmax, self.spi_pct_decode, "pi",
-                                            self.scaling))
+                    o, _, _ = decode("pi", q[:, :, i], k[:, :, :P + 1], v[:, :, :P + 1],
+                                     self.tau_head_vec, Geometry(inv_a, psa, rsa),
+                                     Geometry(inv_c, psc, rsc), n_global=self.spi_ng,
+                                     n_local=self.spi_nl, k_max=self.spi_kmax,
+                                     pct_decode=self.spi_pct_decode, sm_scale=self.scaling)
+                    outs.append(o[0])
                 out = torch.stack(outs, 1).unsqueeze(0)
             attn = out.transpose(1, 2).reshape(B, N, -1).contiguous()
             return self.o_proj(attn), None

@@ -247,6 +247,44 @@ def gen_dca_tables(case, chunk_size, local_window, pretrain, seq_len, dim=64):
                           k_cos=rot.k_cos_cached, k_sin=rot.k_sin_cached))
 
 
+def gen_decode(case, mode, H, M, D, seed, k_max=64, pct_decode=100.0, block_n=32, pos_scale=1.0,
+               rope_scale=1.0, geom="pi", tau_val=5.0):
+    """One decode step of the reference's torch decode paths: the query at position M-1 against
+    the cache 0..M-1 (selection sets + attention output)."""
+    q, k, v = inputs(H, M, D, seed, torch.float32, planted=8)
+    qd, K, V = q[0, :, M - 1].contiguous(), k[0].contiguous(), v[0].contiguous()
+    tau = torch.full((H,), float(tau_val))
+    invf = rope_inv_freq(D, 1e4)
+    sm = 1.0 / D ** 0.5
+    if geom == "yarn":
+        invf, rope_scale = yarn_inv_freq(D, 5e5, 4.0, 128)
+    ng, nl, qpos = 32, 32, M - 1
+    if mode == "pi":
+        ref = __import__("shared_selection_triton_exact")
+        idx, npk, npq = ref._decode_build_sets(qd, K, tau, invf, qpos, pos_scale, rope_scale, sm,
+                                               ng, nl, k_max, pct_decode)
+        out = ref._decode_attend_torch(qd, K, V, idx, npk, npq, invf, rope_scale, sm)
+        invf_c, rs_c = invf, rope_scale
+    elif mode == "rank":
+        ref = __import__("shared_selection_triton_perquery")
+        idx, npk, npq = ref._decode_build_sets_pq(qd, K, tau, invf, qpos, pos_scale, rope_scale,
+                                                  sm, ng, nl, k_max)
+        invf_c, rs_c = rope_inv_freq(D, 1e4), 1.0
+        out = ref._decode_attend_torch_pq(qd, K, V, idx, npk, npq, invf_c, sm)
+    else:
+        ref = __import__("pqstream_kernel")
+        idx, npk, npq = ref._decode_build_sets_pqs(qd, K, tau, invf, qpos, pos_scale, rope_scale,
+                                                   sm, ng, nl, block_n)
+        invf_c, rs_c = rope_inv_freq(D, 1e4), 1.0
+        out = ref._decode_attend_torch(qd, K, V, idx, npk, npq, invf_c, sm)
+    meta = dict(kind="decode", mode=mode, H=H, M=M, D=D, seed=seed, k_max=k_max,
+                pct_decode=pct_decode, block_n=block_n, pos_scale=pos_scale,
+                rope_scale=float(rope_scale), rope_scale_c=float(rs_c), n_global=ng, n_local=nl,
+                tau=float(tau_val))
+    save(case, meta, dict(q=qd, k=K, v=V, tau=tau, inv_freq_a=invf, inv_freq_c=invf_c, idx=idx,
+                          newpos_k=npk, newpos_q=npq, out=out))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -290,6 +328,16 @@ def main():
     gen_pqstream("pqstream_full_f32", 2, 256, 64, 32, f32, pos_advance="full")
     gen_pqstream("pqstream_bn64_f32", 2, 288, 64, 33, f32, block_n=64, geom="yarn")
     gen_pqstream("pqstream_noskip_f32", 2, 256, 64, 34, f32, use_skip=False, pos_scale=0.5)
+    # decode: one query per head against the cache (the reference's torch decode rules)
+    gen_decode("decode_pi_cap_f32", "pi", 3, 700, 64, 51, k_max=96, pos_scale=0.5, tau_val=12.0)
+    gen_decode("decode_pi_pct_f32", "pi", 2, 523, 128, 52, k_max=4096, pct_decode=50.0,
+               tau_val=12.0)
+    gen_decode("decode_pi_yarn_f32", "pi", 2, 640, 64, 53, k_max=128, geom="yarn")
+    gen_decode("decode_rank_cap_f32", "rank", 3, 700, 64, 54, k_max=80, pos_scale=0.5,
+               tau_val=12.0)
+    gen_decode("decode_stream_bn32_f32", "stream", 2, 777, 64, 55, tau_val=9.0)
+    gen_decode("decode_stream_bn64_f32", "stream", 2, 600, 128, 56, block_n=64, geom="yarn",
+               tau_val=9.0)
 
 
 if __name__ == "__main__":

@@ -550,3 +550,59 @@ def test_forward_host_pipeline_equals_device_call(variant):
     for name, x in st_ref.items():
         if torch.is_tensor(x):
             assert torch.equal(st[name], x), name
+
+
+# ---------------------------------------------------------------------------------------------
+# decode (one query per head against the cache) vs the reference's torch decode rules
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("name", names("decode_"))
+def test_decode_vs_reference(name):
+    meta, a = load(name)
+    M, D = meta["M"], meta["D"]
+    q, k, v = cu(a["q"])[None], cu(a["k"])[None], cu(a["v"])[None]
+    mode = meta["mode"]
+    ga = Geometry(torch.from_numpy(a["inv_freq_a"]), meta["pos_scale"], meta["rope_scale"])
+    gc = Geometry(torch.from_numpy(a["inv_freq_c"]), meta["pos_scale"], meta["rope_scale_c"])
+    out, st, sets = core.decode(mode, q, k, v, torch.from_numpy(a["tau"]), ga, gc,
+                                n_global=meta["n_global"], n_local=meta["n_local"],
+                                k_max=meta["k_max"], pct_decode=meta["pct_decode"],
+                                block_n=meta["block_n"], keep_sets=True)
+    cap = min(sets["idx"].shape[-1], a["idx"].shape[1])
+    np.testing.assert_array_equal(sets["idx"][0, :, :cap].cpu().numpy(), a["idx"][:, :cap])
+    np.testing.assert_array_equal(sets["newpos_k"][0, :, :cap].cpu().numpy(),
+                                  a["newpos_k"][:, :cap])
+    np.testing.assert_array_equal(sets["newpos_q"][0].cpu().numpy(), a["newpos_q"])
+    assert np.abs(out[0].cpu().numpy() - a["out"]).max() <= F32_TOL
+
+
+@pytest.mark.parametrize("mode", ["pi", "rank", "stream"])
+def test_decode_bf16_gqa_vs_oracle(mode):
+    H, Hk, M, D = 8, 2, 3001, 128
+    q, k, v = make_inputs(SynthSpec(n_heads=H, n_kv_heads=Hk, seq_len=M, head_dim=D, seed=95,
+                                    n_planted=32, dtype=torch.bfloat16))
+    tau = torch.full((H,), 8.0)
+    invf, rs = yarn_inv_freq(D, 5e5, 4.0, 1024)
+    ga = Geometry(invf, 1.0, rs)
+    gc = Geometry(invf, 1.0, rs) if mode == "pi" else Geometry(rope_inv_freq(D, 5e5))
+    kw = dict(n_global=32, n_local=32, k_max=160, block_n=32)
+    out, st, sets = core.decode(mode, cu(q[:, :, M - 1]), cu(k), cu(v), tau, ga, gc,
+                                keep_sets=True, **kw)
+    G = H // Hk
+    qx = q[0, :, M - 1].float().numpy()
+    kx = np.repeat(k[0].float().numpy(), G, 0)
+    vx = np.repeat(v[0].float().numpy(), G, 0)
+    sm = 1.0 / math.sqrt(D)
+    if mode == "pi":
+        o = oracle.decode_pi(qx, kx, vx, tau.numpy(), invf.numpy(), 1.0, rs, sm, 32, 32, 160)
+    elif mode == "rank":
+        o = oracle.decode_rank(qx, kx, vx, tau.numpy(), invf.numpy(), gc.inv_freq.numpy(), 1.0,
+                               rs, sm, 32, 32, 160)
+    else:
+        o = oracle.decode_stream(qx, kx, vx, tau.numpy(), invf.numpy(), gc.inv_freq.numpy(),
+                                 1.0, rs, sm, 32, 32, 32)
+    idx = sets["idx"][0].cpu().numpy()
+    same = (idx == o[1][:, :idx.shape[1]]).all(1)
+    assert same.sum() >= H - 1, same          # a boundary key may flip on one head
+    err = np.abs(out[0].float().cpu().numpy() - o[0])[same]
+    assert err.max() <= BF16_MAX and err.mean() <= BF16_MEAN, (err.max(), err.mean())
+    assert int(st["kept"].min()) >= 64        # the forced keys at least

@@ -8,6 +8,7 @@ match within the fp32 / bf16 tolerances the parity protocol states.
 """
 import glob
 import json
+import math
 import os
 
 import numpy as np
@@ -231,3 +232,42 @@ def test_dca_positions_match_reference_tables():
     np.testing.assert_allclose(sc, a["qc_cos"], atol=2e-6)
     oc, _ = tab(qo[:1])                        # older chunks: the qc table at offset L - 1
     np.testing.assert_allclose(oc[0], a["qc_cos"][L - 1], atol=2e-6)
+
+
+# ---------------------------------------------------------------------------------------------
+# decode: the oracle's per-query rules against the reference's torch decode paths
+# ---------------------------------------------------------------------------------------------
+def _decode_case(name):
+    z = np.load(os.path.join(HERE, "golden", name + ".npz"))
+    meta = json.loads(str(z["meta"]))
+    return meta, {k: z[k] for k in z.files if k != "meta"}
+
+
+def run_decode_oracle(meta, a):
+    sm = 1.0 / math.sqrt(meta["D"])
+    if meta["mode"] == "pi":
+        return oracle.decode_pi(a["q"], a["k"], a["v"], a["tau"], a["inv_freq_a"],
+                                meta["pos_scale"], meta["rope_scale"], sm, meta["n_global"],
+                                meta["n_local"], meta["k_max"], meta["pct_decode"])
+    if meta["mode"] == "rank":
+        return oracle.decode_rank(a["q"], a["k"], a["v"], a["tau"], a["inv_freq_a"],
+                                  a["inv_freq_c"], meta["pos_scale"], meta["rope_scale"], sm,
+                                  meta["n_global"], meta["n_local"], meta["k_max"])
+    return oracle.decode_stream(a["q"], a["k"], a["v"], a["tau"], a["inv_freq_a"],
+                                a["inv_freq_c"], meta["pos_scale"], meta["rope_scale"], sm,
+                                meta["n_global"], meta["n_local"], meta["block_n"])
+
+
+@pytest.mark.parametrize("name", sorted(os.path.basename(p)[:-4] for p in
+                                        glob.glob(os.path.join(HERE, "golden", "decode_*.npz"))))
+def test_decode_oracle_matches_reference(name):
+    meta, a = _decode_case(name)
+    out, idx, npk, npq = run_decode_oracle(meta, a)
+    # the stream rule pads its slot buffer to a multiple of 1024 (pqstream_kernel.py:756-757):
+    # compare the common slots, the rest must be padding
+    cap = min(a["idx"].shape[1], idx.shape[1])
+    np.testing.assert_array_equal(idx[:, :cap], a["idx"][:, :cap])
+    np.testing.assert_array_equal(npk[:, :cap], a["newpos_k"][:, :cap])
+    assert (a["idx"][:, cap:] == meta["M"]).all() and (idx[:, cap:] == meta["M"]).all()
+    np.testing.assert_array_equal(npq, a["newpos_q"])
+    assert np.abs(out - a["out"]).max() <= 1e-5
