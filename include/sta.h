@@ -425,13 +425,19 @@ int sta_shared_forward_static(const sta_forward_args* a, void* stream);
  *                     (shared_selection_triton_perquery.py:652-740): full set, exact-budget cap
  *                     by score (ties: lowest key index), dense-rank positions;
  *   STA_DECODE_STREAM _decode_build_sets_pqs + _decode_attend_torch (pqstream_kernel.py:694-795):
- *                     full set, no cap, streamed positions over block_n blocks, query at 0.
+ *                     full set, no cap, streamed positions over block_n blocks, query at 0;
+ *   STA_DECODE_CHUNK  _decode_build_sets_chunk + _decode_attend_torch_pq
+ *                     (shared_selection_triton_chunked.py:412-483): chunks of chunk_size keys
+ *                     ranked by the summed (or mean) exp(s - m) / keep count of their passers,
+ *                     forced chunks + the top n_chunk others (ties: lowest chunk), self, dense
+ *                     ranks.
  * Scores use the selection geometry (inv_freq_a, pos_scale_a, rope_scale_a); the attention uses
  * (inv_freq_c, rope_scale_c) at the new positions; softmax and PV in fp32.
  * ------------------------------------------------------------------------------------- */
 #define STA_DECODE_PI 0
 #define STA_DECODE_RANK 1
 #define STA_DECODE_STREAM 2
+#define STA_DECODE_CHUNK 3
 
 typedef struct sta_decode_args {
   const void* q; int64_t q_stride_h;                        /* (batch*n_heads, d) */
@@ -463,6 +469,11 @@ typedef struct sta_decode_args {
   float* newpos_q_out;     /* (heads,) */
   int32_t* kept_out;       /* (heads,) size of the final set */
   int32_t* usize_out;      /* (heads,) threshold passers */
+  /* CHUNK only */
+  int32_t chunk_size;
+  int32_t n_chunk;
+  int32_t chunk_agg;       /* 0 = sum, 1 = mean */
+  int32_t select_score;    /* STA_SCORE_FREQ ranks by keep count, otherwise by exp(s - m) */
 } sta_decode_args;
 
 size_t sta_decode_workspace_bytes(const sta_decode_args* a);

@@ -5,6 +5,8 @@
 //   RANK    _decode_build_sets_pq + _decode_attend_torch_pq,
 //           shared_selection_triton_perquery.py:652-740
 //   STREAM  _decode_build_sets_pqs + _decode_attend_torch, pqstream_kernel.py:694-795
+//   CHUNK   _decode_build_sets_chunk + _decode_attend_torch_pq,
+//           shared_selection_triton_chunked.py:412-483
 // and the score kernels _decode_select_kernel (shared_selection_triton_exact.py:211-247 and
 // siblings).  Three launches:
 //   decode_score_kernel   one warp per key, all q heads of its kv head: raw K row read once
@@ -50,6 +52,7 @@ struct DecP {
   float psc, rsc;
   float sm;
   int mode, n_global, n_local, k_max, bn;
+  int C, n_chunk, mean_agg, weighted;  // CHUNK
   float pct;
   int64_t cap, nblk;
   const float2* ta;
@@ -65,6 +68,9 @@ struct DecP {
   int32_t* kept;
   int32_t* usize;
   float* dblk;
+  float* crank;     // CHUNK: (BH, nC) chunk rank values
+  uint8_t* cflag;   // CHUNK: (BH, nC) bit0 candidate, bit1 forced, bit2 selected
+  int64_t nC;
 };
 
 template <typename TV>
@@ -324,7 +330,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(const DecP p
   const int64_t n_forced = blk_sum<kSelThreads>(nf, sh_i);
 
   // k_max cap by score
-  const bool over = p.mode != STA_DECODE_STREAM && count > p.k_max;
+  const bool over = (p.mode == STA_DECODE_PI || p.mode == STA_DECODE_RANK) && count > p.k_max;
   bool cap_none = false;  // over and no budget: forced keys only
   float cut_c = -INFINITY;
   int64_t need_eq = 0;
@@ -337,6 +343,64 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(const DecP p
       kth_largest(sc, m, bud, [&](int64_t j) { return keep(j) && !forced(j); }, hist, cut_c, gt);
       need_eq = bud - gt;  // RANK: exact budget, ties to the lowest key indices
     }
+  }
+
+  // CHUNK: rank chunks by the passers' summed (or mean) exp(s - m) / keep count; forced chunks
+  // (global prefix, local window) plus the top n_chunk others, ties to the lowest chunk index
+  float* crank = p.crank ? p.crank + bh * p.nC : nullptr;
+  uint8_t* cflag = p.cflag ? p.cflag + bh * p.nC : nullptr;
+  if (p.mode == STA_DECODE_CHUNK) {
+    const int64_t C = p.C;
+    const int64_t gch = ((int64_t)max(p.n_global, 0) + C - 1) / C;
+    const int64_t lo_c = loc_lo / C, hi_c = qpos / C;
+    int ncand = 0;
+    for (int64_t c = tid; c < p.nC; c += kSelThreads) {
+      float mass = 0.f;
+      int cnt = 0;
+      const int64_t e = min((c + 1) * C, m);
+      for (int64_t j = c * C; j < e; ++j) {
+        if (sc[j] >= thr) {
+          mass = __fadd_rn(mass, p.weighted ? expf(__fsub_rn(sc[j], tot)) : 1.f);
+          ++cnt;
+        }
+      }
+      if (p.mean_agg) mass = __fdiv_rn(mass, (float)(cnt > 1 ? cnt : 1));
+      const bool visible = c * C <= qpos;
+      const bool fc = (c < gch || (c >= lo_c && c <= hi_c)) && visible;
+      crank[c] = mass;
+      cflag[c] = fc ? 2 : (visible ? 1 : 0);
+      ncand += !fc && visible;
+    }
+    const int64_t n_cand = blk_sum<kSelThreads>(ncand, sh_i);  // (syncs: the arrays are visible)
+    const int64_t n_take = p.n_chunk < p.nC ? p.n_chunk : p.nC;
+    const bool all = n_cand <= n_take;
+    float cut = 0.f;
+    int64_t need = 0;
+    if (!all && n_take > 0) {
+      int64_t gt;
+      kth_largest(crank, p.nC, n_take, [&](int64_t c) { return cflag[c] == 1; }, hist, cut, gt);
+      need = n_take - gt;
+    }
+    int64_t tie_carry = 0;
+    for (int64_t c0 = 0; c0 < p.nC; c0 += kSelThreads) {
+      const int64_t c = c0 + tid;
+      int tie = 0;
+      bool sel = false;
+      if (c < p.nC) {
+        const uint8_t f = cflag[c];
+        if (f == 2) sel = true;
+        else if (f == 1 && n_take > 0) {
+          if (all || crank[c] > cut) sel = true;
+          else if (crank[c] == cut) tie = 1;
+        }
+      }
+      int tt;
+      const int tr = blk_excl_sum<kSelThreads>(tie, sh_i, tt);
+      if (tie && tie_carry + tr < need) sel = true;
+      if (c < p.nC && sel) cflag[c] |= 4;
+      tie_carry += tt;
+    }
+    __syncthreads();
   }
 
   // streamed offsets: d_b = kept keys in the blocks after b (nearer the query)
@@ -377,7 +441,9 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(const DecP p
       const int64_t j = j0 + i;
       if (j >= m) continue;
       bool f;
-      if (!over) {
+      if (p.mode == STA_DECODE_CHUNK) {
+        f = (cflag[j / p.C] & 4) || j == qpos;
+      } else if (!over) {
         f = base_final(j);
       } else if (forced(j)) {
         f = true;
@@ -428,7 +494,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(const DecP p
       if (p.mode == STA_DECODE_PI) {
         run = fmaxf(run, cr[i]);
         np2 = __fadd_rn(rank0f[i], run);
-      } else if (p.mode == STA_DECODE_RANK) {
+      } else if (p.mode == STA_DECODE_RANK || p.mode == STA_DECODE_CHUNK) {
         np2 = rank0f[i];
       } else {
         const int64_t b = j / p.bn;
@@ -535,8 +601,8 @@ __global__ void __launch_bounds__(kAttThreads) decode_attend_kernel(const DecP p
 }
 
 struct DecLayout {
-  size_t scores, idx, npk, npq, kept, usize, dblk, total;
-  int64_t cap, nblk;
+  size_t scores, idx, npk, npq, kept, usize, dblk, crank, cflag, total;
+  int64_t cap, nblk, nC;
 };
 
 inline size_t al(size_t x) { return (x + 255) & ~size_t(255); }
@@ -559,6 +625,9 @@ DecLayout dec_layout(const sta_decode_args* a) {
   L.kept = take((size_t)BH * 4);
   L.usize = take((size_t)BH * 4);
   L.dblk = take((size_t)BH * (L.nblk > 0 ? L.nblk : 1) * 4);
+  L.nC = a->mode == STA_DECODE_CHUNK ? (a->m + a->chunk_size - 1) / a->chunk_size : 0;
+  L.crank = take((size_t)BH * (L.nC > 0 ? L.nC : 1) * 4);
+  L.cflag = take((size_t)BH * (L.nC > 0 ? L.nC : 1));
   L.total = o;
   return L;
 }
@@ -572,9 +641,11 @@ int dec_check(const sta_decode_args* a) {
   if (a->n_heads <= 0 || a->n_kv_heads <= 0 || a->n_heads % a->n_kv_heads || a->batch <= 0)
     return fail(STA_ERR_ARG, "sta_decode: bad head counts");
   if (a->m <= 0) return fail(STA_ERR_ARG, "sta_decode: empty cache");
-  if (a->mode < STA_DECODE_PI || a->mode > STA_DECODE_STREAM)
+  if (a->mode < STA_DECODE_PI || a->mode > STA_DECODE_CHUNK)
     return fail(STA_ERR_ARG, "sta_decode: mode");
   if (a->mode != STA_DECODE_STREAM && a->k_max <= 0) return fail(STA_ERR_ARG, "sta_decode: k_max");
+  if (a->mode == STA_DECODE_CHUNK && (a->chunk_size <= 0 || a->n_chunk < 0))
+    return fail(STA_ERR_ARG, "sta_decode: chunk_size / n_chunk");
   if (a->mode == STA_DECODE_STREAM && a->block_n <= 0) return fail(STA_ERR_ARG, "sta_decode: block_n");
   if (a->n_kv_heads > 65535 || a->m > ((int64_t)1 << 31) - 1)
     return fail(STA_ERR_UNSUPPORTED, "sta_decode: too many kv heads / keys");
@@ -646,6 +717,13 @@ int decode_forward(const sta_decode_args* a, void* ws, size_t ws_len, cudaStream
   p.kept = a->kept_out ? a->kept_out : reinterpret_cast<int32_t*>(w + L.kept);
   p.usize = a->usize_out ? a->usize_out : reinterpret_cast<int32_t*>(w + L.usize);
   p.dblk = L.nblk > 0 ? reinterpret_cast<float*>(w + L.dblk) : nullptr;
+  p.C = a->chunk_size > 0 ? a->chunk_size : 16;
+  p.n_chunk = a->n_chunk;
+  p.mean_agg = a->chunk_agg == 1;
+  p.weighted = a->select_score != STA_SCORE_FREQ;
+  p.nC = L.nC;
+  p.crank = L.nC > 0 ? reinterpret_cast<float*>(w + L.crank) : nullptr;
+  p.cflag = L.nC > 0 ? w + L.cflag : nullptr;
   const bool f32 = a->dtype == STA_DTYPE_F32;
   if (a->d == 128) return f32 ? dec_launch<128, float>(p, st) : dec_launch<128, __nv_bfloat16>(p, st);
   return f32 ? dec_launch<64, float>(p, st) : dec_launch<64, __nv_bfloat16>(p, st);

@@ -121,10 +121,11 @@ class DecodeArgs(ctypes.Structure):
                 ("rope_table_a", c_vp), ("rope_table_a_R", c_f32), ("rope_table_a_len", c_i64),
                 ("rope_table_c", c_vp), ("rope_table_c_R", c_f32), ("rope_table_c_len", c_i64),
                 ("idx_out", c_vp), ("newpos_k_out", c_vp), ("newpos_q_out", c_vp),
-                ("kept_out", c_vp), ("usize_out", c_vp)]
+                ("kept_out", c_vp), ("usize_out", c_vp), ("chunk_size", c_i32),
+                ("n_chunk", c_i32), ("chunk_agg", c_i32), ("select_score", c_i32)]
 
 
-DECODE = {"pi": 0, "rank": 1, "stream": 2}
+DECODE = {"pi": 0, "rank": 1, "stream": 2, "chunk": 3}
 
 
 # every symbol include/sta.h declares (checked by the CPU test suite)

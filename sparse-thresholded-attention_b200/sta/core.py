@@ -305,13 +305,15 @@ def _table_R(pos_scale):
 
 
 def decode(mode: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, n_global=32, n_local=32,
-           k_max=1024, pct_decode=100.0, block_n=32, sm_scale=None, keep_sets=False):
+           k_max=1024, pct_decode=100.0, block_n=32, sm_scale=None, keep_sets=False,
+           chunk_size=16, n_chunk=0, chunk_agg="sum", select_score="expmass"):
     """One decode step: the query at position m-1 of every head against the cache.
 
     mode: 'pi' (shared hooks: threshold + optional top-pct + forced + tie-inclusive k_max cap by
     score + PI reposition, shared_selection_triton_exact.py:464-560), 'rank' (PQ-Union:
-    exact-budget cap, dense ranks, perquery.py:652-740) or 'stream' (PQ-Stream: no cap, streamed
-    positions, pqstream_kernel.py:694-795).  q (Z,H,D); k, v (Z,Hkv,m,D) raw cache (GQA-native).
+    exact-budget cap, dense ranks, perquery.py:652-740), 'stream' (PQ-Stream: no cap, streamed
+    positions, pqstream_kernel.py:694-795) or 'chunk' (chunk_exact: forced + top n_chunk chunks,
+    dense ranks, shared_selection_triton_chunked.py:412-483).  q (Z,H,D); k, v (Z,Hkv,m,D) raw cache (GQA-native).
     ga: selection geometry; gc: attend geometry (pos_scale_c repositions in 'pi').
     Returns (out (Z,H,D), stats {kept, usize} (Z,H) [+ sets idx / newpos_k / newpos_q])."""
     if not (q.is_cuda and k.is_cuda and v.is_cuda):
@@ -365,7 +367,10 @@ def decode(mode: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, n_global=32, 
     if Ra:
         ta, la = _rope_table(ia, float(ga.rope_scale), Ra, int(M * Ra) + 1)
         a.rope_table_a, a.rope_table_a_R, a.rope_table_a_len = ta.data_ptr(), Ra, la
-    Rc = {"pi": _table_R(gc.pos_scale), "rank": 1.0, "stream": -1.0}[mode]
+    a.chunk_size, a.n_chunk = int(chunk_size), int(n_chunk)
+    a.chunk_agg = {"sum": 0, "mean": 1}[chunk_agg]
+    a.select_score = L.SCORE[select_score]
+    Rc = {"pi": _table_R(gc.pos_scale), "rank": 1.0, "stream": -1.0, "chunk": 1.0}[mode]
     if Rc:
         tc, lc = _rope_table(ic, rs_c, Rc, int(M * abs(Rc)) + 1)
         a.rope_table_c, a.rope_table_c_R, a.rope_table_c_len = tc.data_ptr(), Rc, lc

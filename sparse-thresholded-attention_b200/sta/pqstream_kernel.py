@@ -87,3 +87,13 @@ def pqstream_attention(q, k, v, tau, inv_freq_a, inv_freq_c, pos_scale_a=1.0, ro
         span, kept, blocks, skipped = span[0], kept[0], blocks[0], skipped[0]
     _stats_accumulate(span, kept, blocks, skipped)
     return out, span, kept, blocks, skipped
+
+
+def install_pqstream_forward(*args, **kwargs):
+    """The PQ-Stream HuggingFace hook (pqstream_kernel.py:834); see
+    ``sta.hooks.install_pqstream_forward``."""
+    from .hooks import install_pqstream_forward as f
+    return f(*args, **kwargs)
+
+
+install_shared_pi_forward = install_pqstream_forward   # the reference's alias (:998)

@@ -84,3 +84,10 @@ def shared_chunk_attention(q, k, v, tau, inv_freq_a, inv_freq_c, pos_scale_a=1.0
         s = kept.double().sum()
         d["slots"] = s if d["slots"] is None else d["slots"] + s
     return out, usize, kept
+
+
+def install_shared_pi_forward(*args, **kwargs):
+    """The chunk_exact HuggingFace hook (shared_selection_triton_chunked.py:488); see
+    ``sta.hooks.install_chunk_forward``."""
+    from .hooks import install_chunk_forward
+    return install_chunk_forward(*args, **kwargs)

@@ -68,3 +68,10 @@ def shared_pq_attention(q, k, v, tau, inv_freq_a, inv_freq_c, pos_scale_a=1.0, r
         usize, kept, ovf = usize[0], kept[0], ovf[0]
     _ovf_accumulate(ovf, usize)
     return out, usize, kept, ovf
+
+
+def install_shared_pi_forward(*args, **kwargs):
+    """The PQ-Union HuggingFace hook (shared_selection_triton_perquery.py:784); see
+    ``sta.hooks.install_pq_forward``."""
+    from .hooks import install_pq_forward
+    return install_pq_forward(*args, **kwargs)

@@ -248,7 +248,8 @@ def gen_dca_tables(case, chunk_size, local_window, pretrain, seq_len, dim=64):
 
 
 def gen_decode(case, mode, H, M, D, seed, k_max=64, pct_decode=100.0, block_n=32, pos_scale=1.0,
-               rope_scale=1.0, geom="pi", tau_val=5.0):
+               rope_scale=1.0, geom="pi", tau_val=5.0, chunk_size=16, n_chunk=4,
+               select_score="expmass", chunk_agg="sum"):
     """One decode step of the reference's torch decode paths: the query at position M-1 against
     the cache 0..M-1 (selection sets + attention output)."""
     q, k, v = inputs(H, M, D, seed, torch.float32, planted=8)
@@ -271,6 +272,16 @@ def gen_decode(case, mode, H, M, D, seed, k_max=64, pct_decode=100.0, block_n=32
                                                   sm, ng, nl, k_max)
         invf_c, rs_c = rope_inv_freq(D, 1e4), 1.0
         out = ref._decode_attend_torch_pq(qd, K, V, idx, npk, npq, invf_c, sm)
+    elif mode == "chunk":
+        install_chunk_shim()
+        ref = __import__("shared_selection_triton_chunked")
+        pq = __import__("shared_selection_triton_perquery")
+        idx, npk, npq = ref._decode_build_sets_chunk(qd, K, tau, invf, qpos, pos_scale,
+                                                     rope_scale, sm, ng, nl, k_max, chunk_size,
+                                                     n_chunk, select_score=select_score,
+                                                     chunk_agg=chunk_agg)
+        invf_c, rs_c = rope_inv_freq(D, 1e4), 1.0
+        out = pq._decode_attend_torch_pq(qd, K, V, idx, npk, npq, invf_c, sm)
     else:
         ref = __import__("pqstream_kernel")
         idx, npk, npq = ref._decode_build_sets_pqs(qd, K, tau, invf, qpos, pos_scale, rope_scale,
@@ -280,7 +291,8 @@ def gen_decode(case, mode, H, M, D, seed, k_max=64, pct_decode=100.0, block_n=32
     meta = dict(kind="decode", mode=mode, H=H, M=M, D=D, seed=seed, k_max=k_max,
                 pct_decode=pct_decode, block_n=block_n, pos_scale=pos_scale,
                 rope_scale=float(rope_scale), rope_scale_c=float(rs_c), n_global=ng, n_local=nl,
-                tau=float(tau_val))
+                tau=float(tau_val), chunk_size=chunk_size, n_chunk=n_chunk,
+                select_score=select_score, chunk_agg=chunk_agg)
     save(case, meta, dict(q=qd, k=K, v=V, tau=tau, inv_freq_a=invf, inv_freq_c=invf_c, idx=idx,
                           newpos_k=npk, newpos_q=npq, out=out))
 
@@ -336,6 +348,12 @@ def main():
     gen_decode("decode_rank_cap_f32", "rank", 3, 700, 64, 54, k_max=80, pos_scale=0.5,
                tau_val=12.0)
     gen_decode("decode_stream_bn32_f32", "stream", 2, 777, 64, 55, tau_val=9.0)
+    gen_decode("decode_chunk_expmass_f32", "chunk", 3, 650, 64, 57, k_max=256, tau_val=12.0,
+               n_chunk=6)
+    # (freq ranking ties whole groups of chunks; torch.topk orders ties arbitrarily, so the
+    # pinned cases rank by exp(s - m))
+    gen_decode("decode_chunk_mean_c32_f32", "chunk", 2, 500, 64, 58, k_max=256, tau_val=20.0,
+               n_chunk=1, chunk_size=32, chunk_agg="mean")
     gen_decode("decode_stream_bn64_f32", "stream", 2, 600, 128, 56, block_n=64, geom="yarn",
                tau_val=9.0)
 

@@ -77,3 +77,39 @@ def test_hook_threshold_selects_and_runs():
         assert int(sa.spi_last_kept[:, -1].max()) < 512
     finally:
         ml.LlamaAttention.forward = orig_forward
+
+
+@pytest.mark.parametrize("modname,installer,kw", [
+    ("shared_selection_perquery", "install_shared_pi_forward", dict(k_max=512)),
+    ("shared_selection_chunked", "install_shared_pi_forward", dict(k_max=512, chunk_size=16)),
+    ("pqstream_kernel", "install_pqstream_forward", dict()),
+])
+def test_per_query_hooks_prefill_and_decode_match_dense_at_tau_inf(modname, installer, kw):
+    """tau = +inf keeps every causal key; with positions that reproduce the native ones (dense
+    ranks over all keys = the positions themselves; PQ-Stream 'full' with every key kept gives
+    relative positions, which RoPE does not distinguish) the hooks equal dense attention."""
+    import importlib
+    import transformers.models.llama.modeling_llama as ml
+    mod = importlib.import_module("sta." + modname)
+    orig_forward = ml.LlamaAttention.forward
+    model = tiny_llama(seed=5)
+    ids = torch.randint(0, 211, (1, 160), generator=torch.Generator().manual_seed(4)).cuda()
+    with torch.no_grad():
+        ref_logits = model(ids).logits
+        ref_gen = model.generate(ids, max_new_tokens=3, do_sample=False)
+    try:
+        set_tau(model, math.inf)
+        if modname == "pqstream_kernel":
+            kw = dict(kw, pos_advance="full")
+        if modname == "shared_selection_chunked":
+            kw = dict(kw, n_chunk=4096 // 16)
+        getattr(mod, installer)(model, context_window=4096, **kw)
+        with torch.no_grad():
+            logits = model(ids).logits
+            gen = model.generate(ids, max_new_tokens=3, do_sample=False)
+        assert torch.isfinite(logits).all()
+        err = (logits - ref_logits).abs().max().item()
+        assert err <= 1e-3, err
+        assert torch.equal(gen, ref_gen)
+    finally:
+        ml.LlamaAttention.forward = orig_forward

@@ -338,7 +338,7 @@ def test_errors_are_loud():
 # ---------------------------------------------------------------------------------------------
 # chunk_exact
 # ---------------------------------------------------------------------------------------------
-@pytest.mark.parametrize("name", names("chunk"))
+@pytest.mark.parametrize("name", [n for n in names("chunk") if n.startswith("chunk_")])
 def test_build_sets_chunk_on_reference_votes(name):
     from test_oracle import chunk_tiles_without_ties
     meta, a = load(name)
@@ -363,7 +363,7 @@ def test_build_sets_chunk_on_reference_votes(name):
     np.testing.assert_array_equal(o["kept_size"].cpu().numpy(), ref[5])
 
 
-@pytest.mark.parametrize("name", names("chunk"))
+@pytest.mark.parametrize("name", [n for n in names("chunk") if n.startswith("chunk_")])
 def test_chunk_end_to_end_vs_reference(name):
     from sta import shared_selection_chunked as ch
     meta, a = load(name)
@@ -566,7 +566,11 @@ def test_decode_vs_reference(name):
     out, st, sets = core.decode(mode, q, k, v, torch.from_numpy(a["tau"]), ga, gc,
                                 n_global=meta["n_global"], n_local=meta["n_local"],
                                 k_max=meta["k_max"], pct_decode=meta["pct_decode"],
-                                block_n=meta["block_n"], keep_sets=True)
+                                block_n=meta["block_n"], keep_sets=True,
+                                chunk_size=meta.get("chunk_size", 16),
+                                n_chunk=meta.get("n_chunk", 0),
+                                chunk_agg=meta.get("chunk_agg", "sum"),
+                                select_score=meta.get("select_score", "expmass"))
     cap = min(sets["idx"].shape[-1], a["idx"].shape[1])
     np.testing.assert_array_equal(sets["idx"][0, :, :cap].cpu().numpy(), a["idx"][:, :cap])
     np.testing.assert_array_equal(sets["newpos_k"][0, :, :cap].cpu().numpy(),
@@ -575,7 +579,7 @@ def test_decode_vs_reference(name):
     assert np.abs(out[0].cpu().numpy() - a["out"]).max() <= F32_TOL
 
 
-@pytest.mark.parametrize("mode", ["pi", "rank", "stream"])
+@pytest.mark.parametrize("mode", ["pi", "rank", "stream", "chunk"])
 def test_decode_bf16_gqa_vs_oracle(mode):
     H, Hk, M, D = 8, 2, 3001, 128
     q, k, v = make_inputs(SynthSpec(n_heads=H, n_kv_heads=Hk, seq_len=M, head_dim=D, seed=95,
@@ -584,7 +588,7 @@ def test_decode_bf16_gqa_vs_oracle(mode):
     invf, rs = yarn_inv_freq(D, 5e5, 4.0, 1024)
     ga = Geometry(invf, 1.0, rs)
     gc = Geometry(invf, 1.0, rs) if mode == "pi" else Geometry(rope_inv_freq(D, 5e5))
-    kw = dict(n_global=32, n_local=32, k_max=160, block_n=32)
+    kw = dict(n_global=32, n_local=32, k_max=160, block_n=32, chunk_size=16, n_chunk=4)
     out, st, sets = core.decode(mode, cu(q[:, :, M - 1]), cu(k), cu(v), tau, ga, gc,
                                 keep_sets=True, **kw)
     G = H // Hk
@@ -597,6 +601,9 @@ def test_decode_bf16_gqa_vs_oracle(mode):
     elif mode == "rank":
         o = oracle.decode_rank(qx, kx, vx, tau.numpy(), invf.numpy(), gc.inv_freq.numpy(), 1.0,
                                rs, sm, 32, 32, 160)
+    elif mode == "chunk":
+        o = oracle.decode_chunk(qx, kx, vx, tau.numpy(), invf.numpy(), gc.inv_freq.numpy(), 1.0,
+                                rs, sm, 32, 32, 160, 16, 4)
     else:
         o = oracle.decode_stream(qx, kx, vx, tau.numpy(), invf.numpy(), gc.inv_freq.numpy(),
                                  1.0, rs, sm, 32, 32, 32)

@@ -152,8 +152,8 @@ def test_dca_position_rule():
     assert oracle.dca_mscale(4096, 4096) == 1.0
 
 
-@pytest.mark.parametrize("path", [p for p in FIXTURES if "chunk" in p],
-                         ids=ids([p for p in FIXTURES if "chunk" in p]))
+@pytest.mark.parametrize("path", [p for p in FIXTURES if os.path.basename(p).startswith("chunk_")],
+                         ids=ids([p for p in FIXTURES if os.path.basename(p).startswith("chunk_")]))
 def test_chunk(path):
     meta, a = load(path)
     ws = a.get("wvotes") if meta["select_score"] != "freq" else None
@@ -253,6 +253,12 @@ def run_decode_oracle(meta, a):
         return oracle.decode_rank(a["q"], a["k"], a["v"], a["tau"], a["inv_freq_a"],
                                   a["inv_freq_c"], meta["pos_scale"], meta["rope_scale"], sm,
                                   meta["n_global"], meta["n_local"], meta["k_max"])
+    if meta["mode"] == "chunk":
+        return oracle.decode_chunk(a["q"], a["k"], a["v"], a["tau"], a["inv_freq_a"],
+                                   a["inv_freq_c"], meta["pos_scale"], meta["rope_scale"], sm,
+                                   meta["n_global"], meta["n_local"], meta["k_max"],
+                                   meta["chunk_size"], meta["n_chunk"], meta["select_score"],
+                                   meta["chunk_agg"])
     return oracle.decode_stream(a["q"], a["k"], a["v"], a["tau"], a["inv_freq_a"],
                                 a["inv_freq_c"], meta["pos_scale"], meta["rope_scale"], sm,
                                 meta["n_global"], meta["n_local"], meta["block_n"])
