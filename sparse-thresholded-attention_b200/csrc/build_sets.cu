@@ -344,14 +344,31 @@ __global__ void __launch_bounds__(kBT) build_sets_kernel(const BuildP p) {
   float* npq_row = p.newpos_q + nt_row * T;
   int64_t carry = 0;
   float cm_carry = -INFINITY;
+  // pos_scale 1: j - rank0 never decreases along the kept keys (each gap adds >= 0), so the
+  // running max at a kept key is its own j - rank0 and its position is exactly j -- no max scan.
+  // (Positions of keys that are not kept are only read for the tile's queries, which the local
+  // window keeps whenever n_local >= 1.)
+  const bool identity = p.pos_scale == 1.f && p.n_local >= 1;
   for (int64_t c0 = 0; c0 < E; c0 += kChunk) {
     const int64_t j0 = c0 + (int64_t)tid * kItems;
+    // the thread's kItems consecutive votes, one 8-byte load where aligned and in range
+    uint32_t vb[kItems];
+    if (j0 + kItems <= r.hi && ((reinterpret_cast<uintptr_t>(r.v + j0) & 7u) == 0)) {
+      const uint2 u = *reinterpret_cast<const uint2*>(r.v + j0);
+#pragma unroll
+      for (int i = 0; i < kItems; ++i) vb[i] = ((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 255u;
+    } else {
+#pragma unroll
+      for (int i = 0; i < kItems; ++i) vb[i] = j0 + i < r.hi ? r.v[j0 + i] : 0u;
+    }
     uint32_t flags = 0;
 #pragma unroll
     for (int i = 0; i < kItems; ++i) {
       const int64_t j = j0 + i;
       if (j < E) {
-        const bool kept = (has_shared && rank_value(r, j, weighted) >= cut) || F.has(j);
+        const float rv = !weighted ? (float)vb[i]
+                                   : (j < r.hi ? __fadd_rn(r.w[j], __fmul_rn(1e-6f, (float)vb[i])) : 0.f);
+        const bool kept = (has_shared && rv >= cut) || F.has(j);
         flags |= (kept ? 1u : 0u) << i;
       }
     }
@@ -368,15 +385,17 @@ __global__ void __launch_bounds__(kBT) build_sets_kernel(const BuildP p) {
       cr[i] = f ? __fsub_rn(__fmul_rn((float)j, p.pos_scale), rank0f[i]) : -INFINITY;
       tmax = fmaxf(tmax, cr[i]);
     }
-    float bmax;
-    const float excl = block_excl_max(tmax, sh_f, bmax);
-    float run = fmaxf(cm_carry, excl);
+    float run = cm_carry, bmax = -INFINITY;
+    if (!identity) {
+      const float excl = block_excl_max(tmax, sh_f, bmax);
+      run = fmaxf(cm_carry, excl);
+    }
 #pragma unroll
     for (int i = 0; i < kItems; ++i) {
       const int64_t j = j0 + i;
       if (j >= E) break;
       run = fmaxf(run, cr[i]);
-      const float np = __fadd_rn(rank0f[i], run);
+      const float np = identity ? (float)j : __fadd_rn(rank0f[i], run);
       const bool f = (flags >> i) & 1u;
       const int64_t rk = (int64_t)rank0f[i];
       if (f && rk < p.k_max) {
