@@ -467,10 +467,33 @@ __global__ void __launch_bounds__(kBT) build_sets_pq_kernel(const BuildPQP p) {
   __shared__ int sh_i[32];
 
   int nu = 0, nfu = 0;
-  for (int64_t j = tid; j < r.hi; j += kBT) {
-    if (r.v[j]) {
-      ++nu;
-      if (F.has(j)) ++nfu;
+  if ((reinterpret_cast<uintptr_t>(r.v) & 7u) == 0) {
+    // 8 votes per load; the union is sparse, so only nonzero words are looked at
+    const int64_t nw = r.hi / 8;
+    const uint2* vw = reinterpret_cast<const uint2*>(r.v);
+    for (int64_t w = tid; w < nw; w += kBT) {
+      const uint2 u = vw[w];
+      if ((u.x | u.y) == 0u) continue;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 255u) {
+          ++nu;
+          if (F.has(w * 8 + i)) ++nfu;
+        }
+      }
+    }
+    for (int64_t j = nw * 8 + tid; j < r.hi; j += kBT) {
+      if (r.v[j]) {
+        ++nu;
+        if (F.has(j)) ++nfu;
+      }
+    }
+  } else {
+    for (int64_t j = tid; j < r.hi; j += kBT) {
+      if (r.v[j]) {
+        ++nu;
+        if (F.has(j)) ++nfu;
+      }
     }
   }
   const int64_t usize = block_sum(nu, sh_i);
@@ -521,14 +544,20 @@ __global__ void __launch_bounds__(kBT) build_sets_pq_kernel(const BuildPQP p) {
         else if (rv == vb) tie |= 1u << i;
       }
     }
-    int tie_total;
-    const int tie_base = block_excl_sum(__popc(tie), sh_i, tie_total);
+    // chunks without any kept key (most of them: the union is sparse) only advance
+    const bool has_query = j0 < tstart + T && j0 + kItems > tstart;  // npq needs these ranks
+    if (!__syncthreads_or((sure | tie) != 0u || has_query)) continue;
+    if (overflow) {
+      int tie_total;
+      const int tie_base = block_excl_sum(__popc(tie), sh_i, tie_total);
 #pragma unroll
-    for (int i = 0; i < kItems; ++i) {
-      if ((tie >> i) & 1u) {
-        const int64_t tr = tie_carry + tie_base + __popc(tie & ((1u << i) - 1u));
-        if (tr < need_eq) sure |= 1u << i;
+      for (int i = 0; i < kItems; ++i) {
+        if ((tie >> i) & 1u) {
+          const int64_t tr = tie_carry + tie_base + __popc(tie & ((1u << i) - 1u));
+          if (tr < need_eq) sure |= 1u << i;
+        }
       }
+      tie_carry += tie_total;
     }
     flags = sure;
     int total;
@@ -548,7 +577,6 @@ __global__ void __launch_bounds__(kBT) build_sets_pq_kernel(const BuildPQP p) {
       if (j >= tstart && j < tstart + T) npq_row[j - tstart] = (float)rk;
     }
     carry += total;
-    tie_carry += tie_total;
   }
   __syncthreads();
   if (tstart + T > N) {
