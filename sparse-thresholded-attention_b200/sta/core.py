@@ -251,9 +251,10 @@ def forward_host(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, grou
     with torch.cuda.stream(s_in):
         for g in range(ng):
             hs, ks = slice(g * c * G, (g + 1) * c * G), slice(g * c, (g + 1) * c)
-            qd[:, hs].copy_(q[:, hs], non_blocking=True)
-            kd[:, ks].copy_(k[:, ks], non_blocking=True)
-            vd[:, ks].copy_(v[:, ks], non_blocking=True)
+            for b in range(Z):  # per batch element: contiguous slices, one DMA each
+                qd[b, hs].copy_(q[b, hs], non_blocking=True)
+                kd[b, ks].copy_(k[b, ks], non_blocking=True)
+                vd[b, ks].copy_(v[b, ks], non_blocking=True)
             e = torch.cuda.Event()
             e.record(s_in)
             ev_in.append(e)
@@ -268,7 +269,8 @@ def forward_host(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, grou
         done.record(comp)
         s_out.wait_event(done)
         with torch.cuda.stream(s_out):
-            out_h[:, hs].copy_(o, non_blocking=True)
+            for b in range(Z):
+                out_h[b, hs].copy_(o[b], non_blocking=True)
         o.record_stream(s_out)
     for x in (qd, kd, vd):
         x.record_stream(s_in)

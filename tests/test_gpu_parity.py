@@ -534,8 +534,8 @@ def test_forward_host_pipeline_equals_device_call(variant):
     """Host buffers in, host output back, transfers overlapped by kv-head group: the result is
     the device call's, bit for bit (every stage is independent per kv head)."""
     H, Hk, N, D = 8, 4, 640, 128
-    q, k, v = make_inputs(SynthSpec(n_heads=H, n_kv_heads=Hk, seq_len=N, head_dim=D, seed=90,
-                                    n_planted=16, dtype=torch.bfloat16))
+    q, k, v = make_inputs(SynthSpec(batch=2, n_heads=H, n_kv_heads=Hk, seq_len=N, head_dim=D,
+                                    seed=90, n_planted=16, dtype=torch.bfloat16))
     tau = torch.full((H,), 5.0)
     invf, rs = yarn_inv_freq(D, 5e5, 4.0, 256)
     ga = Geometry(invf, 1.0, rs)
