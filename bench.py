@@ -43,7 +43,10 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["sta", "reference"], default="sta")
+    ap.add_argument("--impl", choices=["sta", "reference", "reference_gpu"], default="sta",
+                    help="reference: the reference algorithm on the host cores (oracle port); "
+                         "reference_gpu: the reference's own Triton kernels on this GPU, from "
+                         "the unmodified install in baseline/_ref (configs 1 and 2)")
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--variant", choices=["shared", "pq_union", "pq_stream"], default="shared")
     ap.add_argument("--seq-len", type=int, default=None, help="override S (profiling only)")
@@ -149,6 +152,58 @@ def cpu_sample(q, k, v, tau, geo, c, n_tiles=12, head=0, seed=0, geo_c=None):
     desc = (f"oracle port (numpy) on {len(tiles)} of {nt} query tiles of 1 of {H} q heads, "
             f"{dt:.1f} s; extrapolated by causal key count to the whole layer ({est:.0f} s)")
     return tok_s, dt, desc
+
+
+def run_reference_gpu(args):
+    """--impl reference_gpu: the reference's own Triton prefill op (shared_pi_attention of
+    shared_selection_triton_exact_2.py / _YaRN_exact.py) on this GPU, same inputs and events
+    protocol.  The reference receives repeat_kv-expanded k / v as its hooks pass them
+    (exact_2.py:644-646).  Rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    line = {"impl": "reference_gpu", "metric": METRIC, "unit": "tokens/s"}
+    if not os.path.isdir(ref_dir) or args.config not in (1, 2) or args.variant != "shared":
+        line["unavailable"] = ("reference install missing (baseline/_ref)" if not os.path.isdir(ref_dir)
+                               else "measured for the shared path of configs 1 and 2 only")
+        emit(line)
+        return
+    import tempfile as _tf
+    os.environ.setdefault("TRITON_CACHE_DIR", _tf.mkdtemp(prefix="ref_triton_"))
+    sys.path.insert(0, ref_dir)
+    import torch
+    q, k, v, tau, geo, geo_c, c = workload(args)
+    mod = __import__("shared_selection_triton_YaRN_exact" if c["geom"] == "yarn"
+                     else "shared_selection_triton_exact_2")
+    dev = torch.device("cuda", 0)
+    G = c["H"] // c["Hkv"]
+    qd = q.to(dev)
+    kd = k.to(dev).repeat_interleave(G, 1)
+    vd = v.to(dev).repeat_interleave(G, 1)
+    taud = tau.to(dev)
+    invf = geo["inv_freq"].to(dev)
+
+    def step():
+        return mod.shared_pi_attention(qd, kd, vd, taud, invf, pos_scale=geo["pos_scale"],
+                                       pct=c["pct"], rope_scale=geo["rope_scale"], tile=c["T"],
+                                       k_max=c["k_max"])
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(args.steps):
+        step()
+    s1.record()
+    torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1) / args.steps
+    line.update({"value": c["B"] * c["S"] / (ms / 1e3), "ms_per_step": ms, "n_gpus": 1,
+                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                 "dtype": "bf16 inputs (reference Triton: fp32 RoPE, tl.dot)",
+                 "config": workload_desc(c, args, 1),
+                 "source": "unmodified reference modules installed by pip into baseline/_ref"})
+    emit(line)
 
 
 def run_reference(args):
@@ -440,7 +495,9 @@ def main():
         sys.stdout.flush()
         _JSON_FD = os.dup(1)
         os.dup2(2, 1)
-    if args.impl == "reference":
+    if args.impl == "reference_gpu":
+        run_reference_gpu(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)
