@@ -55,8 +55,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--partition", choices=["auto", "heads", "slabs", "grid"], default="auto",
                     help="multi-GPU unit: kv-head ranges, query slabs, or both (sta.partition)")
-    ap.add_argument("--e2e-groups", type=int, default=4,
-                    help="kv-head groups of the host-buffer pipeline (transfer / compute overlap)")
+    ap.add_argument("--e2e-groups", default="auto",
+                    help="kv-head groups of the host-buffer pipeline (transfer / compute overlap): "
+                         "a count, comma-separated kv-head counts, or auto (one kv head first and "
+                         "last, the rest in two groups)")
     ap.add_argument("--max-workspace-gb", type=int, default=48,
                     help="scratch cap; larger problems run over groups of kv heads")
     return ap.parse_args()
@@ -377,9 +379,18 @@ def run_gpu(args):
         ekw.pop("max_workspace_bytes")
         ekw["max_workspace_bytes"] = args.max_workspace_gb << 30
 
+        hk_rank = ks.shape[1]
+        if args.e2e_groups == "auto":
+            mid = hk_rank - 2   # one kv head first and last, the rest in two groups
+            groups = ([1] + [x for x in (mid - mid // 2, mid // 2) if x] + [1]) if hk_rank > 2 \
+                else hk_rank
+        elif "," in args.e2e_groups:
+            groups = [int(x) for x in args.e2e_groups.split(",")]
+        else:
+            groups = int(args.e2e_groups)
+
         def step_host():
-            return core.forward_host(args.variant, qh, kh, vh, taus, ga, gc,
-                                     groups=args.e2e_groups, **ekw)
+            return core.forward_host(args.variant, qh, kh, vh, taus, ga, gc, groups=groups, **ekw)
         for _ in range(2):
             out_h, _ = step_host()
         torch.cuda.synchronize()
@@ -400,8 +411,8 @@ def run_gpu(args):
             dist.all_reduce(nb)  # bytes copied by all ranks together
         e2e = {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": int(nb[0].item()), "d2h_bytes_per_step": int(nb[1].item()),
-               "api": f"sta.core.forward_host, pinned host buffers, {args.e2e_groups} kv-head "
-                      "groups overlapping H2D / compute / D2H"}
+               "api": f"sta.core.forward_host, pinned host buffers, kv-head groups {groups} "
+                      "overlapping H2D / compute / D2H"}
 
     # ---- roofline of the dominant kernel (Kernel A on tensor cores)
     pk, pk_kind = peaks()

@@ -218,7 +218,9 @@ def forward_host(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, grou
     """The op on HOST tensors, with the transfers overlapped with the compute.
 
     q (Z,H,N,D), k / v (Z,Hkv,N,D) in pinned host memory (a copy is made otherwise).  The kv
-    heads are cut into ``groups`` equal groups (the largest divisor of Hkv not above it): group
+    heads are cut into ``groups`` equal groups (the largest divisor of Hkv not above it), or into
+    groups of the listed kv-head counts (small first and last groups shorten the transfer that
+    nothing overlaps: the first group's input and the last group's output): group
     g+1 is copied host -> device on one stream while group g computes on the current stream,
     and each group's output is copied back on a third stream as soon as it is done.  Every
     stage is independent per kv head, so the result equals one device call on the whole input.
@@ -234,10 +236,19 @@ def forward_host(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, grou
     if H % Hk:
         raise ValueError("number of q heads must be a multiple of the number of kv heads")
     G = H // Hk
-    ng = max(1, min(int(groups), Hk))
-    while Hk % ng:
-        ng -= 1
-    c = Hk // ng
+    if isinstance(groups, (list, tuple)):
+        sizes = [int(x) for x in groups]
+        if sum(sizes) != Hk or min(sizes) < 1:
+            raise ValueError(f"group sizes {sizes} must be positive and sum to {Hk} kv heads")
+    else:
+        ng = max(1, min(int(groups), Hk))
+        while Hk % ng:
+            ng -= 1
+        sizes = [Hk // ng] * ng
+    bounds = [0]
+    for x in sizes:
+        bounds.append(bounds[-1] + x)
+    ng = len(sizes)
     qd = torch.empty(q.shape, dtype=q.dtype, device=dev)
     kd = torch.empty(k.shape, dtype=k.dtype, device=dev)
     vd = torch.empty(v.shape, dtype=v.dtype, device=dev)
@@ -250,7 +261,7 @@ def forward_host(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, grou
     ev_in = []
     with torch.cuda.stream(s_in):
         for g in range(ng):
-            hs, ks = slice(g * c * G, (g + 1) * c * G), slice(g * c, (g + 1) * c)
+            hs, ks = slice(bounds[g] * G, bounds[g + 1] * G), slice(bounds[g], bounds[g + 1])
             for b in range(Z):  # per batch element: contiguous slices, one DMA each
                 qd[b, hs].copy_(q[b, hs], non_blocking=True)
                 kd[b, ks].copy_(k[b, ks], non_blocking=True)
@@ -261,7 +272,7 @@ def forward_host(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, grou
     tau_h = torch.as_tensor(tau, dtype=torch.float32).reshape(-1)
     stats = []
     for g in range(ng):
-        hs, ks = slice(g * c * G, (g + 1) * c * G), slice(g * c, (g + 1) * c)
+        hs, ks = slice(bounds[g] * G, bounds[g + 1] * G), slice(bounds[g], bounds[g + 1])
         comp.wait_event(ev_in[g])
         o, st, _ = forward(variant, qd[:, hs], kd[:, ks], vd[:, ks], tau_h[hs], ga, gc, **kw)
         stats.append(st)
