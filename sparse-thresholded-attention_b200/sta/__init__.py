@@ -9,6 +9,10 @@ Host-side mirror of the reference repository's prefill call surfaces, backed by 
     sta.shared_selection_hybrid_exact   <- shared_selection_triton_hybrid_exact
     sta.shared_selection_perquery       <- shared_selection_triton_perquery (PQ-Union)
     sta.pqstream_kernel                 <- pqstream_kernel (PQ-Stream)
+    sta.shared_selection_chunked        <- shared_selection_triton_chunked (chunk_exact)
+    sta.hooks                           the HuggingFace attention hooks of every family
+    sta.core                            forward / forward_host / decode and the stage calls
+    sta.partition                       multi-GPU units (kv-head ranges, query slabs)
 """
 from . import core  # noqa: F401
 from ._lib import lib  # noqa: F401

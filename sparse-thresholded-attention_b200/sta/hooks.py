@@ -12,8 +12,6 @@ per query position, GQA-native.
 """
 from __future__ import annotations
 
-import math
-
 import torch
 
 
