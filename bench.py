@@ -379,11 +379,11 @@ def run_gpu(args):
         ekw.pop("max_workspace_bytes")
         ekw["max_workspace_bytes"] = args.max_workspace_gb << 30
 
-        hk_rank = ks.shape[1]
+        units = ks.shape[1] if ks.shape[1] > 1 else qs.shape[1]  # kv heads, or q heads
         if args.e2e_groups == "auto":
-            mid = hk_rank - 2   # one kv head first and last, the rest in two groups
-            groups = ([1] + [x for x in (mid - mid // 2, mid // 2) if x] + [1]) if hk_rank > 2 \
-                else hk_rank
+            mid = units - 2     # one unit first and last, the rest in two groups
+            groups = ([1] + [x for x in (mid - mid // 2, mid // 2) if x] + [1]) if units > 2 \
+                else units
         elif "," in args.e2e_groups:
             groups = [int(x) for x in args.e2e_groups.split(",")]
         else:

@@ -218,9 +218,9 @@ def forward_host(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, grou
     """The op on HOST tensors, with the transfers overlapped with the compute.
 
     q (Z,H,N,D), k / v (Z,Hkv,N,D) in pinned host memory (a copy is made otherwise).  The kv
-    heads are cut into ``groups`` equal groups (the largest divisor of Hkv not above it), or into
-    groups of the listed kv-head counts (small first and last groups shorten the transfer that
-    nothing overlaps: the first group's input and the last group's output): group
+    heads (the q heads when Hkv is 1) are cut into ``groups`` equal groups (the largest divisor
+    not above it), or into groups of the listed counts (small first and last groups shorten the
+    transfer that nothing overlaps: the first group's input and the last group's output): group
     g+1 is copied host -> device on one stream while group g computes on the current stream,
     and each group's output is copied back on a third stream as soon as it is done.  Every
     stage is independent per kv head, so the result equals one device call on the whole input.
@@ -236,19 +236,27 @@ def forward_host(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, grou
     if H % Hk:
         raise ValueError("number of q heads must be a multiple of the number of kv heads")
     G = H // Hk
+    # group units: kv heads, or q heads when there is a single kv head (its k / v go first)
+    units = Hk if Hk > 1 else H
     if isinstance(groups, (list, tuple)):
         sizes = [int(x) for x in groups]
-        if sum(sizes) != Hk or min(sizes) < 1:
-            raise ValueError(f"group sizes {sizes} must be positive and sum to {Hk} kv heads")
+        if sum(sizes) != units or min(sizes) < 1:
+            raise ValueError(f"group sizes {sizes} must be positive and sum to {units}")
     else:
-        ng = max(1, min(int(groups), Hk))
-        while Hk % ng:
+        ng = max(1, min(int(groups), units))
+        while units % ng:
             ng -= 1
-        sizes = [Hk // ng] * ng
+        sizes = [units // ng] * ng
     bounds = [0]
     for x in sizes:
         bounds.append(bounds[-1] + x)
     ng = len(sizes)
+    if Hk > 1:
+        qsl = [slice(bounds[g] * G, bounds[g + 1] * G) for g in range(ng)]
+        ksl = [slice(bounds[g], bounds[g + 1]) for g in range(ng)]
+    else:
+        qsl = [slice(bounds[g], bounds[g + 1]) for g in range(ng)]
+        ksl = [slice(0, 1)] * ng
     qd = torch.empty(q.shape, dtype=q.dtype, device=dev)
     kd = torch.empty(k.shape, dtype=k.dtype, device=dev)
     vd = torch.empty(v.shape, dtype=v.dtype, device=dev)
@@ -261,18 +269,19 @@ def forward_host(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, grou
     ev_in = []
     with torch.cuda.stream(s_in):
         for g in range(ng):
-            hs, ks = slice(bounds[g] * G, bounds[g + 1] * G), slice(bounds[g], bounds[g + 1])
+            hs, ks = qsl[g], ksl[g]
             for b in range(Z):  # per batch element: contiguous slices, one DMA each
+                if Hk > 1 or g == 0:
+                    kd[b, ks].copy_(k[b, ks], non_blocking=True)
+                    vd[b, ks].copy_(v[b, ks], non_blocking=True)
                 qd[b, hs].copy_(q[b, hs], non_blocking=True)
-                kd[b, ks].copy_(k[b, ks], non_blocking=True)
-                vd[b, ks].copy_(v[b, ks], non_blocking=True)
             e = torch.cuda.Event()
             e.record(s_in)
             ev_in.append(e)
     tau_h = torch.as_tensor(tau, dtype=torch.float32).reshape(-1)
     stats = []
     for g in range(ng):
-        hs, ks = slice(bounds[g] * G, bounds[g + 1] * G), slice(bounds[g], bounds[g + 1])
+        hs, ks = qsl[g], ksl[g]
         comp.wait_event(ev_in[g])
         o, st, _ = forward(variant, qd[:, hs], kd[:, ks], vd[:, ks], tau_h[hs], ga, gc, **kw)
         stats.append(st)

@@ -547,6 +547,13 @@ def test_forward_host_pipeline_equals_device_call(variant):
     torch.cuda.synchronize()
     assert not out_h.is_cuda
     assert torch.equal(out_h, ref.cpu())
+    # a single kv head: the groups run over its q heads
+    k1, v1 = k[:, :1].contiguous(), v[:, :1].contiguous()
+    q1 = q[:, :2].contiguous()
+    ref1, _, _ = core.forward(variant, cu(q1), cu(k1), cu(v1), tau[:2], ga, gc, **kw)
+    out1, _ = core.forward_host(variant, q1, k1, v1, tau[:2], ga, gc, groups=[1, 1], **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(out1, ref1.cpu())
     for name, x in st_ref.items():
         if torch.is_tensor(x):
             assert torch.equal(st[name], x), name
