@@ -48,6 +48,7 @@ extern "C" {
  * Library
  * ------------------------------------------------------------------------------------- */
 const char* sta_last_error(void);
+/* ABI version: 2 (query slabs, PQ-Stream pass 2 on Kernel A keep bits, decode) */
 int sta_version(void);
 /* Number of elements of one head of a compact selection array. */
 int64_t sta_tri_head_stride(int64_t n, int32_t tile);

@@ -456,7 +456,7 @@ extern "C" {
 
 const char* sta_last_error(void) { return g_last_error; }
 
-int sta_version(void) { return 1; }
+int sta_version(void) { return 2; }
 
 int64_t sta_tri_head_stride(int64_t n, int32_t tile) { return tri_head_stride(n, tile); }
 

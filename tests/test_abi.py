@@ -35,7 +35,8 @@ def test_struct_layouts_match_header_order():
     for cname, cls in (("sta_select_args", L.SelectArgs), ("sta_build_args", L.BuildArgs),
                        ("sta_build_pq_args", L.BuildPQArgs), ("sta_attend_args", L.AttendArgs),
                        ("sta_pqstream_args", L.PQStreamArgs), ("sta_forward_args", L.ForwardArgs),
-                       ("sta_build_chunk_args", L.BuildChunkArgs)):
+                       ("sta_build_chunk_args", L.BuildChunkArgs),
+                       ("sta_decode_args", L.DecodeArgs)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), src, re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
         fields = re.findall(r"\**\s*([A-Za-z_0-9]+)\s*;", body)
@@ -129,3 +130,7 @@ def test_synth_is_deterministic():
     for x, y in zip(a, b):
         assert torch.equal(x, y)
     assert a[0].shape == (1, 2, 128, 64) and a[1].shape == (1, 1, 128, 64)
+
+
+def test_abi_version():
+    assert L.lib().sta_version() == 2
