@@ -620,3 +620,32 @@ def test_decode_bf16_gqa_vs_oracle(mode):
     err = np.abs(out[0].float().cpu().numpy() - o[0])[same]
     assert err.max() <= BF16_MAX and err.mean() <= BF16_MEAN, (err.max(), err.mean())
     assert int(st["kept"].min()) >= 64        # the forced keys at least
+
+
+TINY = [1, 5, 33, 64, 65, 130, 257]
+
+
+@pytest.mark.parametrize("N", TINY)
+def test_tiny_sequences_vs_oracle(N):
+    """Sequences shorter than one selection block / tile, and just past the boundaries (the
+    reference supports ragged N down to a single token)."""
+    H, D = 2, 64
+    q, k, v = make_inputs(SynthSpec(n_heads=H, n_kv_heads=H, seq_len=N, head_dim=D, seed=100 + N,
+                                    n_planted=min(4, max(N - 1, 0)), n_planted_queries=4))
+    tau = torch.full((H,), 5.0)
+    invf = rope_inv_freq(D, 1e4)
+    res = ex2.shared_pi_attention(cu(q), cu(k), cu(v), tau, invf, 0.5, tile=64, k_max=64)
+    qx, kx, vx = (x[0].float().numpy() for x in (q, k, v))
+    o = oracle.shared_attention(qx, kx, vx, tau.numpy(), invf.numpy(), 0.5, 1.0, invf.numpy(),
+                                0.5, 1.0, tile=64, k_max=64)
+    assert np.abs(res[0][0].cpu().numpy() - o[0]).max() <= F32_TOL
+    np.testing.assert_array_equal(res[2].cpu().numpy(), o[2])
+    out, usize, kept, ovf = pq.shared_pq_attention(cu(q), cu(k), cu(v), tau, invf, invf, 0.5, 1.0,
+                                                   k_max=96)
+    o2 = oracle.pq_attention(qx, kx, vx, tau.numpy(), invf.numpy(), invf.numpy(), 0.5, 1.0,
+                             k_max=96)
+    assert np.abs(out[0].cpu().numpy() - o2[0]).max() <= F32_TOL
+    out3, span, kept3, _, _ = pqs.pqstream_attention(cu(q), cu(k), cu(v), tau, invf, invf, 0.5)
+    o3 = oracle.pqstream_attention(qx, kx, vx, tau.numpy(), invf.numpy(), invf.numpy(), 0.5)
+    assert np.abs(out3[0].cpu().numpy() - o3[0]).max() <= F32_TOL
+    np.testing.assert_array_equal(kept3.cpu().numpy().reshape(o3[2].shape), o3[2])
