@@ -649,3 +649,35 @@ def test_tiny_sequences_vs_oracle(N):
     o3 = oracle.pqstream_attention(qx, kx, vx, tau.numpy(), invf.numpy(), invf.numpy(), 0.5)
     assert np.abs(out3[0].cpu().numpy() - o3[0]).max() <= F32_TOL
     np.testing.assert_array_equal(kept3.cpu().numpy().reshape(o3[2].shape), o3[2])
+
+
+def test_full_length_properties_cfg2_shape():
+    """Config-2 geometry at its full sequence length (32k; 8 of the 32 q heads), checked through
+    size-independent properties: query slabs reproduce the whole call bit for bit, every query
+    keeps its own argmax at tau = 0, and the selection outputs are well formed (slots ascending
+    and in range, positions non-decreasing, the fallback honoured)."""
+    from sta.synth import make_config_inputs
+    q, k, v, c = make_config_inputs(2, n_heads=8)
+    H, N, D, T = 8, c["S"], c["D"], c["T"]
+    invf, rs = yarn_inv_freq(D, 5e5, 4.0, 8192)
+    g = Geometry(invf, 1.0, rs)
+    tau = torch.full((H,), 5.0)
+    qd, kd, vd = cu(q), cu(k), cu(v)
+    kw = dict(tile=T, k_max=2048, keep_sets=True)
+    out, st, sets = core.forward("shared", qd, kd, vd, tau, g, g, **kw)
+    s0 = 16384
+    o2, st2, _ = core.forward("shared", qd[:, :, s0:].contiguous(), kd, vd, tau, g, g,
+                              q_pos_base=s0, **kw)
+    assert torch.equal(o2, out[:, :, s0:])
+    assert torch.equal(st2["kept_size"], st["kept_size"][..., s0 // T:])
+    idx = sets["idx"][0]
+    valid = idx < N
+    assert bool(((idx[..., 1:] > idx[..., :-1]) | ~valid[..., 1:]).all())   # ascending
+    npk = sets["newpos_k"][0]
+    assert bool(((npk[..., 1:] >= npk[..., :-1]) | ~valid[..., 1:]).all())  # monotone positions
+    ks, ch = st["kept_size"][0], st["chosen"][0]
+    assert bool((ks[ch > 0] <= 2048).all())                                  # fitted picks fit
+    assert int(((ch > 0) & (ch < 30)).sum()) > 0                             # fallback exercised
+    sel = core.select(qd[0], kd[0], torch.zeros(H), g, tile=T)
+    assert int(sel["row_count"].min()) >= 1                                  # argmax kept
+    assert core.device_error() == 0
