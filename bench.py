@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--partition", choices=["auto", "heads", "slabs", "grid"], default="auto",
                     help="multi-GPU unit: kv-head ranges, query slabs, or both (sta.partition)")
+    ap.add_argument("--decode", action="store_true",
+                    help="time one decode step (the last position against the whole cache) "
+                         "instead of the prefill op; its own metric line")
     ap.add_argument("--e2e-groups", default="auto",
                     help="kv-head groups of the host-buffer pipeline (transfer / compute overlap): "
                          "a count, comma-separated kv-head counts, or auto (one kv head first and "
@@ -474,6 +477,44 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+def run_decode(args):
+    """--decode: one decode step of the variant's rule (shared -> PI cap + reposition, pq_union
+    -> dense ranks, pq_stream -> streamed positions) for the config's last position against the
+    whole cache, CUDA events, 1 GPU.  HBM traffic: the cache's K once (scores) + the kept rows."""
+    import torch
+    from sta import core
+    from sta.core import Geometry
+    q, k, v, tau, geo, geo_c, c = workload(args)
+    dev = torch.device("cuda", 0)
+    N = c["S"]
+    qd = q[:, :, N - 1].contiguous().to(dev)
+    kd, vd = k.to(dev), v.to(dev)
+    ga = Geometry(geo["inv_freq"], geo["pos_scale"], geo["rope_scale"])
+    gc = Geometry(geo_c["inv_freq"], geo_c["pos_scale"], geo_c["rope_scale"])
+    mode = {"shared": "pi", "pq_union": "rank", "pq_stream": "stream"}[args.variant]
+    kw = dict(k_max=c["k_max"], block_n=32)
+    for _ in range(max(args.warmup, 3)):
+        out, st, _ = core.decode(mode, qd, kd, vd, tau, ga, gc, **kw)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        out, st, _ = core.decode(mode, qd, kd, vd, tau, ga, gc, **kw)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    kv_bytes = kd.numel() * kd.element_size()
+    pk, pk_kind = peaks()
+    gbs = kv_bytes / (ms / 1e3) / 1e9
+    emit({"metric": "decode steps/s per attention layer", "value": 1e3 / ms, "unit": "steps/s",
+          "ms_per_step": ms, "n_gpus": 1, "steps": args.steps, "higher_is_better": True,
+          "config": dict(workload_desc(c, args, 1), context=N, mode=mode),
+          "mean_kept": float(st["kept"].float().mean()),
+          "roofline": {"bound": "hbm", "achieved": gbs, "peak": float(pk["hbm_gbs"]),
+                       "unit": "GB/s", "frac": gbs / float(pk["hbm_gbs"]),
+                       "note": f"K cache read once for the scores ({kv_bytes} bytes); {pk_kind} peak"}})
+
+
 def select_traffic_bytes(c, heads, pairs):
     """DRAM bytes per select launch from the committed ncu summary, scaled by causal work."""
     p = os.path.join(ROOT, "profiles", "select_kernel_traffic.json")
@@ -506,7 +547,9 @@ def main():
         sys.stdout.flush()
         _JSON_FD = os.dup(1)
         os.dup2(2, 1)
-    if args.impl == "reference_gpu":
+    if args.decode:
+        run_decode(args)
+    elif args.impl == "reference_gpu":
         run_reference_gpu(args)
     elif args.impl == "reference":
         run_reference(args)

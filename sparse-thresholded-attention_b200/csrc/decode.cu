@@ -34,7 +34,7 @@ constexpr int kScoreThreads = 256;  // 8 warps, one key per warp at a time
 constexpr int kKeysPerCta = 64;
 constexpr int kSelThreads = 1024;
 constexpr int kItems = 4;           // consecutive keys per thread per scan chunk
-constexpr int kAttThreads = 256;
+constexpr int kAttThreads = 1024;  // 32 warps stream the slots of one q head
 
 struct DecP {
   const void* q;

@@ -303,18 +303,22 @@ def forward_host(variant: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, grou
 _TABLES = {}
 
 
-def _rope_table(inv_freq: torch.Tensor, rope_scale: float, R: float, length: int):
-    """Cached (cos, sin) * rope_scale table at positions i / R, 0 <= i < length (sta_rope_table);
-    grown by doubling so that a decode loop builds it O(log n) times."""
-    key = (inv_freq.device, inv_freq.data_ptr(), inv_freq.numel(), float(rope_scale), float(R))
+def _rope_table(inv_freq: torch.Tensor, rope_scale: float, R: float, length: int, src=None):
+    """Cached (cos, sin) * rope_scale table at positions i / R, 0 <= i < length (sta_rope_table),
+    keyed by the frequencies' VALUES; grown by doubling so that a decode loop builds it
+    O(log n) times.  inv_freq: fp32 on the target device; src: the same values where they are
+    already on the host (saves a device-to-host read for the key)."""
+    vals = (src if src is not None and not src.is_cuda else inv_freq).detach().float().cpu()
+    key = (inv_freq.device, vals.numpy().tobytes(), float(rope_scale), float(R))
     t = _TABLES.get(key)
     if t is None or t[1] < length:
         cap = max(length, 2 * (t[1] if t else 0), 1024)
         half = inv_freq.numel()
         buf = torch.empty((cap, half, 2), dtype=torch.float32, device=inv_freq.device)
-        L.check(L.lib().sta_rope_table(_p(inv_freq), 2 * half, float(rope_scale), float(R), cap,
+        freq = inv_freq.detach().clone()
+        L.check(L.lib().sta_rope_table(_p(freq), 2 * half, float(rope_scale), float(R), cap,
                                        _p(buf), _stream()), "sta_rope_table")
-        t = (buf, cap, inv_freq)  # keep inv_freq alive: its address is part of the key
+        t = (buf, cap)
         _TABLES[key] = t
     return t[0], t[1]
 
@@ -387,14 +391,14 @@ def decode(mode: str, q, k, v, tau, ga: Geometry, gc: Geometry, *, n_global=32, 
     a.pct_decode, a.block_n = float(pct_decode), int(block_n)
     Ra = _table_R(ga.pos_scale)
     if Ra:
-        ta, la = _rope_table(ia, float(ga.rope_scale), Ra, int(M * Ra) + 1)
+        ta, la = _rope_table(ia, float(ga.rope_scale), Ra, int(M * Ra) + 1, src=ga.inv_freq)
         a.rope_table_a, a.rope_table_a_R, a.rope_table_a_len = ta.data_ptr(), Ra, la
     a.chunk_size, a.n_chunk = int(chunk_size), int(n_chunk)
     a.chunk_agg = {"sum": 0, "mean": 1}[chunk_agg]
     a.select_score = L.SCORE[select_score]
     Rc = {"pi": _table_R(gc.pos_scale), "rank": 1.0, "stream": -1.0, "chunk": 1.0}[mode]
     if Rc:
-        tc, lc = _rope_table(ic, rs_c, Rc, int(M * abs(Rc)) + 1)
+        tc, lc = _rope_table(ic, rs_c, Rc, int(M * abs(Rc)) + 1, src=gc.inv_freq)
         a.rope_table_c, a.rope_table_c_R, a.rope_table_c_len = tc.data_ptr(), Rc, lc
     a.kept_out, a.usize_out = st["kept"].data_ptr(), st["usize"].data_ptr()
     if sets:
