@@ -421,7 +421,7 @@ def run_gpu(args):
     pk, pk_kind = peaks()
     Hr = qs.shape[1]
     pairs = (s1 * (s1 + 1) - s0 * (s0 + 1)) / 2   # causal (query, key) pairs of this rank's slab
-    flops_sel = (2 if args.variant != "pq_stream" else 1) * 2 * D * Hr * B * pairs
+    flops_sel = 2 * 2 * D * Hr * B * pairs      # two passes for every variant
     sel_ms = stage_ms[1]
     achieved = flops_sel / (sel_ms / 1e3) / 1e12
     peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
