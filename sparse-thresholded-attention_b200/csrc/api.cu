@@ -92,9 +92,10 @@ inline size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
   int64_t c;          // kv heads per group
-  size_t qh, ql, kh, kl, votes, wvotes, bits, idx, npk, npq, mask, rowcnt, bmax, rtab, total;
-  float rtab_R;
-  int64_t rtab_len;
+  size_t qh, ql, kh, kl, votes, wvotes, bits, idx, npk, npq, mask, rowcnt, bmax, rtab, stab, total;
+  float rtab_R, stab_R;
+  int64_t rtab_len, stab_len;
+  bool stab_shared;  // the selection table is the attend table
 };
 
 int64_t esize(int dt) { return dt == STA_DTYPE_F32 ? 4 : 2; }
@@ -152,6 +153,28 @@ Layout layout_for(const sta_forward_args* a, Variant v, int64_t c) {
       }
   }
   if (L.rtab_len > 0) L.rtab = take((size_t)L.rtab_len * (D / 2) * 8);
+  // cos/sin table of the selection geometry for the RoPE prologue: positions j * pos_scale_a
+  // (DCA position ids are integers), shared with the attend table when they coincide
+  L.stab_R = 0.f;
+  L.stab_len = 0;
+  L.stab_shared = false;
+  if (a->dca_chunk_size > 0) {
+    L.stab_R = 1.f;
+  } else {
+    for (int r = 1; r <= 4; r *= 2)
+      if (a->pos_scale_a * (float)r == 1.f) L.stab_R = (float)r;
+  }
+  if (L.stab_R > 0.f) {
+    L.stab_len = N * (int64_t)L.stab_R + 1;
+    if (v == kShared && a->same_geometry && a->dca_chunk_size <= 0 && L.rtab_R == L.stab_R &&
+        a->rope_scale_a == a->rope_scale_c && L.rtab_len >= L.stab_len) {
+      L.stab_shared = true;
+      L.stab = L.rtab;
+      L.stab_len = L.rtab_len;
+    } else {
+      L.stab = take((size_t)L.stab_len * (D / 2) * 8);
+    }
+  }
   L.total = o;
   return L;
 }
@@ -232,6 +255,10 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
   if (L.rtab_len > 0)
     STA_TRY(launch_rope_table(a->inv_freq_c, a->d, v == kShared ? a->rope_scale_c : 1.0f,
                               L.rtab_R, L.rtab_len, w + L.rtab, st));
+  if (L.stab_len > 0 && !L.stab_shared)
+    STA_TRY(launch_rope_table(a->inv_freq_a, a->d, a->rope_scale_a, L.stab_R, L.stab_len,
+                              w + L.stab, st));
+  const void* stab = L.stab_len > 0 ? w + L.stab : nullptr;
   for (int64_t b = 0; b < a->batch; ++b) {
     for (int64_t g0 = 0; g0 < Hk; g0 += c) {
       const int64_t h0 = b * H + g0 * G;   // first q head (flattened over batch)
@@ -251,20 +278,21 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       if (!dca) {
         STA_TRY(launch_rope_split(q, a->dtype, qn, Nq, a->d, a->q_stride_h, a->q_stride_n,
                                   a->inv_freq_a, a->pos_scale_a, a->rope_scale_a, w + L.qh,
-                                  w + L.ql, st, 0, 0, 0, qbase));
+                                  w + L.ql, st, 0, 0, 0, qbase, stab, L.stab_R, L.stab_len));
         STA_TRY(launch_rope_split(k, a->dtype, c, N, a->d, a->k_stride_h, a->k_stride_n,
                                   a->inv_freq_a, a->pos_scale_a, a->rope_scale_a, w + L.kh,
-                                  w + L.kl, st));
+                                  w + L.kl, st, 0, 0, 0, 0, stab, L.stab_R, L.stab_len));
       } else {
         const size_t plane = (size_t)qn * Nq * a->d * 2;
         for (int role = 1; role <= 3; ++role)
           STA_TRY(launch_rope_split(q, a->dtype, qn, Nq, a->d, a->q_stride_h, a->q_stride_n,
                                     a->inv_freq_a, 1.0f, a->rope_scale_a,
                                     w + L.qh + (role - 1) * plane, w + L.ql + (role - 1) * plane,
-                                    st, role, dL, a->dca_chunk_size, qbase));
+                                    st, role, dL, a->dca_chunk_size, qbase, stab, L.stab_R,
+                                    L.stab_len));
         STA_TRY(launch_rope_split(k, a->dtype, c, N, a->d, a->k_stride_h, a->k_stride_n,
                                   a->inv_freq_a, 1.0f, a->rope_scale_a, w + L.kh, w + L.kl, st,
-                                  1, dL, a->dca_chunk_size));
+                                  1, dL, a->dca_chunk_size, 0, stab, L.stab_R, L.stab_len));
       }
       sta_select_args s{};
       s.q_hi = w + L.qh;

@@ -20,7 +20,8 @@ int launch_rope_split(const void* x, int dtype, int64_t heads, int64_t N, int D,
                       int64_t stride_h, int64_t stride_n, const float* inv_freq,
                       float pos_scale, float rope_scale, void* hi, void* lo,
                       cudaStream_t stream, int mode = 0, int64_t dca_L = 0, int64_t dca_s = 0,
-                      int64_t pos0 = 0);
+                      int64_t pos0 = 0, const void* tab = nullptr, float tab_R = 0.f,
+                      int64_t tab_len = 0);
 
 int launch_select(const sta_select_args* a, cudaStream_t stream);
 int launch_rope_table(const float* inv_freq, int D, float rope_scale, float R, int64_t len,
