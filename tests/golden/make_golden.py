@@ -2,7 +2,7 @@
 
 Runs the reference repository's own Triton kernels on the CPU through the Triton interpreter
 (``TRITON_INTERPRET=1``) on small seeded inputs and stores inputs + outputs as ``.npz``.  The
-reference is imported read-only from ``--ref`` (default ``/root/reference``); it is NOT needed
+reference is imported read-only from the checkout given by ``--ref``; it is NOT needed
 at test time -- the committed fixtures are.
 
 Intermediate tensors (Kernel A's votes / wvotes / bits, and the selection outputs) are captured
