@@ -277,3 +277,26 @@ def test_decode_oracle_matches_reference(name):
     assert (a["idx"][:, cap:] == meta["M"]).all() and (idx[:, cap:] == meta["M"]).all()
     np.testing.assert_array_equal(npq, a["newpos_q"])
     assert np.abs(out - a["out"]).max() <= 1e-5
+
+
+def test_decode_rules_reduce_to_dense_attention_at_tau_inf():
+    """Invariant of every decode rule: tau = +inf keeps every cached key; with positions that
+    preserve the query-key distances (PI at pos_scale 1 = identity, dense ranks over all keys
+    = the positions, streamed positions = minus the distance to the query) each equals the
+    last row of dense causal RoPE attention."""
+    rng = np.random.default_rng(3)
+    H, M, D = 2, 97, 32
+    q = rng.standard_normal((H, M, D)).astype(np.float32)
+    k = rng.standard_normal((H, M, D)).astype(np.float32)
+    v = rng.standard_normal((H, M, D)).astype(np.float32)
+    invf = (1.0 / (1e4 ** (np.arange(0, D, 2, dtype=np.float32) / D))).astype(np.float32)
+    tau = np.full(H, np.inf, np.float32)
+    sm = 1.0 / math.sqrt(D)
+    dense = oracle.dense_rope_attention(q, k, v, invf)[:, M - 1]
+    outs = [oracle.decode_pi(q[:, M - 1], k, v, tau, invf, 1.0, 1.0, sm, 32, 32, 4 * M)[0],
+            oracle.decode_rank(q[:, M - 1], k, v, tau, invf, invf, 1.0, 1.0, sm, 32, 32, 4 * M)[0],
+            oracle.decode_stream(q[:, M - 1], k, v, tau, invf, invf, 1.0, 1.0, sm, 32, 32, 16)[0],
+            oracle.decode_chunk(q[:, M - 1], k, v, tau, invf, invf, 1.0, 1.0, sm, 32, 32, 4 * M,
+                                16, 64)[0]]
+    for o in outs:
+        assert np.abs(o - dense).max() <= 1e-4
