@@ -300,3 +300,24 @@ def test_decode_rules_reduce_to_dense_attention_at_tau_inf():
                                 16, 64)[0]]
     for o in outs:
         assert np.abs(o - dense).max() <= 1e-4
+
+
+def test_prefill_rules_reduce_to_dense_attention_at_tau_inf():
+    """Invariant of the prefill paths: tau = +inf with a budget that keeps everything (pct 100,
+    k_max >= N, every chunk) and positions that preserve distances (pos_scale 1 for the shared
+    path; dense ranks over all keys = the positions for PQ-Union and chunk_exact) equals dense
+    causal RoPE attention -- the property the GPU hook tests rely on."""
+    rng = np.random.default_rng(4)
+    H, N, D = 2, 150, 32
+    q = rng.standard_normal((H, N, D)).astype(np.float32)
+    k = rng.standard_normal((H, N, D)).astype(np.float32)
+    v = rng.standard_normal((H, N, D)).astype(np.float32)
+    invf = (1.0 / (1e4 ** (np.arange(0, D, 2, dtype=np.float32) / D))).astype(np.float32)
+    tau = np.full(H, np.inf, np.float32)
+    dense = oracle.dense_rope_attention(q, k, v, invf)
+    shared = oracle.shared_attention(q, k, v, tau, invf, 1.0, 1.0, invf, 1.0, 1.0, pct=100.0,
+                                     tile=32, k_max=4 * N)[0]
+    pqu = oracle.pq_attention(q, k, v, tau, invf, invf, k_max=4 * N)[0]
+    chk = oracle.chunk_attention(q, k, v, tau, invf, invf, k_max=4 * N, n_chunk=64)[0]
+    for o in (shared, pqu, chk):
+        assert np.abs(o - dense).max() <= 1e-4
