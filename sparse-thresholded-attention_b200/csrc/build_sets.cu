@@ -238,7 +238,26 @@ __global__ void __launch_bounds__(kBT) build_sets_kernel(const BuildP p) {
   for (int i = tid; i < 256; i += kBT) hist[i] = 0u;
   __syncthreads();
   int nz = 0;
-  for (int64_t j = tid; j < r.hi; j += kBT) {
+  int64_t j_tail = 0;
+  if ((reinterpret_cast<uintptr_t>(r.v) & 7u) == 0) {
+    // 8 votes per load; most keys have none, so all-zero words are skipped
+    const int64_t nw = r.hi / 8;
+    const uint2* vw = reinterpret_cast<const uint2*>(r.v);
+    for (int64_t w = tid; w < nw; w += kBT) {
+      const uint2 u = vw[w];
+      if ((u.x | u.y) == 0u) continue;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t v = ((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 255u;
+        if (v) {
+          ++nz;
+          if (!weighted) atomicAdd(&hist[v], 1u);
+        }
+      }
+    }
+    j_tail = nw * 8;
+  }
+  for (int64_t j = j_tail + tid; j < r.hi; j += kBT) {
     const uint32_t v = r.v[j];
     if (v) {
       ++nz;
