@@ -79,29 +79,9 @@ def peaks():
 def workload(args):
     """Inputs + geometry of the benchmark config (full tensors, on the CPU)."""
     import torch
-    from sta.synth import config, make_config_inputs, rope_inv_freq, yarn_inv_freq
-    c = config(args.config)
+    from sta.synth import config_geometry, make_config_inputs
     q, k, v, c = make_config_inputs(args.config, seq_len=args.seq_len, n_heads=args.heads)
-    D = c["D"]
-    if c["geom"] == "yarn":
-        invf, ms = yarn_inv_freq(D, c["theta"], c["yarn_factor"], c["yarn_orig"])
-        geo = dict(inv_freq=invf, pos_scale=1.0, rope_scale=ms)
-        geo_c = dict(geo)
-    elif c["geom"] == "hybrid":
-        # selection: Dual Chunk Attention positions (ChunkLlama rule, s < c as the reference
-        # asserts: s = 6144, w = 1024, c = 8192 -> chunk_len 5120) with its mscale
-        # 0.05 ln(S / c) + 1; attend: PI with base RoPE at pos_scale 0.5
-        invf = rope_inv_freq(D, c["theta"])
-        ms = 0.05 * math.log(c["S"] / c["dca_pretrain"]) + 1.0 if c["S"] > c["dca_pretrain"] else 1.0
-        geo = dict(inv_freq=invf, pos_scale=1.0, rope_scale=ms,
-                   dca=(c["dca_chunk_size"], c["dca_local_window"]))
-        geo_c = dict(inv_freq=invf, pos_scale=c["pos_scale_c"], rope_scale=1.0)
-    else:
-        invf = rope_inv_freq(D, c["theta"])
-        geo = dict(inv_freq=invf, pos_scale=c.get("pos_scale", 1.0), rope_scale=1.0)
-        geo_c = dict(geo)
-    if args.variant != "shared":
-        geo_c = dict(inv_freq=rope_inv_freq(D, c["theta"]), pos_scale=1.0, rope_scale=1.0)
+    geo, geo_c = config_geometry(c, args.variant)
     tau = torch.full((c["H"],), float(c["tau"]))
     return q, k, v, tau, geo, geo_c, c
 
@@ -212,7 +192,12 @@ def run_reference_gpu(args):
 
 
 def run_reference(args):
-    """--impl reference: the reference's algorithm on the host cores (oracle port)."""
+    """--impl reference: the reference's algorithm on the host cores (oracle port).
+
+    A full cfg2 layer would take minutes of CPU time per step, so each step is a bounded sample
+    (48 query tiles of one q head) whose time is extrapolated by causal key count to the whole
+    layer.  The line says so: `extrapolated` is true, `steps` / `ms_per_step` are the timed
+    samples themselves, `value` is the extrapolated whole-layer throughput."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -222,26 +207,42 @@ def run_reference(args):
     world = args.gpus
     for i in range(args.warmup):
         cpu_sample(q, k, v, tau, geo, c, n_tiles=2, seed=100 + i, geo_c=geo_c)
-    vals, secs = [], 0.0
+    vals, secs = [], []
     t0 = time.perf_counter()
     desc = ""
+    n_tiles = 48
     for i in range(args.steps):
-        tok, dt, desc = cpu_sample(q, k, v, tau, geo, c, n_tiles=48, seed=i, geo_c=geo_c)
+        tok, dt, desc = cpu_sample(q, k, v, tau, geo, c, n_tiles=n_tiles, seed=i, geo_c=geo_c)
         vals.append(tok)
-        secs += dt
+        secs.append(dt)
     value = statistics.median(vals)
     cores = os.cpu_count() or 1
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 * c["B"] * c["S"] / value, "higher_is_better": True,
+            "ms_per_step": 1e3 * statistics.median(secs),
+            "extrapolated": True,
+            "sample_per_step": f"{n_tiles} query tiles of 1 of {c['H'] * c['B']} q heads",
+            "est_ms_per_layer": 1e3 * c["B"] * c["S"] / value,
+            "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32 (numpy oracle on bf16 inputs)",
             "data": "synthetic (seeded, sta.synth)", "config": workload_desc(c, args, 1),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": desc},
+                             "cpu_model": cpu_model(), "sample": desc},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
             "wall_s": time.perf_counter() - t0}
     emit(line)
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
 
 
 # ---------------------------------------------------------------------------------------------
@@ -425,10 +426,11 @@ def run_gpu(args):
     sel_ms = stage_ms[1]
     achieved = flops_sel / (sel_ms / 1e3) / 1e12
     peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
-    traffic = select_traffic_bytes(c, Hr, pairs)
+    traffic, traffic_src = select_traffic_bytes(c, Hr, s0, s1)
     roof = {"kernel": "select_kernel (tcgen05 exact-max two-pass Kernel A)", "bound": "tensor",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "peak_kind": f"{pk_kind} bf16 sustained", "traffic": traffic,
+            "traffic_source": traffic_src,
             "algorithmic_flops_per_launch": flops_sel, "launch_ms": sel_ms,
             "tensor_flops_issued_per_launch": 3 * flops_sel,
             "note": "3 bf16 products per fp32-accurate score (hi*hi + hi*lo + lo*hi)"}
@@ -515,15 +517,28 @@ def run_decode(args):
                        "note": f"K cache read once for the scores ({kv_bytes} bytes); {pk_kind} peak"}})
 
 
-def select_traffic_bytes(c, heads, pairs):
-    """DRAM bytes per select launch from the committed ncu summary, scaled by causal work."""
+def select_traffic_bytes(c, heads, s0, s1):
+    """DRAM bytes of one select launch.  A committed ncu measurement at the same shape is used
+    as is; otherwise the committed small-case measurement is split into the part that grows
+    with the rows (first reads of the q / k hi + lo operands: S) and the rest (K re-reads that
+    miss L2 and the compact vote writes: causal pairs, S^2), and each part is scaled by its
+    own law."""
     p = os.path.join(ROOT, "profiles", "select_kernel_traffic.json")
     if not os.path.exists(p):
-        return None
+        return None, None
     with open(p) as f:
         d = json.load(f)
-    scale = (heads * 2 * pairs) / (d["heads"] * d["seq_len"] * (d["seq_len"] + 1))
-    return d["dram_bytes"] * scale
+    D, G = c["D"], c["H"] // c["Hkv"]
+    if d.get("seq_len") == s1 and s0 == 0 and d.get("heads") == heads and d.get("head_dim", D) == D:
+        return d["dram_bytes"], "ncu at this shape"
+    n0, h0 = d["seq_len"], d["heads"]
+    lin0 = 4 * D * n0 * (h0 + h0 // G)                  # q hi + lo, k hi + lo (bf16)
+    quad0 = max(d["dram_bytes"] - lin0, 0)
+    rows = s1 - s0
+    lin = 4 * D * (rows * heads + s1 * max(heads // G, 1))
+    pairs = (s1 * (s1 + 1) - s0 * (s0 + 1)) / 2
+    quad = quad0 * (heads * pairs) / (h0 * n0 * (n0 + 1) / 2)
+    return lin + quad, f"ncu at S={n0}, split into S and S^2 parts and scaled"
 
 
 _JSON_FD = None

@@ -48,7 +48,7 @@ extern "C" {
  * Library
  * ------------------------------------------------------------------------------------- */
 const char* sta_last_error(void);
-/* ABI version: 2 (query slabs, PQ-Stream pass 2 on Kernel A keep bits, decode) */
+/* ABI version: 3 (2: query slabs, PQ-Stream pass 2 on Kernel A keep bits, decode; 3: select wait limit) */
 int sta_version(void);
 /* Number of elements of one head of a compact selection array. */
 int64_t sta_tri_head_stride(int64_t n, int32_t tile);
@@ -121,6 +121,11 @@ typedef struct sta_select_args {
    * apart; a 64-key block's entry sits at its first 32-key index. */
   uint8_t* block_max;
   int32_t block_max_bn;
+  /* bound of every device-side wait of the kernel in nanoseconds (0 = the default, 4 s).  On
+   * expiry the kernel unwinds and sets the device error word read by sta_device_error; the
+   * call itself has already returned STA_OK (launches are asynchronous).  Small values exist
+   * to exercise that failure path in tests. */
+  uint64_t wait_limit_ns;
 } sta_select_args;
 
 int sta_select(const sta_select_args* a, void* stream);
@@ -414,7 +419,6 @@ int sta_pq_stream_forward(const sta_forward_args* a, void* workspace, size_t wor
 #define STA_STATIC_SCRATCH_BYTES (64ull << 20)
 int sta_shared_forward_static(const sta_forward_args* a, void* stream);
 
-/* Error flag of the last bounded device wait on this device: 0 = none. */
 /* ---------------------------------------------------------------------------------------
  * Decode: one query per head against the KV cache (keys 0 .. m-1, the query at position m-1).
  * Replaces the per-query selection + attend of the reference's decode paths:
@@ -481,6 +485,11 @@ size_t sta_decode_workspace_bytes(const sta_decode_args* a);
 int sta_decode_forward(const sta_decode_args* a, void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/* Error word of the bounded device waits on the current device (0 = none; 101-104 name the
+ * wait of the selection kernel that expired).  Kernels report an expired wait only through
+ * this word -- the launching call has already returned STA_OK -- so a C caller that needs to
+ * know polls it after the stream's work: it synchronises `stream`, stores the word in
+ * *code_out, clears it, and returns STA_ERR_TIMEOUT when it was set. */
 int sta_device_error(void* stream, int32_t* code_out);
 
 #ifdef __cplusplus

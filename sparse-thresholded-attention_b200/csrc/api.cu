@@ -484,7 +484,7 @@ extern "C" {
 
 const char* sta_last_error(void) { return g_last_error; }
 
-int sta_version(void) { return 2; }
+int sta_version(void) { return 3; }
 
 int64_t sta_tri_head_stride(int64_t n, int32_t tile) { return tri_head_stride(n, tile); }
 
@@ -559,6 +559,14 @@ int sta_chunk_forward(const sta_forward_args* a, void* workspace, size_t workspa
                       void* stream) {
   return run_forward(a, kChunk, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
+
+}  // extern "C"
+
+namespace sta {
+int check_shared_forward(const sta_forward_args* a) { return check_forward(a, kShared); }
+}  // namespace sta
+
+extern "C" {
 
 int sta_shared_forward(const sta_forward_args* a, void* workspace, size_t workspace_bytes,
                        void* stream) {

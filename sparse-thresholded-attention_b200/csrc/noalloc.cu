@@ -5,11 +5,14 @@
 // under a fixed memory budget decided before the process starts, or integrations that only
 // hand over the input and output buffers.  sta_shared_forward_static serves them: it is
 // sta_shared_forward with its scratch taken from a fixed array in device memory that this
-// library reserves when it is loaded, so a call allocates nothing.
+// library holds, so a call allocates nothing.
 //
 // Contract (also stated in include/sta.h):
 //  * the array holds STA_STATIC_SCRATCH_BYTES (64 MiB); every GPU that loads the library keeps
-//    it for the life of the process;
+//    it for the life of the process.  The CUDA runtime reserves it when it loads this module
+//    on a device: at library load with CUDA_MODULE_LOADING=EAGER, otherwise (the default, lazy
+//    loading) on the first call on that device -- so under lazy loading the first call can
+//    still fail with out-of-memory (STA_ERR_CUDA) if the device is already full;
 //  * when the op's scratch would be larger, the op walks over smaller groups of kv heads; if a
 //    single kv head still needs more, the call fails with STA_ERR_WORKSPACE and a message;
 //  * the first call on a device looks up the array's device address (cudaGetSymbolAddress) with
@@ -36,6 +39,9 @@ void* g_static_scratch_addr[64] = {nullptr};
 extern "C" int sta_shared_forward_static(const sta_forward_args* a, void* stream) {
   using namespace sta;
   if (!a) return fail(STA_ERR_ARG, "sta_shared_forward_static: null arguments");
+  const int rc = check_shared_forward(a);
+  if (rc != STA_OK) return rc;
+  if (a->n <= 0 || a->batch <= 0) return STA_OK;  // nothing to do (as sta_shared_forward)
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(STA_ERR_CUDA, cudaGetErrorString(e));
@@ -52,7 +58,7 @@ extern "C" int sta_shared_forward_static(const sta_forward_args* a, void* stream
   const int64_t cap = (int64_t)STA_STATIC_SCRATCH_BYTES_VALUE;
   if (b.max_workspace_bytes <= 0 || b.max_workspace_bytes > cap) b.max_workspace_bytes = cap;
   const size_t need = sta_shared_workspace_bytes(&b);
-  if (need == 0) return STA_ERR_ARG;  // argument error, message already recorded
+  if (need == 0) return fail(STA_ERR_ARG, "sta_shared_forward_static: empty workspace layout");
   if (need > (size_t)STA_STATIC_SCRATCH_BYTES_VALUE)
     return fail(STA_ERR_WORKSPACE,
                 "sta_shared_forward_static: one kv head of this problem needs more scratch than "

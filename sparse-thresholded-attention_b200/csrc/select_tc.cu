@@ -75,6 +75,7 @@ struct Params {
   uint8_t* block_max;   // PQ-Stream block maxima (tile 32) or null
   int bmax_bn;
   int64_t bmax_head_stride;
+  uint64_t limit_ns;    // bound of every mbarrier wait
 };
 
 // Which rotated Q plane scores key block kb of query block qb: 0 = plain (or same DCA chunk),
@@ -195,7 +196,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             const int plane = q_plane(p, qb, kb);
             if (plane != cur) {
               if (qloads > 0 &&
-                  !mbar_wait(q_empty, (qloads - 1) & 1, s_abort, p.err, kErrTimeoutQ)) {
+                  !mbar_wait(q_empty, (qloads - 1) & 1, s_abort, p.err, kErrTimeoutQ, p.limit_ns)) {
                 ok = false;
                 break;
               }
@@ -211,7 +212,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             }
             for (int piece = 0; piece < 2; ++piece, ++kc) {  // hi piece, then lo piece
               const uint32_t s = kc % C::NSTAGE, r = kc / C::NSTAGE;
-              if (r > 0 && !mbar_wait(k_empty + s, (r - 1) & 1, s_abort, p.err, kErrTimeoutEmpty)) {
+              if (r > 0 && !mbar_wait(k_empty + s, (r - 1) & 1, s_abort, p.err, kErrTimeoutEmpty, p.limit_ns)) {
                 ok = false;
                 break;
               }
@@ -246,7 +247,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             if (plane != cur) {
               // the resident Q tile is released once every MMA issued so far has completed
               if (qloads > 0) umma_commit(q_empty);
-              if (!mbar_wait(q_full, qloads & 1, s_abort, p.err, kErrTimeoutQ)) {
+              if (!mbar_wait(q_full, qloads & 1, s_abort, p.err, kErrTimeoutQ, p.limit_ns)) {
                 ok = false;
                 break;
               }
@@ -256,7 +257,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             }
             const uint32_t slot = ac % NACC, use = ac / NACC;
             if (use > 0 && !mbar_wait(acc_empty + slot, (use - 1) & 1, s_abort, p.err,
-                                      kErrTimeoutAcc)) {
+                                      kErrTimeoutAcc, p.limit_ns)) {
               ok = false;
               break;
             }
@@ -265,7 +266,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             // piece 0 (K hi): Qhi.Khi + Qlo.Khi ; piece 1 (K lo): Qhi.Klo
             for (int piece = 0; piece < 2; ++piece, ++kc) {
               const uint32_t s = kc % C::NSTAGE, r = kc / C::NSTAGE;
-              if (!mbar_wait(k_full + s, r & 1, s_abort, p.err, kErrTimeoutK)) {
+              if (!mbar_wait(k_full + s, r & 1, s_abort, p.err, kErrTimeoutK, p.limit_ns)) {
                 ok = false;
                 break;
               }
@@ -328,7 +329,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
         for (int kb = 0; kb < nb; ++kb, ++ac) {
           const uint32_t slot = ac % NACC, use = ac / NACC;
           int bad = 0;
-          if (ok && lane == 0) bad = !mbar_wait(acc_full + slot, use & 1, s_abort, p.err, kErrTimeoutAcc);
+          if (ok && lane == 0) bad = !mbar_wait(acc_full + slot, use & 1, s_abort, p.err, kErrTimeoutAcc, p.limit_ns);
           if (__shfl_sync(0xffffffffu, bad, 0)) ok = false;
           if (ok) {
             tc_fence_after();
@@ -546,6 +547,7 @@ int launch_select(const sta_select_args* a, cudaStream_t stream) {
   p.block_max = a->max_only ? nullptr : a->block_max;
   p.bmax_bn = a->block_max_bn;
   p.bmax_head_stride = tri_head_stride((a->n + 31) / 32, 1, a->q_pos_base / 32);
+  p.limit_ns = a->wait_limit_ns > 0 ? a->wait_limit_ns : 4000000000ull;
   if (p.block_max && (a->tile != 32 || (p.bmax_bn != 32 && p.bmax_bn != 64)))
     return fail(STA_ERR_UNSUPPORTED, "sta_select: block_max needs tile 32 and block_max_bn 32 or 64");
   if (p.dca_L > 0 && (p.dca_L % BN)) return fail(STA_ERR_UNSUPPORTED, "sta_select: DCA chunk_len must be a multiple of 256");

@@ -13,6 +13,9 @@ namespace sta {
 void set_error(const char* msg);
 int fail(int code, const char* msg);
 
+// argument check of sta_shared_forward (STA_OK or the failure code, message recorded)
+int check_shared_forward(const sta_forward_args* a);
+
 // global device error word (bounded waits that expired)
 int* device_error_word();
 

@@ -30,7 +30,7 @@ class SelectArgs(ctypes.Structure):
                 ("tau", c_vp), ("max_only", c_i32), ("votes", c_vp), ("wvotes", c_vp),
                 ("bits", c_vp), ("row_max", c_vp), ("row_count", c_vp),
                 ("dca_chunk_len", c_i32), ("q_pos_base", c_i64),
-                ("block_max", c_vp), ("block_max_bn", c_i32)]
+                ("block_max", c_vp), ("block_max_bn", c_i32), ("wait_limit_ns", ctypes.c_uint64)]
 
 
 class BuildArgs(ctypes.Structure):

@@ -19,10 +19,15 @@ def _batch(q, k, v):
     return q.shape[0]
 
 
+_Q_POS_BASE_MSG = ("q_pos_base must be 0 here: every reference prefill call passes 0 with q and k "
+                   "covering the same positions 0..N-1.  Query slabs (q holding positions "
+                   "q_pos_base..N-1 against all N keys) are sta.core.forward(..., q_pos_base=...)")
+
+
 def _check_prefill(q_pos_base):
+    """Raise ValueError unless q_pos_base == 0 (see _Q_POS_BASE_MSG)."""
     if int(q_pos_base) != 0:
-        raise NotImplementedError("prefill kernels index keys by absolute position from 0 "
-                                  "(q_pos_base must be 0, as at every reference prefill call)")
+        raise ValueError(_Q_POS_BASE_MSG)
 
 
 def shared_attention(q, k, v, tau, ga: Geometry, gc: Geometry, pct=30.0, sm_scale=None,

@@ -431,16 +431,43 @@ def tri_head_stride(n: int, tile: int) -> int:
     return int(L.lib().sta_tri_head_stride(n, tile))
 
 
+def rope_split_dca(x: torch.Tensor, g: Geometry, role: int, out_hi=None, out_lo=None):
+    """x (heads, n, d) -> (hi, lo) bf16 rotated at Dual Chunk Attention position role
+    (1 keys / same-chunk queries, 2 previous-chunk queries, 3 older-chunk queries)."""
+    x = _rows(x)
+    Hx, N, D = x.shape
+    hi = out_hi if out_hi is not None else torch.empty((Hx, N, D), dtype=torch.bfloat16,
+                                                       device=x.device)
+    lo = out_lo if out_lo is not None else torch.empty_like(hi)
+    invf = _dev_f32(g.inv_freq, x.device)
+    L.check(L.lib().sta_rope_split_dca(_p(x), dtype_code(x.dtype), Hx, N, D, x.stride(0),
+                                       x.stride(1), _p(invf), float(g.rope_scale),
+                                       int(g.dca[0]), int(g.dca[1]), int(role), _p(hi), _p(lo),
+                                       _stream()), "sta_rope_split_dca")
+    return hi, lo
+
+
 def select(q: torch.Tensor, k: torch.Tensor, tau, g: Geometry, *, tile, sm_scale=None,
-           wmode=0, bits=False, max_only=False):
+           wmode=0, bits=False, max_only=False, wait_limit_ns=0):
     """Kernel A on raw (H,N,D) q and (Hkv,N,D) k.  Returns dict of compact votes / wvotes /
-    bits, row_max (H,N) and row_count (H,N)."""
+    bits, row_max (H,N) and row_count (H,N).  `wait_limit_ns` bounds every device-side wait
+    (0: the library default); an expired wait shows in device_error(), not here.  With
+    ``g.dca`` the selection geometry is Dual Chunk Attention (three rotated query planes)."""
     H, N, D = q.shape
     Hk = k.shape[0]
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
-    qh, ql = rope_split(q, g)
-    kh, kl = rope_split(k, g)
+    dca_len = 0
+    if g.dca is None:
+        qh, ql = rope_split(q, g)
+        kh, kl = rope_split(k, g)
+    else:
+        qh = torch.empty((3, H, N, D), dtype=torch.bfloat16, device=q.device)
+        ql = torch.empty_like(qh)
+        for role in (1, 2, 3):
+            rope_split_dca(q, g, role, qh[role - 1], ql[role - 1])
+        kh, kl = rope_split_dca(k, g, 1)
+        dca_len = int(g.dca[0]) - int(g.dca[1])
     HS = tri_head_stride(N, tile)
     dev = q.device
     res = {"row_max": torch.empty((H, N), dtype=torch.float32, device=dev),
@@ -464,6 +491,8 @@ def select(q: torch.Tensor, k: torch.Tensor, tau, g: Geometry, *, tile, sm_scale
     a.bits = res["bits"].data_ptr() if "bits" in res else None
     a.row_max = res["row_max"].data_ptr()
     a.row_count = res["row_count"].data_ptr()
+    a.dca_chunk_len = dca_len
+    a.wait_limit_ns = int(wait_limit_ns)
     L.check(L.lib().sta_select(ctypes.byref(a), _stream()), "sta_select")
     return res
 
@@ -492,6 +521,8 @@ def compact_from_dense(dense: torch.Tensor, tile: int):
 
 
 def device_error() -> int:
+    """Synchronise the current stream and return (and clear) the device error word of the
+    bounded waits: 0 when no wait expired since the last read."""
     code = L.c_i32(0)
     L.lib().sta_device_error(_stream(), ctypes.byref(code))
     return int(code.value)

@@ -15,6 +15,17 @@ from __future__ import annotations
 import torch
 
 
+def _check_device_waits():
+    """Raise when a bounded device wait of the prefill kernels expired (the launches return
+    before the kernels run, so such a failure only shows in the device error word; reading it
+    synchronises the stream once per prefill call)."""
+    from .core import device_error
+    code = device_error()
+    if code:
+        raise RuntimeError(f"thresholded attention: a bounded device wait expired (code {code}); "
+                           "the layer output is incomplete")
+
+
 def _rope_theta(cfg):
     theta = 10000.0
     rp = getattr(cfg, "rope_parameters", None) or getattr(cfg, "rope_scaling", None)
@@ -107,6 +118,7 @@ def make_shared_installer(geom, attention_fn, select_score=False, hybrid=False):
                 (self.spi_last_shared, self.spi_last_kept, self.spi_last_kpct,
                  self.spi_last_overflow, self.spi_last_kpct_meas,
                  self.spi_last_overflow20) = res[1:]
+                _check_device_waits()
             else:
                 from .core import Geometry, decode
                 outs = []
@@ -222,6 +234,7 @@ def _install_per_query(kind, model, prefix, cfg):
                     *args, pos_advance=g("advance"), use_skip=g("use_skip"), **kw)
                 self.pqs_last_span, self.pqs_last_kept = span, kept
                 self.pqs_last_skipped = skipped
+            _check_device_waits()
         else:
             # decode, or the per-query prefill mode: one device decode call per query position
             mode = {"pq": "rank", "chunk": "chunk", "stream": "stream"}[kind]

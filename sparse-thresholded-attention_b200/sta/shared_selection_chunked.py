@@ -11,6 +11,7 @@ reference's ``torch.topk`` order among ties is implementation-defined).
 """
 from __future__ import annotations
 
+from ._surface import _check_prefill
 from .core import Geometry, forward
 
 
@@ -67,8 +68,7 @@ def shared_chunk_attention(q, k, v, tau, inv_freq_a, inv_freq_c, pos_scale_a=1.0
     bound = min(nC_total, nf + n_chunk) * chunk_size
     assert bound <= k_max, (f"budget overflow: min(nC={nC_total}, {nf} forced + {n_chunk} "
                             f"selected) * {chunk_size} = {bound} > k_max={k_max}")
-    if int(q_pos_base) != 0:
-        raise NotImplementedError("prefill requires q_pos_base == 0")
+    _check_prefill(q_pos_base)
     if chunk_agg not in ("sum", "mean"):
         raise KeyError(chunk_agg)
     out, st, _ = forward("chunk", q, k, v, tau, Geometry(inv_freq_a, pos_scale_a, rope_scale_a),

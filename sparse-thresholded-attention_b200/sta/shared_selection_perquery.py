@@ -6,6 +6,7 @@ via the tile's full union + forced keys, dense-rank positions and a per-query sl
 reference accessors (get_overflow_stats / reset_overflow_stats, :56-110)."""
 from __future__ import annotations
 
+from ._surface import _check_prefill
 from .core import Geometry, forward
 
 
@@ -58,8 +59,7 @@ def shared_pq_attention(q, k, v, tau, inv_freq_a, inv_freq_c, pos_scale_a=1.0, r
         raise AssertionError("pq_exact packs per-query keep bits into int32 -> tile must be 32")
     if n_global + n_local + tile - 1 > k_max:
         raise AssertionError(f"forced set ({n_global + n_local + tile - 1}) exceeds k_max={k_max}")
-    if int(q_pos_base) != 0:
-        raise NotImplementedError("prefill requires q_pos_base == 0")
+    _check_prefill(q_pos_base)
     out, st, _ = forward("pq_union", q, k, v, tau, Geometry(inv_freq_a, pos_scale_a, rope_scale_a),
                          Geometry(inv_freq_c, 1.0, 1.0), sm_scale=sm_scale, n_global=n_global,
                          n_local=n_local, tile=32, k_max=k_max, select_score=select_score)

@@ -180,3 +180,34 @@ def make_config_inputs(idx: int, seq_len: int | None = None, n_heads: int | None
     q, k, v = make_inputs(spec)
     c = dict(c, S=S, H=H, Hkv=Hk, B=B, planted=planted)
     return q, k, v, c
+
+
+def config_geometry(c: dict, variant: str = "shared"):
+    """Selection and attend geometries of a benchmark config: (ga, gc) dicts with inv_freq,
+    pos_scale, rope_scale (and dca for the hybrid config's selection).
+
+    * yarn: YaRN frequencies and attention factor, raw positions, for both;
+    * hybrid: selection in the Dual Chunk Attention geometry (ChunkLlama rule with s < c as the
+      reference asserts, dca_kernel.py:553: s = 6144, w = 1024 for c = 8192, so chunk_len 5120)
+      with its mscale 0.05 ln(S / c) + 1; attend with base RoPE at PI scale pos_scale_c;
+    * pi: base RoPE at pos_scale for both.
+    The per-query variants attend with base RoPE at raw positions (rope_scale 1)."""
+    import math
+    D = c["D"]
+    if c["geom"] == "yarn":
+        invf, ms = yarn_inv_freq(D, c["theta"], c["yarn_factor"], c["yarn_orig"])
+        ga = dict(inv_freq=invf, pos_scale=1.0, rope_scale=ms)
+        gc = dict(ga)
+    elif c["geom"] == "hybrid":
+        invf = rope_inv_freq(D, c["theta"])
+        ms = 0.05 * math.log(c["S"] / c["dca_pretrain"]) + 1.0 if c["S"] > c["dca_pretrain"] else 1.0
+        ga = dict(inv_freq=invf, pos_scale=1.0, rope_scale=ms,
+                  dca=(c["dca_chunk_size"], c["dca_local_window"]))
+        gc = dict(inv_freq=invf, pos_scale=c["pos_scale_c"], rope_scale=1.0)
+    else:
+        invf = rope_inv_freq(D, c["theta"])
+        ga = dict(inv_freq=invf, pos_scale=c.get("pos_scale", 1.0), rope_scale=1.0)
+        gc = dict(ga)
+    if variant != "shared":
+        gc = dict(inv_freq=rope_inv_freq(D, c["theta"]), pos_scale=1.0, rope_scale=1.0)
+    return ga, gc

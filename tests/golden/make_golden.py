@@ -8,7 +8,7 @@ at test time -- the committed fixtures are.
 Intermediate tensors (Kernel A's votes / wvotes / bits, and the selection outputs) are captured
 by wrapping the reference module's host selection function for the duration of one call.
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py --ref <reference checkout>
 """
 from __future__ import annotations
 
@@ -124,6 +124,32 @@ def gen_shared(ref, mod_name, case, H, N, D, T, k_max, seed, dtype, select_score
     if wvotes is not None and wvotes.shape[-1] == N:
         arrays["wvotes"] = wvotes
     save(case, meta, arrays)
+
+
+def gen_cfg0(case):
+    """Benchmark config 0 exactly (sta.synth.config(0): fp32, H = Hkv = 4, S 1024, D 64, tile 64,
+    tau 5, top 30 %, cap 2048, plain RoPE theta 1e4, seed 0, 32 planted keys per head) through
+    the reference's shared_pi_attention (shared_selection_triton_exact_2.py:432-486).  The
+    inputs are regenerated by sta.synth at test time; the fixture stores their SHA-256."""
+    import hashlib
+    from sta.synth import config_geometry, make_config_inputs
+    mod = __import__("shared_selection_triton_exact_2")
+    q, k, v, c = make_config_inputs(0)
+    ga, _ = config_geometry(c)
+    tau = torch.full((c["H"],), float(c["tau"]))
+    with Capture(mod, "_build_sets") as cap:
+        res = mod.shared_pi_attention(q, k, v, tau, ga["inv_freq"], pos_scale=ga["pos_scale"],
+                                      pct=c["pct"], rope_scale=ga["rope_scale"], tile=c["T"],
+                                      k_max=c["k_max"])
+    h = hashlib.sha256()
+    for x in (q, k, v):
+        h.update(x.contiguous().numpy().tobytes())
+    meta = dict(kind="shared", module="shared_selection_triton_exact_2", config=0, H=c["H"],
+                N=c["S"], S=c["S"], D=c["D"], T=c["T"], k_max=c["k_max"], seed=c["seed"],
+                pct=c["pct"], tau=c["tau"], inputs_sha256=h.hexdigest())
+    sets = cap.result
+    save(case, meta, dict(out=res[0][0], shared_size=res[1], kept_size=res[2], kpct=res[3],
+                          overflow=res[4], votes=cap.args[0], idx=sets[0]))
 
 
 def gen_pq(case, H, N, D, k_max, seed, dtype, select_score="expmass", geom="pi",
@@ -299,7 +325,8 @@ def gen_decode(case, mode, H, M, D, seed, k_max=64, pct_decode=100.0, block_n=32
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True,
+                    help="directory of the reference checkout (its modules are imported)")
     ap.add_argument("--only", default=None, help="generate only cases whose name contains this")
     args = ap.parse_args()
     global ONLY
@@ -325,6 +352,8 @@ def main():
                64, 32, 128, 16, f32, geom="hybrid", pos_scale=0.5, select_score="expmass")
     gen_shared(None, "shared_selection_triton_exact_2", "shared_pi_freq_tau1_f32", 2, 256, 64, 64,
                2048, 18, f32, tau_val=1.0)
+    # benchmark config 0 at its own shape
+    gen_cfg0("config0_f32")
     # PQ-Union: overflow-forcing k_max, expmass and freq ranking, yarn select geometry
     gen_pq("pq_union_expmass_f32", 2, 288, 64, 160, 21, f32)
     gen_pq("pq_union_freq_f32", 2, 256, 64, 4096, 22, f32, select_score="freq")

@@ -133,4 +133,30 @@ def test_synth_is_deterministic():
 
 
 def test_abi_version():
-    assert L.lib().sta_version() == 2
+    assert L.lib().sta_version() == 3
+
+
+def _static_args():
+    a = L.ForwardArgs()
+    for f in ("q", "k", "v", "out", "tau", "inv_freq_a", "inv_freq_c", "shared_size",
+              "kept_size", "chosen", "overflow", "kpct_meas", "overflow20"):
+        setattr(a, f, 256)  # non-null placeholders: these calls return before any device work
+    a.dtype, a.batch, a.n_heads, a.n_kv_heads, a.d = 1, 1, 4, 2, 128
+    a.tile, a.k_max, a.pct = 64, 512, 30.0
+    a.pos_scale_a = a.pos_scale_c = a.rope_scale_a = a.rope_scale_c = 1.0
+    return a
+
+
+def test_static_entry_passes_through_argument_codes_without_gpu():
+    """The allocation-free entry reports the argument check's own code (head_dim 96 is
+    unsupported, not an argument error) and accepts an empty problem like sta_shared_forward,
+    whatever its position scales."""
+    lib = L.lib()
+    a = _static_args()
+    a.n, a.d = 256, 96
+    assert lib.sta_shared_forward_static(ctypes.byref(a), None) == 2
+    assert b"head_dim" in lib.sta_last_error()
+    a = _static_args()
+    a.n = 0
+    a.pos_scale_a = a.pos_scale_c = 0.125
+    assert lib.sta_shared_forward_static(ctypes.byref(a), None) == 0

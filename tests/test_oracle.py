@@ -321,3 +321,43 @@ def test_prefill_rules_reduce_to_dense_attention_at_tau_inf():
     chk = oracle.chunk_attention(q, k, v, tau, invf, invf, k_max=4 * N, n_chunk=64)[0]
     for o in (shared, pqu, chk):
         assert np.abs(o - dense).max() <= 1e-4
+
+
+def cfg0_inputs_sha256(q, k, v):
+    import hashlib
+    h = hashlib.sha256()
+    for x in (q, k, v):
+        h.update(x.contiguous().numpy().tobytes())
+    return h.hexdigest()
+
+
+def test_oracle_matches_reference_at_config0():
+    """Benchmark config 0 at its own shape (fixture made by the unmodified reference under the
+    Triton interpreter): votes equal except boundary pairs, the selection bit-exact on the
+    reference's votes, stats and outputs equal on every tile without boundary pairs."""
+    import json
+    import math
+    from sta.synth import config_geometry, make_config_inputs
+    q, k, v, c = make_config_inputs(0)
+    z = np.load(os.path.join(HERE, "golden", "config0_f32.npz"))
+    meta = json.loads(str(z["meta"]))
+    assert cfg0_inputs_sha256(q, k, v) == meta["inputs_sha256"]
+    ga, _ = config_geometry(c)
+    qx, kx, vx = (x[0].numpy() for x in (q, k, v))
+    invf = ga["inv_freq"].numpy()
+    T, N = c["T"], c["S"]
+    sm = 1.0 / math.sqrt(c["D"])
+    tau = np.full(c["H"], c["tau"], np.float32)
+    sel = oracle.select_vote(qx, kx, tau, invf, 1.0, 1.0, sm, T)
+    assert int(np.abs(sel["votes"] - z["votes"]).sum()) <= sel["boundary"]
+    s = oracle.build_sets(z["votes"], 1.0, 32, 32, c["pct"], T, c["k_max"])
+    np.testing.assert_array_equal(s[0], z["idx"])
+    np.testing.assert_array_equal(s[4], z["kept_size"])
+    o = oracle.shared_attention(qx, kx, vx, tau, invf, 1.0, 1.0, invf, 1.0, 1.0, tile=T,
+                                k_max=c["k_max"])
+    clean = sel["near_tiles"] == 0
+    assert clean.sum() >= clean.size // 2
+    np.testing.assert_array_equal(o[2][clean], z["kept_size"][clean])
+    for h, t in zip(*np.nonzero(clean)):
+        r0, r1 = t * T, min((t + 1) * T, N)
+        assert np.abs(o[0][h, r0:r1] - z["out"][h, r0:r1]).max() <= 1e-4, (h, t)
