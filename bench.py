@@ -46,12 +46,16 @@ def parse():
     ap.add_argument("--impl", choices=["sta", "reference", "reference_gpu"], default="sta",
                     help="reference: the reference algorithm on the host cores (oracle port); "
                          "reference_gpu: the reference's own Triton kernels on this GPU, from "
-                         "the unmodified install in baseline/_ref (configs 1 and 2)")
+                         "the unmodified install in baseline/_ref")
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--variant", choices=["shared", "pq_union", "pq_stream"], default="shared")
     ap.add_argument("--seq-len", type=int, default=None, help="override S (profiling only)")
     ap.add_argument("--heads", type=int, default=None, help="override q heads (profiling only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-compare", action="store_true",
+                    help="reference_gpu: skip the comparison with this build's results")
+    ap.add_argument("--ref-heads", type=int, default=2,
+                    help="reference_gpu, configs 3 / 4: (batch, head) units timed")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--partition", choices=["auto", "heads", "slabs", "grid"], default="auto",
                     help="multi-GPU unit: kv-head ranges, query slabs, or both (sta.partition)")
@@ -139,19 +143,105 @@ def cpu_sample(q, k, v, tau, geo, c, n_tiles=12, head=0, seed=0, geo_c=None):
     return tok_s, dt, desc
 
 
+class _Capture:
+    """Record the inputs / result of one module-level function of the reference for one call."""
+
+    def __init__(self, module, name):
+        self.module, self.name, self.orig = module, name, getattr(module, name)
+        self.args = self.result = None
+
+    def __enter__(self):
+        def wrapped(*a, **kw):
+            self.args = a
+            self.result = self.orig(*a, **kw)
+            return self.result
+        setattr(self.module, self.name, wrapped)
+        return self
+
+    def __exit__(self, *exc):
+        setattr(self.module, self.name, self.orig)
+
+
+def _time_calls(fn, warmup, steps):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def _compare_with_reference(c, q, k, v, tau, geo, geo_c, ref_out, ref_votes, ref_stats):
+    """This build vs the reference's Triton op on identical inputs (the reference receives
+    repeat_kv-expanded k / v, this build the GQA-native ones): Kernel A votes, per-tile
+    statistics, and outputs overall and on the tiles whose votes agree exactly."""
+    import numpy as np
+    import torch
+    from sta import core
+    from sta.core import Geometry
+    dev = q.device
+    H, N, T = c["H"], c["S"], c["T"]
+    nt = (N + T - 1) // T
+    ga = Geometry(geo["inv_freq"], geo["pos_scale"], geo["rope_scale"])
+    gc = Geometry(geo_c["inv_freq"], geo_c["pos_scale"], geo_c["rope_scale"])
+    out, st, _ = core.forward("shared", q, k, v, tau, ga, gc, tile=T, k_max=c["k_max"],
+                              pct=c["pct"])
+    sel = core.select(q[0], k[0], tau, ga, tile=T)
+    hi = torch.clamp((torch.arange(nt, device=dev) + 1) * T, max=N)
+    mask = torch.arange(N, device=dev)[None, :] < hi[:, None]            # (nt, N)
+    ours = sel["votes"].view(H, -1).int()
+    d = (ref_votes[0][:, mask].int() - ours).abs() if ref_votes.dim() == 4 else \
+        (ref_votes[:, mask].int() - ours).abs()
+    seg = torch.cumsum(hi, 0)
+    csum = torch.cumsum(d.long(), 1)
+    ends = csum[:, seg - 1]
+    per_tile = torch.diff(ends, dim=1, prepend=torch.zeros_like(ends[:, :1]))  # (H, nt)
+    agree = per_tile == 0
+    res = {"vote_entries": int(d.numel()), "vote_entries_differing": int((d > 0).sum()),
+           "vote_abs_diff_sum": int(d.sum()), "tiles": int(agree.numel()),
+           "tiles_votes_identical": int(agree.sum())}
+    for name in ("shared_size", "kept_size"):
+        r = ref_stats[name].to(dev).reshape(H, nt)
+        o = st[name][0].to(r.dtype)
+        res[f"{name}_equal_tiles"] = int((r == o).sum())
+        res[f"{name}_equal_on_identical_vote_tiles"] = bool((r == o)[agree].all())
+    err = (out[0].float() - ref_out[0].float()).abs()                    # (H, N, D)
+    res["out_max_abs"] = float(err.max())
+    res["out_mean_abs"] = float(err.mean())
+    row_agree = agree.repeat_interleave(T, 1)[:, :N]
+    e_ok = err[row_agree]
+    res["out_max_abs_identical_vote_tiles"] = float(e_ok.max()) if e_ok.numel() else None
+    res["out_mean_abs_identical_vote_tiles"] = float(e_ok.mean()) if e_ok.numel() else None
+    res["note"] = ("reference scores with tl.dot (TF32 on this GPU); this build with three bf16 "
+                   "products (~2^-16); vote differences are keys near the threshold")
+    return res
+
+
 def run_reference_gpu(args):
-    """--impl reference_gpu: the reference's own Triton prefill op (shared_pi_attention of
-    shared_selection_triton_exact_2.py / _YaRN_exact.py) on this GPU, same inputs and events
-    protocol.  The reference receives repeat_kv-expanded k / v as its hooks pass them
-    (exact_2.py:644-646).  Rank 0 only."""
+    """--impl reference_gpu: the reference's own Triton prefill ops on this GPU, unmodified,
+    imported from baseline/_ref, same seeded inputs and CUDA-events protocol.  The reference
+    receives repeat_kv-expanded k / v as its hooks pass them (exact_2.py:644-646).
+
+    configs 1 / 2 (shared): the whole layer, plus a comparison with this build on the same
+    inputs (votes, statistics, outputs).  Config 3 (the reference's two-geometry hybrid kernel,
+    shared_selection_triton_hybrid_exact.py:450-510; the reference has no thresholded DCA) and
+    config 4 (PQ-Union, perquery.py:459-525; PQ-Stream, pqstream_kernel.py:498-564): the
+    reference's (H, n_tiles, N) buffers do not fit a whole layer (68 GiB per array at 128k), so
+    the op runs per (batch element, head) -- exact, every head is independent -- on a few
+    heads, and the layer time is that per-head time x batch x heads (`extrapolated`).
+    Rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     ref_dir = os.path.join(ROOT, "baseline", "_ref")
     line = {"impl": "reference_gpu", "metric": METRIC, "unit": "tokens/s"}
-    if not os.path.isdir(ref_dir) or args.config not in (1, 2) or args.variant != "shared":
-        line["unavailable"] = ("reference install missing (baseline/_ref)" if not os.path.isdir(ref_dir)
-                               else "measured for the shared path of configs 1 and 2 only")
+    if not os.path.isdir(ref_dir):
+        line["unavailable"] = "reference install missing (baseline/_ref)"
         emit(line)
         return
     import tempfile as _tf
@@ -159,35 +249,77 @@ def run_reference_gpu(args):
     sys.path.insert(0, ref_dir)
     import torch
     q, k, v, tau, geo, geo_c, c = workload(args)
-    mod = __import__("shared_selection_triton_YaRN_exact" if c["geom"] == "yarn"
-                     else "shared_selection_triton_exact_2")
     dev = torch.device("cuda", 0)
-    G = c["H"] // c["Hkv"]
-    qd = q.to(dev)
-    kd = k.to(dev).repeat_interleave(G, 1)
-    vd = v.to(dev).repeat_interleave(G, 1)
+    torch.cuda.set_device(dev)
+    B, H, Hk, N = c["B"], c["H"], c["Hkv"], c["S"]
+    G = H // Hk
     taud = tau.to(dev)
-    invf = geo["inv_freq"].to(dev)
+    ia = geo["inv_freq"].to(dev)
+    ic = geo_c["inv_freq"].to(dev)
+    extra = {}
+    if args.config in (1, 2) and args.variant == "shared":
+        mod = __import__("shared_selection_triton_YaRN_exact" if c["geom"] == "yarn"
+                         else "shared_selection_triton_exact_2")
+        qd = q.to(dev)
+        kd = k.to(dev).repeat_interleave(G, 1)
+        vd = v.to(dev).repeat_interleave(G, 1)
 
-    def step():
-        return mod.shared_pi_attention(qd, kd, vd, taud, invf, pos_scale=geo["pos_scale"],
-                                       pct=c["pct"], rope_scale=geo["rope_scale"], tile=c["T"],
-                                       k_max=c["k_max"])
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s0.record()
-    for _ in range(args.steps):
-        step()
-    s1.record()
-    torch.cuda.synchronize()
-    ms = s0.elapsed_time(s1) / args.steps
-    line.update({"value": c["B"] * c["S"] / (ms / 1e3), "ms_per_step": ms, "n_gpus": 1,
+        def step():
+            return mod.shared_pi_attention(qd, kd, vd, taud, ia, pos_scale=geo["pos_scale"],
+                                           pct=c["pct"], rope_scale=geo["rope_scale"],
+                                           tile=c["T"], k_max=c["k_max"])
+        ms = _time_calls(step, args.warmup, args.steps)
+        est = False
+        if not args.no_compare:
+            with _Capture(mod, "_build_sets") as cap:
+                r = step()
+            torch.cuda.synchronize()
+            stats = {"shared_size": r[1], "kept_size": r[2]}
+            votes = cap.args[0]
+            del kd, vd
+            extra["vs_this_build"] = _compare_with_reference(
+                c, qd, k.to(dev), v.to(dev), tau, geo, geo_c, r[0], votes, stats)
+    else:
+        n_units = max(1, args.ref_heads)
+        units = [(b, h) for b in range(B) for h in range(H)]
+        step_idx = [int(i * (len(units) - 1) / max(n_units - 1, 1)) for i in range(n_units)]
+        picks = [units[i] for i in step_idx]
+        per = []
+        for b, h in picks:
+            qd = q[b:b + 1, h:h + 1].to(dev)
+            kd = k[b:b + 1, h // G:h // G + 1].to(dev)
+            vd = v[b:b + 1, h // G:h // G + 1].to(dev)
+            t1 = taud[h:h + 1]
+            if args.variant == "shared":
+                mod = __import__("shared_selection_triton_hybrid_exact")
+                fn = lambda: mod.shared_pi_attention(  # noqa: E731
+                    qd, kd, vd, t1, ia, geo["pos_scale"], geo["rope_scale"], ic,
+                    geo_c["pos_scale"], geo_c["rope_scale"], pct=c["pct"], tile=c["T"],
+                    k_max=c["k_max"])
+            elif args.variant == "pq_union":
+                mod = __import__("shared_selection_triton_perquery")
+                fn = lambda: mod.shared_pq_attention(  # noqa: E731
+                    qd, kd, vd, t1, ia, ic, geo["pos_scale"], geo["rope_scale"],
+                    k_max=c["k_max"], select_score="expmass")
+            else:
+                mod = __import__("pqstream_kernel")
+                fn = lambda: mod.pqstream_attention(  # noqa: E731
+                    qd, kd, vd, t1, ia, ic, geo["pos_scale"], geo["rope_scale"], block_n=32)
+            per.append(_time_calls(fn, 1, max(1, min(args.steps, 2))))
+            del qd, kd, vd
+            torch.cuda.empty_cache()
+        ms = statistics.mean(per) * B * H
+        est = True
+        extra["per_head_ms"] = per
+        extra["sampled_units"] = [list(x) for x in picks]
+        extra["extrapolated"] = True
+        extra["how"] = "per-(batch, head) calls of the reference op, mean x batch x heads"
+    line.update({"value": B * N / (ms / 1e3), "ms_per_step": ms, "n_gpus": 1,
                  "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
                  "dtype": "bf16 inputs (reference Triton: fp32 RoPE, tl.dot)",
-                 "config": workload_desc(c, args, 1),
+                 "config": workload_desc(c, args, 1), "extrapolated": est,
                  "source": "unmodified reference modules installed by pip into baseline/_ref"})
+    line.update(extra)
     emit(line)
 
 
