@@ -92,16 +92,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: returns false (and raises the CTA-wide abort flag and the global error code)
 // when the barrier phase has not completed within `limit_ns` or when another role aborted.
+// Limits below 1 ms (test-only: they make waits run out on purpose) poll with the
+// non-blocking test_wait and read the clock on every poll, so any phase that is not already
+// complete when first tested expires; normal limits use the suspending try_wait and read the
+// clock every 256 polls.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* err, int code, uint64_t limit_ns = 4000000000ull) {
-  if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = globaltimer_ns();
+  const bool fine = limit_ns < 1000000ull;
+  if (fine ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
   uint32_t it = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++it & 255u) == 0u) {
+    if (fine ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity)) return true;
+    if (fine || (++it & 255u) == 0u) {
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > limit_ns) {
         *abort_flag = 1;

@@ -99,7 +99,8 @@ def test_full_length_shared_sampled_tiles(idx, b, kv):
     nt = (N + T - 1) // T
     chosen = st["chosen"][0].cpu().numpy()
     fallback = [int(t) for t in np.nonzero((chosen[0] > 0) & (chosen[0] < 30))[0][:3]]
-    if idx == 2:
+    if idx == 2 and kv == 0:
+        # the dense query clusters sit in kv head 0's q heads: 25 / 20 % fallback tiles
         assert fallback, "config 2's dense clusters drive the 25 / 20 % fallback"
     tiles = sample_tiles(nt, fallback, seed=idx * 10 + kv)
     sm = 1.0 / math.sqrt(D)
