@@ -405,6 +405,42 @@ int sta_pq_stream_forward(const sta_forward_args* a, void* workspace, size_t wor
                           void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Dense Dual Chunk Attention prefill (replaces dca_forward's prefill, dca_kernel.py:447-487:
+ * the intra / succ / inter flash-attention blocks and their log-sum-exp merge, :292-366).
+ * Every query attends to all its causal keys; keys are rotated at j mod L (L = chunk_size -
+ * local_window), a query at the intra position for keys of its own chunk, the succ position
+ * min(L + i mod L, chunk_size) for the previous chunk and the inter position
+ * min(2L - 1, chunk_size) for older chunks, cos / sin multiplied by rope_scale (ChunkLlama's
+ * mscale); one softmax over all of them.  chunk_size == 0: plain causal attention with RoPE at
+ * the true positions.  L must be a multiple of 128.  bf16 inputs: one bf16 product per score
+ * and for P.V (as flash-attention on bf16); f32 inputs: hi / lo bf16 pieces, three products.
+ * q_pos_base (multiple of 128): q holds the queries at positions q_pos_base .. n-1, out
+ * (batch*n_heads, n - q_pos_base, d); k / v hold keys 0 .. n-1 (a decode step is the last row
+ * of the slab that holds it).
+ * ------------------------------------------------------------------------------------- */
+typedef struct sta_dca_args {
+  const void* q; int64_t q_stride_h; int64_t q_stride_n;    /* (batch*n_heads, n - q_pos_base, d) */
+  const void* k; int64_t k_stride_h; int64_t k_stride_n;    /* raw (batch*n_kv_heads, n, d) */
+  const void* v; int64_t v_stride_h; int64_t v_stride_n;
+  void* out;               /* (batch*n_heads, n - q_pos_base, d), dtype, contiguous */
+  int32_t dtype;
+  int64_t batch;
+  int64_t n_heads;
+  int64_t n_kv_heads;
+  int64_t n;
+  int32_t d;               /* 64 or 128 */
+  const float* inv_freq;   /* (d/2,) */
+  float rope_scale;        /* mscale on cos / sin */
+  float sm_scale;
+  int32_t chunk_size;      /* s; 0 = plain causal RoPE attention */
+  int32_t local_window;    /* w */
+  int64_t q_pos_base;
+} sta_dca_args;
+
+size_t sta_dca_workspace_bytes(const sta_dca_args* a);
+int sta_dca_forward(const sta_dca_args* a, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * Allocation-free variant of sta_shared_forward.  No counterpart in the reference: it exists
  * for hosts that may not allocate device memory themselves (plugins whose runtime owns every
  * device allocation, code under a fixed pre-reserved memory budget).  Scratch comes from a

@@ -128,6 +128,16 @@ class DecodeArgs(ctypes.Structure):
 DECODE = {"pi": 0, "rank": 1, "stream": 2, "chunk": 3}
 
 
+class DcaArgs(ctypes.Structure):
+    _fields_ = [("q", c_vp), ("q_stride_h", c_i64), ("q_stride_n", c_i64),
+                ("k", c_vp), ("k_stride_h", c_i64), ("k_stride_n", c_i64),
+                ("v", c_vp), ("v_stride_h", c_i64), ("v_stride_n", c_i64),
+                ("out", c_vp), ("dtype", c_i32), ("batch", c_i64), ("n_heads", c_i64),
+                ("n_kv_heads", c_i64), ("n", c_i64), ("d", c_i32), ("inv_freq", c_vp),
+                ("rope_scale", c_f32), ("sm_scale", c_f32), ("chunk_size", c_i32),
+                ("local_window", c_i32), ("q_pos_base", c_i64)]
+
+
 # every symbol include/sta.h declares (checked by the CPU test suite)
 EXPORTED = ["sta_last_error", "sta_version", "sta_tri_head_stride", "sta_rope_split",
             "sta_select", "sta_build_sets", "sta_build_sets_pq", "sta_gather_attend",
@@ -136,7 +146,8 @@ EXPORTED = ["sta_last_error", "sta_version", "sta_tri_head_stride", "sta_rope_sp
             "sta_pq_stream_workspace_bytes", "sta_pq_stream_forward", "sta_device_error",
             "sta_shared_forward_static", "sta_build_sets_chunk", "sta_chunk_workspace_bytes",
             "sta_chunk_forward", "sta_rope_split_dca", "sta_rope_table", "sta_tri_head_stride_q",
-            "sta_decode_workspace_bytes", "sta_decode_forward"]
+            "sta_decode_workspace_bytes", "sta_decode_forward", "sta_dca_workspace_bytes",
+            "sta_dca_forward"]
 
 _lib = None
 
@@ -182,6 +193,10 @@ def lib():
     L.sta_decode_workspace_bytes.argtypes = [ctypes.POINTER(DecodeArgs)]
     L.sta_decode_forward.restype = ctypes.c_int
     L.sta_decode_forward.argtypes = [ctypes.POINTER(DecodeArgs), c_vp, ctypes.c_size_t, c_vp]
+    L.sta_dca_workspace_bytes.restype = ctypes.c_size_t
+    L.sta_dca_workspace_bytes.argtypes = [ctypes.POINTER(DcaArgs)]
+    L.sta_dca_forward.restype = ctypes.c_int
+    L.sta_dca_forward.argtypes = [ctypes.POINTER(DcaArgs), c_vp, ctypes.c_size_t, c_vp]
     L.sta_shared_forward_static.restype = ctypes.c_int
     L.sta_shared_forward_static.argtypes = [ctypes.POINTER(ForwardArgs), c_vp]
     L.sta_device_error.restype = ctypes.c_int

@@ -520,6 +520,45 @@ def compact_from_dense(dense: torch.Tensor, tile: int):
     return torch.cat(parts).contiguous()
 
 
+def dca_dense(q, k, v, inv_freq, *, chunk_size, local_window, rope_scale=1.0, sm_scale=None,
+              q_pos_base=0):
+    """Dense Dual Chunk Attention prefill (sta_dca_forward): q (Z,H,Nq,D), k / v (Z,Hkv,N,D)
+    raw, Nq = N - q_pos_base.  chunk_size == 0: plain causal attention with RoPE at the true
+    positions.  Returns out (Z,H,Nq,D) in q's dtype."""
+    q_pos_base = int(q_pos_base)
+    Z, H, Hk, N, D = _check_inputs(q, k, v, q_pos_base)
+    dev = q.device
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    invf = _dev_f32(inv_freq, dev)
+    if invf.numel() != D // 2:
+        raise ValueError("inv_freq must have head_dim/2 entries")
+    out = torch.empty((Z, H, N - q_pos_base, D), dtype=q.dtype, device=dev)
+    lib = L.lib()
+    ws = None
+    for b in range(Z):
+        qb, kb, vb = _rows(q[b]), _rows(k[b]), _rows(v[b])
+        a = L.DcaArgs()
+        a.q, a.q_stride_h, a.q_stride_n = qb.data_ptr(), qb.stride(0), qb.stride(1)
+        a.k, a.k_stride_h, a.k_stride_n = kb.data_ptr(), kb.stride(0), kb.stride(1)
+        a.v, a.v_stride_h, a.v_stride_n = vb.data_ptr(), vb.stride(0), vb.stride(1)
+        a.out = out[b].data_ptr()
+        a.dtype = dtype_code(q.dtype)
+        a.batch, a.n_heads, a.n_kv_heads, a.n, a.d = 1, H, Hk, N, D
+        a.inv_freq = invf.data_ptr()
+        a.rope_scale, a.sm_scale = float(rope_scale), float(sm_scale)
+        a.chunk_size, a.local_window = int(chunk_size), int(local_window)
+        a.q_pos_base = q_pos_base
+        nbytes = lib.sta_dca_workspace_bytes(ctypes.byref(a))
+        if nbytes == 0:
+            L.check(1, "sta_dca_workspace_bytes")
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        L.check(lib.sta_dca_forward(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()),
+                                    ctypes.c_size_t(ws.numel()), _stream()), "sta_dca_forward")
+    return out
+
+
 def device_error() -> int:
     """Synchronise the current stream and return (and clear) the device error word of the
     bounded waits: 0 when no wait expired since the last read."""

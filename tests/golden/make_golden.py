@@ -152,6 +152,43 @@ def gen_cfg0(case):
                           overflow=res[4], votes=cap.args[0], idx=sets[0]))
 
 
+def gen_dca_dense(case, H, Hkv, N, D, chunk_size, pretrain_len, local_window, seed):
+    """The reference's dense DCA attention (dca_forward prefill, dca_kernel.py:447-487) on a
+    one-layer random-init Llama patched by the reference's own patch_model_with_dca.  On the
+    CPU the reference takes its PyTorch block path (_fa_block's fallback, fp32) and merges the
+    three blocks by log-sum-exp.  Stores the layer's raw q / k / v (projection outputs, before
+    any rotation) and the attention output (the input of o_proj)."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    dca = __import__("dca_kernel")
+    torch.manual_seed(seed)
+    cfg = LlamaConfig(hidden_size=H * D, num_attention_heads=H, num_key_value_heads=Hkv,
+                      head_dim=D, num_hidden_layers=1, intermediate_size=64, vocab_size=64,
+                      max_position_embeddings=pretrain_len, rope_theta=10000.0)
+    model = LlamaForCausalLM(cfg).float().eval()
+    originals = dca.patch_model_with_dca(model, chunk_size, pretrain_len, local_window)
+    attn = model.model.layers[0].self_attn
+    cap = {}
+    hooks = [attn.q_proj.register_forward_hook(lambda m, i, o: cap.__setitem__("q", o)),
+             attn.k_proj.register_forward_hook(lambda m, i, o: cap.__setitem__("k", o)),
+             attn.v_proj.register_forward_hook(lambda m, i, o: cap.__setitem__("v", o)),
+             attn.o_proj.register_forward_pre_hook(lambda m, i: cap.__setitem__("out", i[0]))]
+    x = torch.randn(1, N, H * D) * 2.0
+    with torch.no_grad():
+        attn(x, position_embeddings=None, attention_mask=None)
+    for h in hooks:
+        h.remove()
+    dca.unpatch_model(originals)
+    q = cap["q"].view(1, N, H, D).transpose(1, 2)[0]
+    k = cap["k"].view(1, N, Hkv, D).transpose(1, 2)[0]
+    v = cap["v"].view(1, N, Hkv, D).transpose(1, 2)[0]
+    out = cap["out"].view(1, N, H, D).transpose(1, 2)[0]
+    inv_freq = 1.0 / (10000 ** (torch.arange(0, D, 2).float() / D))
+    meta = dict(kind="dca_dense", H=H, Hkv=Hkv, N=N, D=D, chunk_size=chunk_size,
+                pretrain_len=pretrain_len, local_window=local_window, seed=seed,
+                mscale=dca.get_mscale(N / pretrain_len), sm_scale=float(attn.scaling))
+    save(case, meta, dict(q=q, k=k, v=v, out=out, inv_freq=inv_freq))
+
+
 def gen_pq(case, H, N, D, k_max, seed, dtype, select_score="expmass", geom="pi",
            pos_scale=1.0, tau_val=5.0, planted=8):
     mod = __import__("shared_selection_triton_perquery")
@@ -354,6 +391,8 @@ def main():
                2048, 18, f32, tau_val=1.0)
     # benchmark config 0 at its own shape
     gen_cfg0("config0_f32")
+    # dense Dual Chunk Attention (dca_kernel.py), GQA, three chunk relations, ragged tail
+    gen_dca_dense("dca_dense_gqa_f32", 4, 2, 700, 64, 320, 512, 64, 61)
     # PQ-Union: overflow-forcing k_max, expmass and freq ranking, yarn select geometry
     gen_pq("pq_union_expmass_f32", 2, 288, 64, 160, 21, f32)
     gen_pq("pq_union_freq_f32", 2, 256, 64, 4096, 22, f32, select_score="freq")

@@ -36,7 +36,7 @@ def test_struct_layouts_match_header_order():
                        ("sta_build_pq_args", L.BuildPQArgs), ("sta_attend_args", L.AttendArgs),
                        ("sta_pqstream_args", L.PQStreamArgs), ("sta_forward_args", L.ForwardArgs),
                        ("sta_build_chunk_args", L.BuildChunkArgs),
-                       ("sta_decode_args", L.DecodeArgs)):
+                       ("sta_decode_args", L.DecodeArgs), ("sta_dca_args", L.DcaArgs)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), src, re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
         fields = re.findall(r"\**\s*([A-Za-z_0-9]+)\s*;", body)

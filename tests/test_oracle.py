@@ -361,3 +361,19 @@ def test_oracle_matches_reference_at_config0():
     for h, t in zip(*np.nonzero(clean)):
         r0, r1 = t * T, min((t + 1) * T, N)
         assert np.abs(o[0][h, r0:r1] - z["out"][h, r0:r1]).max() <= 1e-4, (h, t)
+
+
+def test_oracle_dense_dca_matches_reference():
+    """Dense DCA (the reference's dca_forward prefill on a one-layer Llama, its three blocks
+    merged by log-sum-exp) equals one softmax over all causal keys with per-relation query
+    rotations."""
+    import json
+    z = np.load(os.path.join(HERE, "golden", "dca_dense_gqa_f32.npz"))
+    meta = json.loads(str(z["meta"]))
+    G = meta["H"] // meta["Hkv"]
+    k = np.repeat(z["k"], G, 0)
+    v = np.repeat(z["v"], G, 0)
+    o = oracle.dca_dense_attention(z["q"], k, v, meta["chunk_size"], meta["local_window"],
+                                   z["inv_freq"], meta["mscale"], meta["sm_scale"])
+    err = np.abs(o - z["out"])
+    assert err.max() <= 1e-4, err.max()
