@@ -48,7 +48,9 @@ def parse():
                          "reference_gpu: the reference's own Triton kernels on this GPU, from "
                          "the unmodified install in baseline/_ref")
     ap.add_argument("--config", type=int, default=2)
-    ap.add_argument("--variant", choices=["shared", "pq_union", "pq_stream"], default="shared")
+    ap.add_argument("--variant", choices=["shared", "pq_union", "pq_stream", "dca_dense"],
+                    default="shared",
+                    help="dca_dense: the dense Dual Chunk Attention prefill (config 3 geometry)")
     ap.add_argument("--seq-len", type=int, default=None, help="override S (profiling only)")
     ap.add_argument("--heads", type=int, default=None, help="override q heads (profiling only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -671,6 +673,51 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+def run_gpu_dca(args):
+    """--variant dca_dense: the dense Dual Chunk Attention prefill (sta_dca_forward, the
+    reference's dca_forward core) on the config's inputs and DCA geometry (config 3: chunk
+    6144, local window 1024, mscale of the sequence length), 1 GPU, CUDA events."""
+    import torch
+    from sta import core
+    q, k, v, tau, geo, geo_c, c = workload(args)
+    if not geo.get("dca"):
+        raise SystemExit("--variant dca_dense needs a DCA geometry (config 3)")
+    dev = torch.device("cuda", 0)
+    B, H, N, D = c["B"], c["H"], c["S"], c["D"]
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    s_, w_ = geo["dca"]
+
+    def step():
+        return core.dca_dense(qd, kd, vd, geo["inv_freq"], chunk_size=s_, local_window=w_,
+                              rope_scale=geo["rope_scale"])
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    pk, pk_kind = peaks()
+    flops = 4 * D * B * H * N * (N + 1) / 2     # S = Q.K^T and O = P.V over causal pairs
+    achieved = flops / (ms / 1e3) / 1e12
+    peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
+    emit({"metric": METRIC, "value": B * N / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+          "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+          "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+          "data": "synthetic (seeded generator sta.synth, BASELINE config shapes)",
+          "config": dict(workload_desc(c, args, 1), chunk_size=s_, local_window=w_),
+          "clocks": clk.summary(), "gpu_launches": args.steps * B * 6,
+          "roofline": {"kernel": "dca_dense_kernel (tcgen05 S = Q.K^T, O = P.V, P in TMEM)",
+                       "bound": "tensor", "achieved": achieved, "peak": peak,
+                       "unit": "TFLOP/s", "frac": achieved / peak,
+                       "peak_kind": f"{pk_kind} bf16 sustained",
+                       "algorithmic_flops_per_launch": flops / B}})
+
+
 def run_decode(args):
     """--decode: one decode step of the variant's rule (shared -> PI cap + reposition, pq_union
     -> dense ranks, pq_stream -> streamed positions) for the config's last position against the
@@ -756,6 +803,8 @@ def main():
         os.dup2(2, 1)
     if args.decode:
         run_decode(args)
+    elif args.variant == "dca_dense" and args.impl == "sta":
+        run_gpu_dca(args)
     elif args.impl == "reference_gpu":
         run_reference_gpu(args)
     elif args.impl == "reference":

@@ -412,8 +412,9 @@ int sta_pq_stream_forward(const sta_forward_args* a, void* workspace, size_t wor
  * min(L + i mod L, chunk_size) for the previous chunk and the inter position
  * min(2L - 1, chunk_size) for older chunks, cos / sin multiplied by rope_scale (ChunkLlama's
  * mscale); one softmax over all of them.  chunk_size == 0: plain causal attention with RoPE at
- * the true positions.  L must be a multiple of 128.  bf16 inputs: one bf16 product per score
- * and for P.V (as flash-attention on bf16); f32 inputs: hi / lo bf16 pieces, three products.
+ * the true positions.  L must be a multiple of 128.  Scores: three bf16 products of hi / lo
+ * pieces of the fp32-rotated rows; P.V: P rounded to bf16 times V for bf16 inputs (as the
+ * reference), hi / lo pieces of P and V (three products) for f32 inputs.
  * q_pos_base (multiple of 128): q holds the queries at positions q_pos_base .. n-1, out
  * (batch*n_heads, n - q_pos_base, d); k / v hold keys 0 .. n-1 (a decode step is the last row
  * of the slab that holds it).

@@ -22,9 +22,11 @@
 //              three TMEM slots, then O += P.V with P read from TMEM (the A operand) and V^T
 //              from shared memory; S of block g+1 is issued before P.V of block g so the
 //              softmax of one block overlaps the tensor work of the next.
-// Numerics: bf16 inputs score with one bf16 product of the fp32-rotated, bf16-rounded rows
-// (the reference runs flash-attention on bf16 rows) and multiply P (bf16) by V (bf16); fp32
-// inputs use hi / lo bf16 pieces: three products for S and for P.V (~2^-16 relative).
+// Numerics: scores from the fp32-rotated rows split into hi / lo bf16 pieces, three products
+// (~2^-16 relative: a single bf16 product of the rounded rows, as flash-attention on bf16 rows
+// computes it, moves outputs by up to ~5e-2 on these inputs).  P.V: bf16 inputs multiply P
+// rounded to bf16 by V (bf16, exact), as the reference does; fp32 inputs split P and V into
+// hi / lo pieces as well (three products).
 // Every wait is bounded; on expiry the kernel records STA_ERR_TIMEOUT and unwinds.
 #include <cstdio>
 
@@ -44,13 +46,13 @@ constexpr int kChunk = 128 * 128; // one 128-row x 64-bf16 swizzled chunk (16 KB
 template <int D, bool F32>
 struct DCfg {
   static constexpr int NC = D / 64;                   // 64-column chunks of a row of Q / K
-  static constexpr int NP = F32 ? 2 : 1;              // bf16 pieces (hi [, lo])
-  static constexpr int Q_BYTES = NP * NC * kChunk;
-  static constexpr int K_STAGE = NP * NC * kChunk;    // one 128-key block, all pieces
+  static constexpr int NPV = F32 ? 2 : 1;             // bf16 pieces of P and V^T
+  static constexpr int Q_BYTES = 2 * NC * kChunk;     // Q hi + lo
+  static constexpr int K_STAGE = 2 * NC * kChunk;     // one 128-key block, hi + lo
   static constexpr int VT_CHUNK = D * 128;            // D rows (d) x 64 keys, swizzled
-  static constexpr int V_STAGE = NP * 2 * VT_CHUNK;   // one 128-key block of V^T, all pieces
+  static constexpr int V_STAGE = NPV * 2 * VT_CHUNK;  // one 128-key block of V^T, all pieces
   static constexpr int NSK = F32 ? 1 : 2;
-  static constexpr int NSV = F32 ? 1 : 2;
+  static constexpr int NSV = 1;
   static constexpr int SMEM = 1024 + Q_BYTES + NSK * K_STAGE + NSV * V_STAGE + 512;
   static constexpr int kThreads = 192;
 };
@@ -62,7 +64,6 @@ struct DParams {
   int64_t Nq;        // query rows held (positions qbase .. N-1)
   int64_t qbase;     // multiple of 128
   int qb0, nqb;
-  int qc;            // query blocks per scheduling chunk
   int64_t dca_L;     // chunk_len (multiple of 128), 0: plain causal
   float c_log2;      // sm_scale * log2(e)
   void* out;         // (BH, Nq, D) in the input dtype
@@ -77,16 +78,11 @@ __device__ __forceinline__ int dplane(const DParams& p, int qb, int kb) {
   return rel <= 0 ? 0 : (rel == 1 ? 1 : 2);
 }
 
-// Longest-first in chunks of qc query blocks, head-major inside a chunk (the items running at
-// the same time share one kv group's K / V in L2).
+// Longest-first: the largest query blocks of every head first.
 __device__ __forceinline__ void ditem(int64_t w, const DParams& p, int64_t& bh, int& qb,
                                       int64_t& kvh) {
-  const int64_t per_chunk = (int64_t)p.qc * p.BH;
-  const int c = (int)(w / per_chunk);
-  const int64_t r = w - (int64_t)c * per_chunk;
-  const int qcount = min(p.qc, p.nqb - c * p.qc);
-  bh = r / qcount;
-  qb = p.nqb - 1 - (c * p.qc + (int)(r % qcount)) + p.qb0;
+  qb = p.nqb - 1 - (int)(w / p.BH) + p.qb0;
+  bh = w % p.BH;
   const int G = p.H / p.Hkv;
   kvh = (bh / p.H) * p.Hkv + (bh % p.H) / G;
 }
@@ -210,7 +206,7 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
             const int qrow = (qb - p.qb0) * BM;
             for (int c = 0; c < C::NC; ++c) {
               tma_load_3d(sQ + c * kChunk, &tm_qhi, q_full, c * 64, qrow, z);
-              if (F32) tma_load_3d(sQ + (C::NC + c) * kChunk, &tm_qlo, q_full, c * 64, qrow, z);
+              tma_load_3d(sQ + (C::NC + c) * kChunk, &tm_qlo, q_full, c * 64, qrow, z);
             }
             ++qloads;
             cur = plane;
@@ -226,7 +222,7 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
             mbar_arrive_expect_tx(k_full + s, C::K_STAGE);
             for (int c = 0; c < C::NC; ++c) {
               tma_load_3d(st + c * kChunk, &tm_khi, k_full + s, c * 64, kb * BN, (int)kvh);
-              if (F32) tma_load_3d(st + (C::NC + c) * kChunk, &tm_klo, k_full + s, c * 64, kb * BN, (int)kvh);
+              tma_load_3d(st + (C::NC + c) * kChunk, &tm_klo, k_full + s, c * 64, kb * BN, (int)kvh);
             }
             ++kc;
           }
@@ -333,14 +329,12 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
               const uint32_t off = c * kChunk + kk * 32;
               const uint64_t qh = sw128_kmajor_desc(q_addr + off);
               const uint64_t kh = sw128_kmajor_desc(st + off);
+              const uint64_t ql = sw128_kmajor_desc(q_addr + C::NC * kChunk + off);
+              const uint64_t kl = sw128_kmajor_desc(st + C::NC * kChunk + off);
               umma_bf16(d_s, qh, kh, idesc_s, acc);
               acc = 1;
-              if (F32) {
-                const uint64_t ql = sw128_kmajor_desc(q_addr + C::NC * kChunk + off);
-                const uint64_t kl = sw128_kmajor_desc(st + C::NC * kChunk + off);
-                umma_bf16(d_s, ql, kh, idesc_s, 1);
-                umma_bf16(d_s, qh, kl, idesc_s, 1);
-              }
+              umma_bf16(d_s, ql, kh, idesc_s, 1);
+              umma_bf16(d_s, qh, kl, idesc_s, 1);
             }
           }
           umma_commit(k_empty + s);
@@ -398,32 +392,37 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
           x[j] = keep ? x[j] * p.c_log2 : -INFINITY;
           mx = fmaxf(mx, x[j]);
         }
-        if (mx > m_used + 8.f) {
-          if (kb > 0 && m_used > -INFINITY) {
-            // O holds the blocks so far at m_used: rescale it to mx after the last P.V landed
-            const uint32_t gp = g - 1;
-            int bad2 = 0;
-            if (lane == 0) bad2 = !mbar_wait(pv_done + gp % NS, (gp / NS) & 1, s_abort, p.err,
-                                              kErrTimeoutAcc, p.limit_ns);
-            if (__shfl_sync(0xffffffffu, bad2, 0)) {
-              ok = false;
-              continue;
-            }
-            tc_fence_after();
-            const float f = exp2f(m_used - mx);
-#pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-              float v[32];
-              tmem_ld32(lane_addr + OCOL + c * 32, v);
-              tmem_wait_ld();
-              uint32_t u[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) u[j] = __float_as_uint(v[j] * f);
-              tmem_st32(lane_addr + OCOL + c * 32, u);
-            }
-            l *= f;
+        // Lazy rescale: only when some row's max grew by more than 2^8.  The TMEM accesses are
+        // warp-collective, so the decision is taken per warp: every row of the warp then moves
+        // to its own new max (factor <= 1; 0 for a row without earlier contributions).
+        const float m_new = fmaxf(m_used, mx);
+        const bool want = mx > m_used + 8.f;
+        if (kb == 0) {
+          m_used = m_new;
+        } else if (__any_sync(0xffffffffu, want)) {
+          // O holds the blocks so far at m_used: rescale once the last P.V has landed
+          const uint32_t gp = g - 1;
+          int bad2 = 0;
+          if (lane == 0) bad2 = !mbar_wait(pv_done + gp % NS, (gp / NS) & 1, s_abort, p.err,
+                                            kErrTimeoutAcc, p.limit_ns);
+          if (__shfl_sync(0xffffffffu, bad2, 0)) {
+            ok = false;
+            continue;
           }
-          m_used = mx;
+          tc_fence_after();
+          const float f = m_used > -INFINITY ? exp2f(m_used - m_new) : 0.f;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float v[32];
+            tmem_ld32(lane_addr + OCOL + c * 32, v);
+            tmem_wait_ld();
+            uint32_t u[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) u[j] = __float_as_uint(v[j] * f);
+            tmem_st32(lane_addr + OCOL + c * 32, u);
+          }
+          l *= f;
+          m_used = m_new;
         }
         // P = 2^(x - m_used) as bf16 pairs (key 2w in the low half of column w), 64 keys at a
         // time; fp32 inputs also store the residual lo pieces 64 columns further
@@ -697,9 +696,6 @@ int sta_dca_forward(const sta_dca_args* a, void* workspace, size_t workspace_byt
     p.limit_ns = 4000000000ull;
     const int64_t total = H * p.nqb;
     const int grid = (int)(total < nsm ? total : nsm);
-    p.qc = (int)((grid + (H / Hk) - 1) / (H / Hk));
-    if (p.qc > p.nqb) p.qc = p.nqb;
-    if (p.qc < 1) p.qc = 1;
     cudaError_t e;
     if (D == 128) e = f32 ? launch_dca_kernel<128, true>(m, p, grid, st) : launch_dca_kernel<128, false>(m, p, grid, st);
     else e = f32 ? launch_dca_kernel<64, true>(m, p, grid, st) : launch_dca_kernel<64, false>(m, p, grid, st);

@@ -60,7 +60,6 @@ struct Params {
   int qb0;              // qbase / BM
   int T;
   int nqb;              // local query blocks
-  int qc;               // query blocks per scheduling chunk (item order, see decode_item)
   int npass;
   int wmode;
   float sm_scale;
@@ -114,18 +113,10 @@ __device__ __forceinline__ float raw_threshold(float thr, float sm) {
   return x;
 }
 
-// Item order: query blocks in descending chunks of qc blocks (longest first), and inside a
-// chunk head-major, so that the items that run at the same time (consecutive w) belong to few
-// q heads -- about one kv group when qc = grid / G -- and their K blocks stay in L2 while every
-// CTA of the group streams them.
 __device__ __forceinline__ void decode_item(int64_t w, const Params& p, int64_t& bh, int& qb,
                                             int64_t& kvh) {
-  const int64_t per_chunk = (int64_t)p.qc * p.BH;
-  const int c = (int)(w / per_chunk);
-  const int64_t r = w - (int64_t)c * per_chunk;
-  const int qcount = min(p.qc, p.nqb - c * p.qc);
-  bh = r / qcount;
-  qb = p.nqb - 1 - (c * p.qc + (int)(r % qcount)) + p.qb0;  // absolute query block
+  qb = p.nqb - 1 - (int)(w / p.BH) + p.qb0;  // absolute query block
+  bh = w % p.BH;
   const int G = p.H / p.Hkv;
   kvh = (bh / p.H) * p.Hkv + (bh % p.H) / G;
 }
@@ -566,12 +557,6 @@ int launch_select(const sta_select_args* a, cudaStream_t stream) {
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   const int64_t total = BH * p.nqb;
   const int grid = (int)(total < nsm ? total : nsm);
-  {
-    const int G = (int)(a->n_heads / a->n_kv_heads);
-    p.qc = (grid + G - 1) / G;  // one kv group's q heads fill the grid
-    if (p.qc > p.nqb) p.qc = p.nqb;
-    if (p.qc < 1) p.qc = 1;
-  }
   cudaError_t e;
   if (a->d == 128) {
     e = cudaFuncSetAttribute(select_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
