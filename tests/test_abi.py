@@ -160,3 +160,20 @@ def test_static_entry_passes_through_argument_codes_without_gpu():
     a.n = 0
     a.pos_scale_a = a.pos_scale_c = 0.125
     assert lib.sta_shared_forward_static(ctypes.byref(a), None) == 0
+
+
+def test_dca_arguments_checked_without_gpu():
+    """The dense DCA entry validates before touching the device: chunk_len must be a multiple
+    of 128; an empty problem is a no-op."""
+    lib = L.lib()
+    a = L.DcaArgs()
+    for f in ("q", "k", "v", "out", "inv_freq"):
+        setattr(a, f, 256)
+    a.dtype, a.batch, a.n_heads, a.n_kv_heads, a.n, a.d = 1, 1, 4, 2, 1000, 128
+    a.chunk_size, a.local_window, a.rope_scale, a.sm_scale = 320, 100, 1.0, 0.088
+    assert lib.sta_dca_workspace_bytes(ctypes.byref(a)) == 0
+    assert b"multiple of 128" in lib.sta_last_error()
+    a.local_window = 64
+    assert lib.sta_dca_workspace_bytes(ctypes.byref(a)) > 0
+    a.n = 0
+    assert lib.sta_dca_forward(ctypes.byref(a), None, 0, None) == 0
