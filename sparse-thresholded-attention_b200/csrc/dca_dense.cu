@@ -87,34 +87,6 @@ __device__ __forceinline__ void ditem(int64_t w, const DParams& p, int64_t& bh, 
   kvh = (bh / p.H) * p.Hkv + (bh % p.H) / G;
 }
 
-// D[tmem] (+)= A[tmem] * B[smem]^T (kind::f16): A = P (M = 128 rows in the lanes, 16 keys per
-// MMA packed two bf16 per column), B = V^T (N = d rows, keys contiguous).
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
-                                        uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
-      ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
-      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),
-        "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]),
-        "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]),
-        "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
-        "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_wait_st() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // a -> low half, b -> high half
   return *reinterpret_cast<const uint32_t*>(&h);
@@ -273,12 +245,12 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
         for (int kk = 0; kk < 8; ++kk) {  // 16 keys per MMA
           const uint32_t voff = (kk >> 2) * C::VT_CHUNK + (kk & 3) * 32;
           const uint64_t vh = sw128_kmajor_desc(st + voff);
-          umma_ts(tmem_base + OCOL, a0 + kk * 8, vh, idesc_o, acc);
+          umma_bf16_ts(tmem_base + OCOL, a0 + kk * 8, vh, idesc_o, acc);
           acc = 1;
           if (F32) {
             const uint64_t vl = sw128_kmajor_desc(st + 2 * C::VT_CHUNK + voff);
-            umma_ts(tmem_base + OCOL, a0 + 64 + kk * 8, vh, idesc_o, 1);  // P lo . V hi
-            umma_ts(tmem_base + OCOL, a0 + kk * 8, vl, idesc_o, 1);       // P hi . V lo
+            umma_bf16_ts(tmem_base + OCOL, a0 + 64 + kk * 8, vh, idesc_o, 1);  // P lo . V hi
+            umma_bf16_ts(tmem_base + OCOL, a0 + kk * 8, vl, idesc_o, 1);       // P hi . V lo
           }
         }
         umma_commit(v_empty + s);

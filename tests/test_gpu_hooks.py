@@ -60,22 +60,58 @@ def test_hook_prefill_and_decode_match_dense_at_tau_inf(modname):
         ml.LlamaAttention.forward = orig_forward
 
 
-def test_hook_threshold_selects_and_runs():
-    """A finite tau selects (kept sets smaller than the causal count) and stays finite."""
+def test_hook_threshold_selects_and_matches_oracle():
+    """At a finite tau the hook's attention output (the input of o_proj) equals the oracle's
+    shared thresholded attention of the layer's own q / k / v (captured at the projections),
+    run on the device's Kernel A votes with the geometry the hook freezes at prefill."""
+    import numpy as np
     import transformers.models.llama.modeling_llama as ml
+    from conftest import oracle
+    from sta import core
     from sta import shared_selection_exact_2 as st
+    from sta.core import Geometry
     orig_forward = ml.LlamaAttention.forward
     model = tiny_llama(seed=3)
-    ids = torch.randint(0, 211, (1, 512), generator=torch.Generator().manual_seed(2)).cuda()
+    N, H, Hk, D = 512, 4, 2, 64
+    ids = torch.randint(0, 211, (1, N), generator=torch.Generator().manual_seed(2)).cuda()
+    sa = model.model.layers[1].self_attn
+    cap = {}
+    hooks = [sa.q_proj.register_forward_hook(lambda m, i, o: cap.__setitem__("q", o)),
+             sa.k_proj.register_forward_hook(lambda m, i, o: cap.__setitem__("k", o)),
+             sa.v_proj.register_forward_hook(lambda m, i, o: cap.__setitem__("v", o)),
+             sa.o_proj.register_forward_pre_hook(lambda m, i: cap.__setitem__("out", i[0]))]
     try:
         set_tau(model, 0.5)
         st.install_shared_pi_forward(model, pct=30.0, tile=64, k_max=256)
         with torch.no_grad():
             out = model(ids).logits
         assert torch.isfinite(out).all()
-        sa = model.model.layers[1].self_attn
-        assert int(sa.spi_last_kept[:, -1].max()) < 512
+        assert int(sa.spi_last_kept[:, -1].max()) < N
+        q = cap["q"].view(1, N, H, D).transpose(1, 2)[0].contiguous()
+        k = cap["k"].view(1, N, Hk, D).transpose(1, 2)[0].contiguous()
+        v = cap["v"].view(1, N, Hk, D).transpose(1, 2)[0].contiguous()
+        got = cap["out"].view(1, N, H, D).transpose(1, 2)[0].cpu().numpy()
+        inv_a, ps_a, rs_a = sa.spi_sel
+        ps = sa.spi_pos_scale
+        ps_a = ps if ps_a is None else ps_a
+        tau = torch.full((H,), 0.5)
+        votes = core.select(q, k, tau, Geometry(inv_a.cpu(), ps_a, rs_a), tile=64)["votes"]
+        dense = core.expand_compact(votes, H, N, 64).cpu().numpy().astype(np.int32)
+        G = H // Hk
+        qx = q.cpu().numpy()
+        kx = np.repeat(k.cpu().numpy(), G, 0)
+        vx = np.repeat(v.cpu().numpy(), G, 0)
+        inv_c, ps_c, rs_c = sa.spi_att
+        ps_c = ps if ps_c is None else ps_c
+        o = oracle.shared_attention(qx, kx, vx, tau.numpy(), inv_a.cpu().numpy(), ps_a, rs_a,
+                                    inv_c.cpu().numpy(), ps_c, rs_c, pct=30.0,
+                                    sm_scale=sa.scaling, tile=64, k_max=256,
+                                    sel={"votes": dense})
+        assert np.abs(got - o[0]).max() <= 1e-4
+        np.testing.assert_array_equal(sa.spi_last_kept.cpu().numpy(), o[2])
     finally:
+        for h in hooks:
+            h.remove()
         ml.LlamaAttention.forward = orig_forward
 
 
