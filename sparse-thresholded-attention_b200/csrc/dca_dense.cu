@@ -11,14 +11,15 @@
 // attention with RoPE at the true positions.
 //
 // Per CTA (persistent, one per SM, longest-first over items of 128 query rows of one q head):
-//   warps 0-3  softmax: thread r owns query row r (TMEM lane r).  Per key block: read S from
-//              TMEM, mask, running max in the log2 domain with a lazy rescale of O (only when
+//   warps 0-7  softmax: two warps per TMEM lane quadrant share each query row (TMEM lane r),
+//              64 S columns each.  Per key block: read S from TMEM, mask, the row max of both
+//              halves (shared memory), running max in the log2 domain, lazy rescale of O (only when
 //              the max grows by more than 2^8, after the previous P.V has completed), P = 2^(x-m)
 //              written back into the same TMEM columns as bf16 (hi, and lo for fp32 inputs),
 //              row sum in fp32; at the item's end O / l to global memory;
-//   warp 4     TMA producer: the item's query plane (single buffer, reloaded on a plane change),
+//   warp 8     TMA producer: the item's query plane (single buffer, reloaded on a plane change),
 //              K blocks and V^T blocks through two rings;
-//   warp 5     MMA issuer (one thread): S = Q.K^T (M128 N128 K16, smem operands) into one of
+//   warp 9     MMA issuer (one thread): S = Q.K^T (M128 N128 K16, smem operands) into one of
 //              three TMEM slots, then O += P.V with P read from TMEM (the A operand) and V^T
 //              from shared memory; S of block g+1 is issued before P.V of block g so the
 //              softmax of one block overlaps the tensor work of the next.
@@ -42,6 +43,8 @@ constexpr int BN = 128;           // keys per block == MMA N of S
 constexpr int NS = 3;             // S / P slots (128 TMEM columns each)
 constexpr int OCOL = NS * BN;     // O accumulator columns [384, 384 + D)
 constexpr int kChunk = 128 * 128; // one 128-row x 64-bf16 swizzled chunk (16 KB)
+constexpr int kSP = 2;            // softmax warps per TMEM lane quadrant
+constexpr int kSoftmax = 4 * kSP; // softmax warps (warps 0 .. kSoftmax-1)
 
 template <int D, bool F32>
 struct DCfg {
@@ -53,8 +56,9 @@ struct DCfg {
   static constexpr int V_STAGE = NPV * 2 * VT_CHUNK;  // one 128-key block of V^T, all pieces
   static constexpr int NSK = F32 ? 1 : 2;
   static constexpr int NSV = 1;
-  static constexpr int SMEM = 1024 + Q_BYTES + NSK * K_STAGE + NSV * V_STAGE + 512;
-  static constexpr int kThreads = 192;
+  // + barriers (< 256 B) and the softmax parts' row exchange (kSP x 128 floats)
+  static constexpr int SMEM = 1024 + Q_BYTES + NSK * K_STAGE + NSV * V_STAGE + 256 + kSP * 512;
+  static constexpr int kThreads = (kSoftmax + 2) * 32;
 };
 
 struct DParams {
@@ -93,7 +97,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 }
 
 template <int D, bool F32>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__((kSoftmax + 2) * 32, 1)
 dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
                  const __grid_constant__ CUtensorMap tm_khi, const __grid_constant__ CUtensorMap tm_klo,
                  const __grid_constant__ CUtensorMap tm_vhi, const __grid_constant__ CUtensorMap tm_vlo,
@@ -113,9 +117,9 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
   uint64_t* v_full = k_empty + C::NSK;
   uint64_t* v_empty = v_full + C::NSV;
   uint64_t* s_full = v_empty + C::NSV;   // [NS] S of a block in its slot
-  uint64_t* p_full = s_full + NS;        // [NS] P written (128 arrivals)
+  uint64_t* p_full = s_full + NS;        // [NS] P written (all softmax threads)
   uint64_t* pv_done = p_full + NS;       // [NS] P.V of the slot's block completed
-  uint64_t* o_free = pv_done + NS;       // O read out by the softmax warps (128 arrivals)
+  uint64_t* o_free = pv_done + NS;       // O read out (all softmax threads)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(o_free + 1);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
@@ -134,10 +138,10 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
     }
     for (int s = 0; s < NS; ++s) {
       mbar_init(s_full + s, 1);
-      mbar_init(p_full + s, 128);
+      mbar_init(p_full + s, kSoftmax * 32);
       mbar_init(pv_done + s, 1);
     }
-    mbar_init(o_free, 128);
+    mbar_init(o_free, kSoftmax * 32);
     *s_abort = 0;
     fence_barrier_init();
     fence_proxy_async();
@@ -152,7 +156,7 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
   const uint32_t tmem_base = *s_tmem;
   const int64_t total = p.BH * (int64_t)p.nqb;
 
-  if (warp == 4) {
+  if (warp == kSoftmax) {
     // -------------------------------------------------------------- TMA producer
     if (lane == 0) {
       prefetch_tmap(&tm_qhi);
@@ -216,7 +220,7 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kSoftmax + 1) {
     // -------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(BM, BN);
@@ -327,11 +331,20 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
     }
   } else {
     // -------------------------------------------------------------- softmax / epilogue
-    const int quad = warp;                 // warps 0-3: TMEM lane quadrant == warp
+    // kSP warps per TMEM lane quadrant share each row: warp (quad, part) handles the row's
+    // columns [part * BN / kSP, +BN / kSP) of S and the O columns of chunks c with
+    // c % kSP == part.  Row maxima and sums of the parts meet in shared memory behind the
+    // quadrant's named barrier (id 1 + quad).  After a failed wait a warp keeps walking the
+    // schedule without touching TMEM, so every warp still reaches every barrier.
+    const int quad = warp & 3;
+    const int part = warp >> 2;
     const int row = quad * 32 + lane;
     const uint32_t lane_addr = tmem_base + ((uint32_t)(quad * 32) << 16);
+    constexpr int CW = BN / kSP;  // S columns per warp
+    float* s_x = reinterpret_cast<float*>(s_tmem + 4);  // [kSP][128] partial max / sum
     uint32_t g = 0;
     bool ok = true;
+    auto quad_sync = [&]() { named_bar_sync(1 + quad, kSP * 32); };
     for (int64_t w = blockIdx.x; w < total; w += gridDim.x) {
       int64_t bh, kvh;
       int qb;
@@ -345,28 +358,37 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
         if (ok && lane == 0) bad = !mbar_wait(s_full + slot, (g / NS) & 1, s_abort, p.err,
                                                kErrTimeoutAcc, p.limit_ns);
         if (__shfl_sync(0xffffffffu, bad, 0)) ok = false;
-        if (!ok) continue;
-        tc_fence_after();
-        float x[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld32(lane_addr + slot * BN + c * 32, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) x[c * 32 + j] = v[j];
-        }
-        const int64_t kbase = (int64_t)kb * BN;
+        float x[CW];
+        const int64_t kbase = (int64_t)kb * BN + part * CW;
         float mx = -INFINITY;
+        if (ok) {
+          tc_fence_after();
 #pragma unroll
-        for (int j = 0; j < 128; ++j) {
-          const bool keep = row_ok && (kbase + j <= qp);
-          x[j] = keep ? x[j] * p.c_log2 : -INFINITY;
-          mx = fmaxf(mx, x[j]);
+          for (int c = 0; c < CW / 32; ++c) {
+            float v[32];
+            tmem_ld32(lane_addr + slot * BN + part * CW + c * 32, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) x[c * 32 + j] = v[j];
+          }
+#pragma unroll
+          for (int j = 0; j < CW; ++j) {
+            const bool keep = row_ok && (kbase + j <= qp);
+            x[j] = keep ? x[j] * p.c_log2 : -INFINITY;
+            mx = fmaxf(mx, x[j]);
+          }
         }
+        // the row max over all parts
+        s_x[part * 128 + row] = mx;
+        quad_sync();
+#pragma unroll
+        for (int q2 = 0; q2 < kSP; ++q2) mx = fmaxf(mx, s_x[q2 * 128 + row]);
+        quad_sync();
+        if (!ok) continue;
         // Lazy rescale: only when some row's max grew by more than 2^8.  The TMEM accesses are
-        // warp-collective, so the decision is taken per warp: every row of the warp then moves
-        // to its own new max (factor <= 1; 0 for a row without earlier contributions).
+        // warp-collective, so the decision is taken per warp (the parts of a quadrant see the
+        // same row maxima and decide alike): every row then moves to its own new max (factor
+        // <= 1; 0 for a row without earlier contributions).
         const float m_new = fmaxf(m_used, mx);
         const bool want = mx > m_used + 8.f;
         if (kb == 0) {
@@ -384,7 +406,7 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
           tc_fence_after();
           const float f = m_used > -INFINITY ? exp2f(m_used - m_new) : 0.f;
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = part; c < D / 32; c += kSP) {
             float v[32];
             tmem_ld32(lane_addr + OCOL + c * 32, v);
             tmem_wait_ld();
@@ -396,11 +418,11 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
           l *= f;
           m_used = m_new;
         }
-        // P = 2^(x - m_used) as bf16 pairs (key 2w in the low half of column w), 64 keys at a
-        // time; fp32 inputs also store the residual lo pieces 64 columns further
+        // P = 2^(x - m_used) as bf16 pairs (key 2w in the low half of column w), 64 keys per
+        // store; fp32 inputs also store the residual lo pieces 64 columns further
         float bsum = 0.f;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < CW / 64; ++h) {
           uint32_t ph[32], pl[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -414,15 +436,22 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
               pl[j] = pack_bf16(a - __low2float(hv), b - __high2float(hv));
             }
           }
-          tmem_st32(lane_addr + slot * BN + 32 * h, ph);
-          if (F32) tmem_st32(lane_addr + slot * BN + 64 + 32 * h, pl);
+          const uint32_t pc = slot * BN + (part * CW) / 2 + 32 * h;
+          tmem_st32(lane_addr + pc, ph);
+          if (F32) tmem_st32(lane_addr + pc + 64, pl);
         }
         l += bsum;
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(p_full + slot);
       }
-      // item end: O after the last P.V, divided by the row sum
+      // item end: the row sum over the parts, O after the last P.V divided by it
+      s_x[part * 128 + row] = l;
+      quad_sync();
+      float lt = 0.f;
+#pragma unroll
+      for (int q2 = 0; q2 < kSP; ++q2) lt += s_x[q2 * 128 + row];
+      quad_sync();
       if (ok) {
         const uint32_t gp = g - 1;
         int bad = 0;
@@ -432,10 +461,10 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
       }
       if (ok) {
         tc_fence_after();
-        const float inv = (row_ok && l > 0.f) ? 1.f / l : 0.f;
+        const float inv = (row_ok && lt > 0.f) ? 1.f / lt : 0.f;
         const int64_t orow = bh * p.Nq + (qp - p.qbase);
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = part; c < D / 32; c += kSP) {
           float v[32];
           tmem_ld32(lane_addr + OCOL + c * 32, v);
           tmem_wait_ld();
