@@ -371,11 +371,19 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
 #pragma unroll
             for (int j = 0; j < 32; ++j) x[c * 32 + j] = v[j];
           }
+          if (kb == qb || !row_ok) {  // the diagonal block (or a row past the end): mask
+            const int64_t lim = row_ok ? qp - kbase : -1;  // keys j <= lim are causal
 #pragma unroll
-          for (int j = 0; j < CW; ++j) {
-            const bool keep = row_ok && (kbase + j <= qp);
-            x[j] = keep ? x[j] * p.c_log2 : -INFINITY;
-            mx = fmaxf(mx, x[j]);
+            for (int j = 0; j < CW; ++j) {
+              x[j] = (j <= lim) ? x[j] * p.c_log2 : -INFINITY;
+              mx = fmaxf(mx, x[j]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < CW; ++j) {
+              x[j] *= p.c_log2;
+              mx = fmaxf(mx, x[j]);
+            }
           }
         }
         // the row max over all parts
@@ -427,8 +435,9 @@ dca_dense_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_consta
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const float xa = x[64 * h + 2 * j], xb = x[64 * h + 2 * j + 1];
-            const float a = xa > -INFINITY ? exp2f(xa - m_used) : 0.f;
-            const float b = xb > -INFINITY ? exp2f(xb - m_used) : 0.f;
+            // m_used is finite for every row with a causal key; 2^(-inf) = 0 for masked keys
+            const float a = row_ok ? exp2f(xa - m_used) : 0.f;
+            const float b = row_ok ? exp2f(xb - m_used) : 0.f;
             bsum += a + b;
             ph[j] = pack_bf16(a, b);
             if (F32) {
