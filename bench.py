@@ -338,6 +338,51 @@ def run_reference_gpu(args):
     emit(line)
 
 
+def parity_block(q, k, v, tau, geo, geo_c, c, qd, kd, out, ga, n_tiles=12, seed=7):
+    """Checker beside the CPU baseline: this run's output against the oracle on a seeded
+    sample of query tiles (plus the last tile) of q head 0 at the benchmark's full length.
+    Kernel A's votes of head 0 (read back through sta_select) must equal the oracle's except
+    keys whose score is within 1e-3 of the threshold; the oracle then selects and attends on
+    those device votes, and the op's output rows must be within max-abs 2e-2 / mean-abs 1e-3."""
+    import numpy as np
+    from oracle import sta_oracle as oracle
+    from sta import core
+    T, N, D, k_max = c["T"], c["S"], c["D"], c["k_max"]
+    nt = (N + T - 1) // T
+    rng = np.random.default_rng(seed)
+    tiles = sorted(set(int(x) for x in rng.choice(nt, size=min(n_tiles, nt), replace=False)) | {nt - 1})
+    sel = core.select(qd[0, 0:1], kd[0, 0:1], tau[0:1], ga, tile=T)
+    votes = sel["votes"].cpu().numpy()
+    sm = 1.0 / math.sqrt(D)
+    qx, kx, vx = q[0, 0].float().numpy(), k[0, 0].float().numpy(), v[0, 0].float().numpy()
+    ora = oracle.select_tiles(qx, kx, c["tau"], geo["inv_freq"].numpy(), geo["pos_scale"],
+                              geo["rope_scale"], sm, T, tiles, dca=geo.get("dca"))
+    outside = flips = 0
+    idx = np.full((1, nt, k_max), N, np.int32)
+    npk = np.zeros((1, nt, k_max), np.float32)
+    npq = np.zeros((1, nt, T), np.float32)
+    for t in tiles:
+        o = ora[t]
+        off = T * t * (t + 1) // 2
+        dv = votes[off:off + o["hi"]].astype(np.int64)
+        d = np.abs(dv - o["votes"])
+        outside += int((d > o["near"]).sum())
+        flips += int(d.sum())
+        v1 = np.zeros((1, 1, N), np.int64)
+        v1[0, 0, :o["hi"]] = dv
+        s_ = oracle.build_sets(v1, geo_c["pos_scale"], 32, 32, c["pct"], T, k_max, q_pos_base=t * T)
+        idx[0, t], npk[0, t], npq[0, t] = s_[0][0, 0], s_[1][0, 0], s_[2][0, 0]
+    ref = oracle.gather_attn(qx[None], kx[None], vx[None], geo_c["inv_freq"].numpy(), idx, npk,
+                             npq, sm, geo_c["rope_scale"], T, v_is_bf16=True, tiles=tiles)
+    got = out[0, 0].float().cpu().numpy()
+    rows = np.concatenate([np.arange(t * T, min((t + 1) * T, N)) for t in tiles])
+    err = np.abs(got[rows] - ref[0, rows])
+    return {"head": 0, "tiles": len(tiles), "vote_keys_outside_boundary": outside,
+            "boundary_vote_flips": flips, "out_max_abs": float(err.max()),
+            "out_mean_abs": float(err.mean()), "tolerance": "max-abs 2e-2, mean-abs 1e-3",
+            "pass": bool(outside == 0 and err.max() <= 2e-2 and err.mean() <= 1e-3)}
+
+
 def run_reference(args):
     """--impl reference: the reference's algorithm on the host cores (oracle port).
 
@@ -639,6 +684,8 @@ def run_gpu(args):
         tok_cpu, _, desc = cpu_sample(q, k, v, tau, geo, c, n_tiles=240, geo_c=geo_c)
         cpu = {"value": tok_cpu, "unit": "tokens/s", "cores": os.cpu_count() or 1,
                "kind": "port", "sample": desc}
+        if args.variant == "shared" and s0 == 0 and k0 == 0:
+            cpu["parity"] = parity_block(q, k, v, tau, geo, geo_c, c, qd, kd, out, ga)
     stats = {}
     if args.variant == "shared":
         ks_ = st["kept_size"].float()
@@ -667,7 +714,8 @@ def run_gpu(args):
                 "kv_head_groups": ngroups,
                 "stage_ms": {"rope_prologue": stage_ms[0], "select_tcgen05": stage_ms[1],
                              "build_sets": stage_ms[2], "attend": stage_ms[3]},
-                "roofline": roof, "cpu_baseline": cpu, "selection": stats}
+                "roofline": roof, "cpu_baseline": cpu, "selection": stats,
+                "parity": (cpu or {}).get("parity")}
         emit(line)
     if world > 1:
         dist.destroy_process_group()
