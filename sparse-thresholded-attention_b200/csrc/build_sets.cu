@@ -546,13 +546,23 @@ __global__ void __launch_bounds__(kBT) build_sets_pq_kernel(const BuildPQP p) {
   int64_t carry = 0, tie_carry = 0;
   for (int64_t c0 = 0; c0 < E; c0 += kChunk) {
     const int64_t j0 = c0 + (int64_t)tid * kItems;
+    // the thread's kItems consecutive votes, one 8-byte load where aligned and in range
+    uint32_t vb8[kItems];
+    if (j0 + kItems <= r.hi && ((reinterpret_cast<uintptr_t>(r.v + j0) & 7u) == 0)) {
+      const uint2 u = *reinterpret_cast<const uint2*>(r.v + j0);
+#pragma unroll
+      for (int i = 0; i < kItems; ++i) vb8[i] = ((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 255u;
+    } else {
+#pragma unroll
+      for (int i = 0; i < kItems; ++i) vb8[i] = j0 + i < r.hi ? r.v[j0 + i] : 0u;
+    }
     uint32_t flags = 0, tie = 0, sure = 0;
 #pragma unroll
     for (int i = 0; i < kItems; ++i) {
       const int64_t j = j0 + i;
       if (j >= E) continue;
       const bool forced = F.has(j);
-      const bool uni = j < r.hi && r.v[j] != 0;
+      const bool uni = vb8[i] != 0;
       if (!overflow) {
         if (forced || uni) sure |= 1u << i;
       } else if (forced) {
