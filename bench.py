@@ -658,6 +658,8 @@ def run_gpu(args):
                       "overlapping H2D / compute / D2H"}
 
     # ---- roofline of the dominant kernel (Kernel A on tensor cores)
+    # screened scoring runs for unweighted selections (shared freq votes, PQ-Stream bits)
+    screened = os.environ.get("STA_SELECT_SCREEN", "0") == "1" and args.variant != "pq_union"
     pk, pk_kind = peaks()
     Hr = qs.shape[1]
     pairs = (s1 * (s1 + 1) - s0 * (s0 + 1)) / 2   # causal (query, key) pairs of this rank's slab
@@ -666,13 +668,17 @@ def run_gpu(args):
     achieved = flops_sel / (sel_ms / 1e3) / 1e12
     peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
     traffic, traffic_src = select_traffic_bytes(c, Hr, s0, s1)
-    roof = {"kernel": "select_kernel (tcgen05 exact-max two-pass Kernel A)", "bound": "tensor",
+    roof = {"kernel": "select_kernel (tcgen05 exact-max Kernel A)", "bound": "tensor",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "peak_kind": f"{pk_kind} bf16 sustained", "traffic": traffic,
             "traffic_source": traffic_src,
             "algorithmic_flops_per_launch": flops_sel, "launch_ms": sel_ms,
-            "tensor_flops_issued_per_launch": 3 * flops_sel,
-            "note": "3 bf16 products per fp32-accurate score (hi*hi + hi*lo + lo*hi)"}
+            "tensor_flops_issued_per_launch": (1.5 if screened else 3) * flops_sel,
+            "note": ("screened scoring: 3 passes of ONE fp16 product per pair (screened max, "
+                     "exact max of the candidates, votes); pairs within the proven bound of the "
+                     "max / threshold rescored exactly on the CUDA cores; the launch time "
+                     "includes the fp16-operand / norm prep kernel") if screened else
+                    "3 bf16 products per fp32-accurate score (hi*hi + hi*lo + lo*hi)"}
 
     # per op call: the cos/sin table, then per kv-head group the RoPE prologue of q and k (q in
     # 3 planes for DCA), Kernel A, the selection and the attend (PQ-Stream: pass 2 fused)

@@ -48,7 +48,8 @@ extern "C" {
  * Library
  * ------------------------------------------------------------------------------------- */
 const char* sta_last_error(void);
-/* ABI version: 3 (2: query slabs, PQ-Stream pass 2 on Kernel A keep bits, decode; 3: select wait limit) */
+/* ABI version: 4 (2: query slabs, PQ-Stream pass 2 on Kernel A keep bits, decode; 3: select wait
+ * limit; 4: screened select scoring, sta_select_args.screen_ws) */
 int sta_version(void);
 /* Number of elements of one head of a compact selection array. */
 int64_t sta_tri_head_stride(int64_t n, int32_t tile);
@@ -126,9 +127,21 @@ typedef struct sta_select_args {
    * call itself has already returned STA_OK (launches are asynchronous).  Small values exist
    * to exercise that failure path in tests. */
   uint64_t wait_limit_ns;
+  /* optional scratch of sta_select_screen_bytes(a) bytes (256-byte aligned) enabling screened
+   * scoring for unweighted votes / bits / row maxima (wmode 0): every score is first formed as
+   * ONE fp16 tensor-core product, and only the (query, key) pairs whose screened score lies
+   * within a proven bound of the row max or of the threshold are scored exactly (the fixed-order
+   * fp32 sum of the three bf16 piece products).  Results are those of exact scoring; NULL
+   * scores every pair with three bf16 products.  Measured on B200 the exact kernel is the
+   * faster one at the benchmark shapes (its per-block epilogue, not the tensor products, sets
+   * the pace, and screening adds a third epilogue pass); the forward entry points use
+   * screening only when STA_SELECT_SCREEN=1 is set in the environment. */
+  void* screen_ws;
 } sta_select_args;
 
 int sta_select(const sta_select_args* a, void* stream);
+/* Bytes of sta_select_args.screen_ws for these arguments (0 for invalid shapes). */
+size_t sta_select_screen_bytes(const sta_select_args* a);
 
 /* ---------------------------------------------------------------------------------------
  * Stage 2 -- device selection of the shared path (top pct% of the pooled set with the

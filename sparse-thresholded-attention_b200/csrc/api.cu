@@ -9,6 +9,7 @@
 // Scratch lives in a caller-provided workspace; when a cap is given, the op walks over groups of
 // kv heads (every stage is independent per (batch, kv head)), reusing the same scratch.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -93,12 +94,24 @@ inline size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 struct Layout {
   int64_t c;          // kv heads per group
   size_t qh, ql, kh, kl, votes, wvotes, bits, idx, npk, npq, mask, rowcnt, bmax, rtab, stab, total;
+  size_t scr, scr_len;  // screened-select scratch (0 length: exact three-product scoring)
   float rtab_R, stab_R;
   int64_t rtab_len, stab_len;
   bool stab_shared;  // the selection table is the attend table
 };
 
 int64_t esize(int dt) { return dt == STA_DTYPE_F32 ? 4 : 2; }
+
+// STA_SELECT_SCREEN=1 in the environment turns screened Kernel A scoring on in the forward
+// entry points.  Off by default: on B200 the screened kernel's three epilogue passes cost more
+// than the two products per pair it saves (cfg2: 23.7 ms vs 20.1 ms exact).
+bool screen_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("STA_SELECT_SCREEN");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
 
 Layout layout_for(const sta_forward_args* a, Variant v, int64_t c) {
   Layout L{};
@@ -174,6 +187,19 @@ Layout layout_for(const sta_forward_args* a, Variant v, int64_t c) {
     } else {
       L.stab = take((size_t)L.stab_len * (D / 2) * 8);
     }
+  }
+  // screened Kernel A scoring for unweighted selections (sta_select_args.screen_ws)
+  if (screen_enabled() && (v == kPQStream || a->select_score == STA_SCORE_FREQ)) {
+    sta_select_args s{};
+    s.batch = 1;
+    s.n_heads = qh;
+    s.n_kv_heads = c;
+    s.n = N;
+    s.d = a->d;
+    s.dca_chunk_len = a->dca_chunk_size > 0 ? 1 : 0;
+    s.q_pos_base = a->q_pos_base;
+    L.scr_len = select_screen_bytes(&s);
+    if (L.scr_len > 0) L.scr = take(L.scr_len);
   }
   L.total = o;
   return L;
@@ -309,6 +335,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       s.tau = tau;
       s.dca_chunk_len = (int32_t)dL;
       s.q_pos_base = qbase;
+      s.screen_ws = L.scr_len > 0 ? w + L.scr : nullptr;
       mark(1);
       if (v == kPQStream) {
         s.bits = reinterpret_cast<uint32_t*>(w + L.bits);
@@ -484,7 +511,7 @@ extern "C" {
 
 const char* sta_last_error(void) { return g_last_error; }
 
-int sta_version(void) { return 3; }
+int sta_version(void) { return 4; }
 
 int64_t sta_tri_head_stride(int64_t n, int32_t tile) { return tri_head_stride(n, tile); }
 
@@ -529,6 +556,8 @@ int sta_rope_table(const float* inv_freq, int32_t d, float rope_scale, float R, 
 int sta_select(const sta_select_args* a, void* stream) {
   return launch_select(a, static_cast<cudaStream_t>(stream));
 }
+
+size_t sta_select_screen_bytes(const sta_select_args* a) { return select_screen_bytes(a); }
 
 int sta_build_sets(const sta_build_args* a, void* stream) {
   return launch_build_sets(a, static_cast<cudaStream_t>(stream));

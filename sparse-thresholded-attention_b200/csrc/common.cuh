@@ -257,6 +257,13 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
          | ((uint32_t)(M >> 4) << 24);      // M / 16
 }
 
+// kind::f16 with fp16 A / B (format code 0), fp32 accumulation
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+  return (1u << 4)                          // D format: f32
+         | ((uint32_t)(N >> 3) << 17)       // N / 8
+         | ((uint32_t)(M >> 4) << 24);      // M / 16
+}
+
 // ------------------------------------------------------------------------------------------
 // misc
 // ------------------------------------------------------------------------------------------

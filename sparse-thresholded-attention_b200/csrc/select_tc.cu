@@ -20,6 +20,7 @@
 //   warp 17    MMA issuer (one thread), M=128 N=256 K=16, 2 TMEM accumulator slots of 256
 //              columns; the K ring holds one bf16 piece (hi or lo) of a key block per stage.
 // All waits are bounded; on expiry the kernel records STA_ERR_TIMEOUT and unwinds.
+#include <cuda_fp16.h>
 #include "common.cuh"
 #include "sta_internal.h"
 
@@ -76,6 +77,12 @@ struct Params {
   int bmax_bn;
   int64_t bmax_head_stride;
   uint64_t limit_ns;    // bound of every mbarrier wait
+  // screened scoring (SCR kernels): canonical bf16 pieces for exact recomputation, per-row
+  // query norms and per-32-key-chunk key norm maxima of the fp16 screening operands
+  const __nv_bfloat16 *qh, *ql, *kh, *kl;
+  const float2* qnorm;  // (BH, Nq): ||q16||, ||q' - q16|| (max over DCA planes)
+  const float2* knorm;  // (BHk): max ||k16||, max ||k' - k16|| over the head's keys
+  int64_t nkc;          // 32-key chunks per kv head
 };
 
 // Which rotated Q plane scores key block kb of query block qb: 0 = plain (or same DCA chunk),
@@ -113,6 +120,87 @@ __device__ __forceinline__ float raw_threshold(float thr, float sm) {
   return x;
 }
 
+// Canonical exact score of one (query row, key) pair in raw accumulator units: the three
+// products hi*hi + hi*lo + lo*hi of the bf16 pieces, lane l taking dims [l*E, l*E+E) in a
+// fixed FMA order and a xor butterfly summing the lanes (every lane ends with the identical
+// value).  Every pass that needs an exact score calls this, so they agree bit for bit.
+template <int D>
+__device__ __forceinline__ float exact_score(const __nv_bfloat16* qh, const __nv_bfloat16* ql,
+                                             const __nv_bfloat16* kh, const __nv_bfloat16* kl) {
+  constexpr int E = D / 32;
+  const int l = lane_id();
+  __nv_bfloat16 a[E], b[E], c[E], d[E];
+  if constexpr (E == 4) {
+    *reinterpret_cast<uint2*>(a) = __ldg(reinterpret_cast<const uint2*>(qh) + l);
+    *reinterpret_cast<uint2*>(b) = __ldg(reinterpret_cast<const uint2*>(ql) + l);
+    *reinterpret_cast<uint2*>(c) = __ldg(reinterpret_cast<const uint2*>(kh) + l);
+    *reinterpret_cast<uint2*>(d) = __ldg(reinterpret_cast<const uint2*>(kl) + l);
+  } else {
+    *reinterpret_cast<uint32_t*>(a) = __ldg(reinterpret_cast<const unsigned int*>(qh) + l);
+    *reinterpret_cast<uint32_t*>(b) = __ldg(reinterpret_cast<const unsigned int*>(ql) + l);
+    *reinterpret_cast<uint32_t*>(c) = __ldg(reinterpret_cast<const unsigned int*>(kh) + l);
+    *reinterpret_cast<uint32_t*>(d) = __ldg(reinterpret_cast<const unsigned int*>(kl) + l);
+  }
+  float acc = 0.f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float x = __bfloat162float(a[e]), y = __bfloat162float(b[e]);
+    const float u = __bfloat162float(c[e]), w = __bfloat162float(d[e]);
+    acc = __fmaf_rn(x, u, acc);
+    acc = __fmaf_rn(x, w, acc);
+    acc = __fmaf_rn(y, u, acc);
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+  return acc;
+}
+
+// Warp-collective exact scoring of the pairs (this lane's query row, key j) for the bits j of
+// pend; q* point at the warp's first query row, k* at the chunk's first key.  MAX: returns the
+// max of x and the exact scores; otherwise returns (as float bits) the bits whose exact score
+// reaches x (the raw threshold).  Out of line: it runs for few chunks, and keeping its
+// registers out of the epilogue's hot loop avoids spills there.
+template <int D, bool MAX>
+__device__ __noinline__ float resolve_pairs(uint32_t pend, float x, const __nv_bfloat16* qh,
+                                            const __nv_bfloat16* ql, const __nv_bfloat16* kh,
+                                            const __nv_bfloat16* kl) {
+  const int lane = lane_id();
+  float mx = x;
+  uint32_t res = 0;
+  for (;;) {
+    uint32_t lanes = __ballot_sync(0xffffffffu, pend != 0u);
+    if (!lanes) break;
+    const int myj = pend ? __ffs(pend) - 1 : 0;
+    while (lanes) {
+      const int src = __ffs(lanes) - 1;
+      lanes &= lanes - 1;
+      const int j = __shfl_sync(0xffffffffu, myj, src);
+      const float sc = exact_score<D>(qh + (int64_t)src * D, ql + (int64_t)src * D,
+                                      kh + (int64_t)j * D, kl + (int64_t)j * D);
+      if (lane == src) {
+        if (MAX) mx = fmaxf(mx, sc);
+        else if (sc >= x) res |= 1u << j;
+      }
+    }
+    if (pend) pend &= pend - 1u;
+  }
+  return MAX ? mx : __uint_as_float(res);
+}
+
+// Upper bound of |screened score - canonical score| for a query row with fp16-operand norms
+// (qa, qr) against a key chunk with (ka, kr):  q' = q16 + rq, k' = k16 + rk gives
+// q'.k' - q16.k16 = q16.rk + rq.k16 + rq.rk (Cauchy-Schwarz per term); the 2^-13 |q16||k16|
+// slack covers the dropped lo*lo product (<= 2^-16), fp32 accumulation of the tensor-core sum
+// (<= 128 * 2^-24) and of the canonical FMA chain (<= 384 * 2^-24), all relative to |q||k|.
+__device__ __forceinline__ float screen_bound(float qa, float qr, float ka, float kr) {
+  return __fmaf_ru(qa, kr, __fmaf_ru(qr, ka, __fmaf_ru(qr, kr, __fmul_ru(1.220703125e-4f, __fmul_ru(qa, ka)))));
+}
+
+// first canonical query row (q_hi / q_lo row index) of an epilogue warp's 32 rows
+__device__ __forceinline__ int64_t qrow_of(const Params& p, int qb, int kb, int64_t bh, int quad) {
+  return ((int64_t)q_plane(p, qb, kb) * p.BH + bh) * p.Nq + ((int64_t)qb * BM - p.qbase) + quad * 32;
+}
+
 __device__ __forceinline__ void decode_item(int64_t w, const Params& p, int64_t& bh, int& qb,
                                             int64_t& kvh) {
   qb = p.nqb - 1 - (int)(w / p.BH) + p.qb0;  // absolute query block
@@ -121,12 +209,15 @@ __device__ __forceinline__ void decode_item(int64_t w, const Params& p, int64_t&
   kvh = (bh / p.H) * p.Hkv + (bh % p.H) / G;
 }
 
-template <int D>
+template <int D, bool SCR>
 __global__ void __launch_bounds__(kThreads, 1)
 select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
               const __grid_constant__ CUtensorMap tm_khi, const __grid_constant__ CUtensorMap tm_klo,
               const Params p) {
   using C = Cfg<D>;
+  // screened: one fp16 operand piece per block and three passes (screened max, exact max of
+  // the candidates, votes); exact: two bf16 pieces, three products, two passes
+  constexpr int kPieces = SCR ? 1 : 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -200,17 +291,17 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
                 ok = false;
                 break;
               }
-              mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+              mbar_arrive_expect_tx(q_full, SCR ? C::Q_BYTES / 2 : C::Q_BYTES);
               const int z = (int)(plane * p.BH + bh);
               for (int c = 0; c < C::NC; ++c) {
                 const int qrow = (qb - p.qb0) * BM;  // local row in the Q slab
                 tma_load_3d(sQ + c * kTileBytes, &tm_qhi, q_full, c * 64, qrow, z);
-                tma_load_3d(sQ + (C::NC + c) * kTileBytes, &tm_qlo, q_full, c * 64, qrow, z);
+                if (!SCR) tma_load_3d(sQ + (C::NC + c) * kTileBytes, &tm_qlo, q_full, c * 64, qrow, z);
               }
               ++qloads;
               cur = plane;
             }
-            for (int piece = 0; piece < 2; ++piece, ++kc) {  // hi piece, then lo piece
+            for (int piece = 0; piece < kPieces; ++piece, ++kc) {  // hi piece, then lo piece
               const uint32_t s = kc % C::NSTAGE, r = kc / C::NSTAGE;
               if (r > 0 && !mbar_wait(k_empty + s, (r - 1) & 1, s_abort, p.err, kErrTimeoutEmpty, p.limit_ns)) {
                 ok = false;
@@ -229,7 +320,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
   } else if (warp == kEpi / 32 + 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      constexpr uint32_t idesc = SCR ? idesc_f16_f32(BM, BN) : idesc_bf16_f32(BM, BN);
       const uint32_t q_addr = smem_u32(sQ);
       const uint32_t k_addr = smem_u32(sK);
       uint32_t kc = 0, ac = 0, qloads = 0;
@@ -263,8 +354,9 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             }
             const uint32_t d_tmem = tmem_base + slot * BN;
             uint32_t acc = 0;
-            // piece 0 (K hi): Qhi.Khi + Qlo.Khi ; piece 1 (K lo): Qhi.Klo
-            for (int piece = 0; piece < 2; ++piece, ++kc) {
+            // piece 0 (K hi): Qhi.Khi + Qlo.Khi ; piece 1 (K lo): Qhi.Klo.  Screened: the one
+            // fp16 product Q16.K16
+            for (int piece = 0; piece < kPieces; ++piece, ++kc) {
               const uint32_t s = kc % C::NSTAGE, r = kc / C::NSTAGE;
               if (!mbar_wait(k_full + s, r & 1, s_abort, p.err, kErrTimeoutK, p.limit_ns)) {
                 ok = false;
@@ -281,7 +373,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
                   const uint64_t kd = sw128_kmajor_desc(st + c * kKTileBytes + kk * 32);
                   umma_bf16(d_tmem, qh, kd, idesc, acc);
                   acc = 1;
-                  if (piece == 0) {
+                  if (!SCR && piece == 0) {
                     const uint64_t ql = sw128_kmajor_desc(q_addr + C::NC * kTileBytes + qoff);
                     umma_bf16(d_tmem, ql, kd, idesc, 1);
                   }
@@ -299,12 +391,20 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
     // ---------------------------------------------------------------- epilogue
     // Thread r owns accumulator row r.  Scores are compared in raw accumulator units against a
     // per-row threshold derived exactly (see raw_threshold), so no per-element scaling is
-    // needed for the keep decision; pass 1 keeps the raw row max and scales it once.
+    // needed for the keep decision.
+    // Exact kernels: pass 0 keeps the raw row max, pass 1 votes.
+    // Screened kernels (SCR): the accumulator holds the fp16 product s16 = Q16.K16, within
+    // Bc = screen_bound(row norms, the kv head's maximum key norms) of the canonical score.
+    // Pass 0: max16 = max of s16, so the exact max is >= max16 - Bc.  Pass 1: every key with
+    // s16 >= max16 - 2 Bc is scored exactly (exact_score); their max is the exact row max.
+    // Pass 2: s16 > thr + Bc keeps, s16 < thr - Bc drops, the keys in between are scored exactly.
+    constexpr int kVotePass = SCR ? 2 : 1;
     const int quad = warp & 3;             // TMEM lane quadrant
     const int part = warp >> 2;            // which kChunks of the block's eight 32-column chunks
     const int row = quad * 32 + lane;
     const int64_t nt = (p.N + p.T - 1) / p.T;
     const int quads_per_tile = p.T / 32;
+    const int max_pass = SCR ? 1 : 0;      // the pass after which the exact row max is known
     uint32_t ac = 0;
     int rb = 0;
     bool ok = true;
@@ -320,11 +420,23 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
       const float tau_h = __ldg(p.tau + (bh % p.H));
       const int nb = qb / 2 + 1;
       float mraw = -INFINITY, m = -INFINITY, thr = -INFINITY, thr_raw = INFINITY;
+      float thr_pad = 0.f;
+      float Bc = 0.f;  // screen bound of this row against every key of the head (SCR)
+      if (SCR && row_ok) {
+        const float2 qn = __ldg(p.qnorm + bh * p.Nq + (qp - p.qbase));
+        const float2 kn = __ldg(p.knorm + kvh);
+        Bc = screen_bound(qn.x, qn.y, kn.x, kn.y);
+      }
+      float cthr = -INFINITY, hi_thr = INFINITY, lo_thr = INFINITY;
       int cnt = 0;
       for (int pass = 0; pass < p.npass; ++pass) {
-        if (pass == 1) {
+        if (pass == kVotePass) {
           thr = __fsub_rn(m, tau_h);
           thr_raw = row_ok ? raw_threshold(thr, p.sm_scale) : INFINITY;
+          // covers the rounding of thr_raw +- Bc
+          thr_pad = fabsf(thr_raw) < INFINITY ? 1.9073486e-6f * fabsf(thr_raw) : 0.f;
+          hi_thr = __fadd_ru(__fadd_ru(thr_raw, Bc), thr_pad);
+          lo_thr = __fsub_rd(__fsub_rd(thr_raw, Bc), thr_pad);
         }
         for (int kb = 0; kb < nb; ++kb, ++ac) {
           const uint32_t slot = ac % NACC, use = ac / NACC;
@@ -364,19 +476,56 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
                   for (int j = 0; j < 32; ++j)
                     m4[j & 3] = fmaxf(m4[j & 3], ((cmask >> j) & 1u) ? v[j] : -INFINITY);
                 }
-                mraw = fmaxf(mraw, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
-              } else {
-                uint32_t w4[4] = {0u, 0u, 0u, 0u};
+                const float cm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+                mraw = fmaxf(mraw, cm);
+              } else if (SCR && pass == 1) {
+                // candidates: s16 >= (max16 - Bc) - Bc; most chunks have none (chunk max first)
+                float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                for (int j = 0; j < 32; ++j) w4[j & 3] |= (v[j] >= thr_raw ? 1u : 0u) << j;
-                uint32_t word = ((w4[0] | w4[1]) | (w4[2] | w4[3])) & cmask;
+                for (int j = 0; j < 32; ++j) m4[j & 3] = fmaxf(m4[j & 3], v[j]);
+                uint32_t cand = 0;
+                if (fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) >= cthr) {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) cand |= (v[j] >= cthr ? 1u : 0u) << j;
+                }
+                cand &= cmask;
+                if (!row_ok) cand = 0;
+                if (__any_sync(0xffffffffu, cand != 0u)) {
+                  const int64_t qo = qrow_of(p, qb, kb, bh, quad) * D, ko = (kvh * p.N + kbase) * D;
+                  mraw = resolve_pairs<D, true>(cand, mraw, p.qh + qo, p.ql + qo, p.kh + ko, p.kl + ko);
+                }
+              } else {
+                uint32_t word;
+                if constexpr (SCR) {
+                  const float hi = hi_thr, lo = lo_thr;
+                  uint32_t k4[4] = {0u, 0u, 0u, 0u}, b4[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) {
+                    k4[j & 3] |= (v[j] > hi ? 1u : 0u) << j;
+                    b4[j & 3] |= (v[j] >= lo ? 1u : 0u) << j;
+                  }
+                  word = (k4[0] | k4[1]) | (k4[2] | k4[3]);
+                  uint32_t band = ((b4[0] | b4[1]) | (b4[2] | b4[3])) & ~word & cmask;
+                  if (!row_ok) band = 0;
+                  if (__any_sync(0xffffffffu, band != 0u)) {
+                    const int64_t qo = qrow_of(p, qb, kb, bh, quad) * D, ko = (kvh * p.N + kbase) * D;
+                    word |= __float_as_uint(resolve_pairs<D, false>(band, thr_raw, p.qh + qo, p.ql + qo,
+                                                                    p.kh + ko, p.kl + ko));
+                  }
+                } else {
+                  uint32_t w4[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) w4[j & 3] |= (v[j] >= thr_raw ? 1u : 0u) << j;
+                  word = (w4[0] | w4[1]) | (w4[2] | w4[3]);
+                }
+                word &= cmask;
                 if (!row_ok) word = 0;
                 cnt += __popc(word);
                 const uint32_t colw = transpose32(word);  // lane j: keep bits of column j, bit r = row r
                 float myw = 0.f;
                 // weighted votes only where some row of the warp keeps a key of this chunk (the
                 // kept sets are sparse: most chunks have none, and their sums are exactly 0)
-                if (p.wmode != 0 && __any_sync(0xffffffffu, word != 0u)) {
+                if (!SCR && p.wmode != 0 && __any_sync(0xffffffffu, word != 0u)) {
                   // v is not read again for this chunk: reuse it for the per-key weights
 #pragma unroll
                   for (int j = 0; j < 32; ++j) {
@@ -433,7 +582,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             tc_fence_before();
             mbar_arrive(acc_empty + slot);
           }  // ok
-          if (pass == 1 && p.T != 32) {
+          if (pass == kVotePass && p.T != 32) {
             // combine the quadrants of each query tile and store compact votes / wvotes: the
             // warps of one tile's quadrants meet at their own barrier (ids 4, 5)
             const int g = quad / quads_per_tile;                 // == tile of the item
@@ -457,8 +606,20 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             rb ^= 1;
           }
         }
-        if (pass == 0) {
-          // the two column halves of each row meet: exact row max, then scale once
+        if (SCR && pass == 0) {
+          // screened max of the row: max16 - Bc bounds the exact max from below, so a key can
+          // be the exact max only if s16 >= max16 - 2 Bc
+          s_rowx[part * 128 + row] = mraw;
+          named_bar_sync(3, kEpi);
+          float mh = -INFINITY;
+#pragma unroll
+          for (int q2 = 0; q2 < kParts; ++q2) mh = fmaxf(mh, s_rowx[q2 * 128 + row]);
+          named_bar_sync(3, kEpi);
+          cthr = __fsub_rd(__fsub_rd(mh, Bc), Bc);
+          mraw = -INFINITY;  // pass 1 collects the exact max
+        }
+        if (pass == max_pass) {
+          // the column parts of each row meet: exact row max, then scale once
           s_rowx[part * 128 + row] = mraw;
           named_bar_sync(3, kEpi);
 #pragma unroll
@@ -475,7 +636,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
       named_bar_sync(3, kEpi);
       if (ok && part == 0 && row_ok) {
         if (p.row_max) p.row_max[bh * p.Nq + (qp - p.qbase)] = m;
-        if (p.row_count && p.npass == 2) p.row_count[bh * p.Nq + (qp - p.qbase)] = cnt;
+        if (p.row_count && p.npass > kVotePass) p.row_count[bh * p.Nq + (qp - p.qbase)] = cnt;
       }
     }
   }
@@ -493,7 +654,107 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
   if (warp == 0) tmem_dealloc(tmem_base, 512);
 }
 
+// Screening operands of the screened select kernel: q16 = fp16(q_hi + q_lo) (saturated to
+// the fp16 range; the residual then only widens the bound), the row norms ||q16|| and
+// ||q' - q16|| (max over the DCA planes), k16 likewise and per kv head the maxima of the key
+// norms (kn zeroed by the caller).  One warp per query row (all planes) or per 32-key chunk;
+// lane l owns dims [l*E, l*E+E).
+template <int D>
+__global__ void __launch_bounds__(256)
+select_prep_kernel(const __nv_bfloat16* __restrict__ qh, const __nv_bfloat16* __restrict__ ql,
+                   int64_t qrows, int qplanes, const __nv_bfloat16* __restrict__ kh,
+                   const __nv_bfloat16* __restrict__ kl, int64_t BHk, int64_t N, int64_t nkc,
+                   __half* __restrict__ q16, __half* __restrict__ k16, float2* __restrict__ qn,
+                   float2* __restrict__ kn) {
+  constexpr int E = D / 32;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int l = threadIdx.x & 31;
+  // squared norms of the fp16 part and of the residual of one row, summed over the warp
+  auto row = [&](const __nv_bfloat16* h, const __nv_bfloat16* lo, __half* o, float& na, float& nr) {
+    __nv_bfloat16 a[E], b[E];
+    __half c[E];
+    if constexpr (E == 4) {
+      *reinterpret_cast<uint2*>(a) = *reinterpret_cast<const uint2*>(h + l * E);
+      *reinterpret_cast<uint2*>(b) = *reinterpret_cast<const uint2*>(lo + l * E);
+    } else {
+      *reinterpret_cast<uint32_t*>(a) = *reinterpret_cast<const uint32_t*>(h + l * E);
+      *reinterpret_cast<uint32_t*>(b) = *reinterpret_cast<const uint32_t*>(lo + l * E);
+    }
+    float sa = 0.f, sr = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float x = __fadd_rn(__bfloat162float(a[e]), __bfloat162float(b[e]));  // exact
+      const float xs = fminf(fmaxf(x, -65504.f), 65504.f);
+      c[e] = __float2half_rn(xs);
+      const float f = __half2float(c[e]);
+      const float r = __fsub_rn(x, f);
+      sa = __fmaf_ru(f, f, sa);
+      sr = __fmaf_ru(r, r, sr);
+    }
+    if constexpr (E == 4) *reinterpret_cast<uint2*>(o + l * E) = *reinterpret_cast<uint2*>(c);
+    else *reinterpret_cast<uint32_t*>(o + l * E) = *reinterpret_cast<uint32_t*>(c);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      sa = __fadd_ru(sa, __shfl_xor_sync(0xffffffffu, sa, off));
+      sr = __fadd_ru(sr, __shfl_xor_sync(0xffffffffu, sr, off));
+    }
+    na = __fsqrt_ru(sa);
+    nr = __fsqrt_ru(sr);
+  };
+  if (gw < qrows) {
+    float ma = 0.f, mr = 0.f;
+    for (int pl = 0; pl < qplanes; ++pl) {
+      const int64_t o = ((int64_t)pl * qrows + gw) * D;
+      float na, nr;
+      row(qh + o, ql + o, q16 + o, na, nr);
+      ma = fmaxf(ma, na);
+      mr = fmaxf(mr, nr);
+    }
+    if (l == 0) qn[gw] = make_float2(ma, mr);
+  } else if (gw < qrows + BHk * nkc) {
+    const int64_t c = gw - qrows, h = c / nkc, j0 = (c % nkc) * 32;
+    float ma = 0.f, mr = 0.f;
+    for (int64_t j = j0; j < j0 + 32 && j < N; ++j) {
+      const int64_t o = (h * N + j) * D;
+      float na, nr;
+      row(kh + o, kl + o, k16 + o, na, nr);
+      ma = fmaxf(ma, na);
+      mr = fmaxf(mr, nr);
+    }
+    if (l == 0) {  // norms are >= 0: their bit patterns order like the values
+      atomicMax(reinterpret_cast<int*>(&kn[h].x), __float_as_int(ma));
+      atomicMax(reinterpret_cast<int*>(&kn[h].y), __float_as_int(mr));
+    }
+  }
+}
+
+struct ScreenLayout {
+  size_t q16, k16, qn, kn, total;
+};
+
+ScreenLayout screen_layout(const sta_select_args* a) {
+  auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
+  const int64_t qplanes = a->dca_chunk_len > 0 ? 3 : 1;
+  const int64_t nq = a->n - a->q_pos_base;
+  const int64_t BH = a->batch * a->n_heads, BHk = a->batch * a->n_kv_heads;
+  ScreenLayout L{};
+  size_t o = 0;
+  L.q16 = o; o += al((size_t)qplanes * BH * nq * a->d * 2);
+  L.k16 = o; o += al((size_t)BHk * a->n * a->d * 2);
+  L.qn = o; o += al((size_t)BH * nq * 8);
+  L.kn = o; o += al((size_t)BHk * 8);
+  L.total = o;
+  return L;
+}
+
 }  // namespace
+
+size_t select_screen_bytes(const sta_select_args* a) {
+  if (!a || a->n <= 0 || a->batch <= 0 || a->n_heads <= 0 || a->n_kv_heads <= 0 ||
+      (a->d != 64 && a->d != 128) || a->q_pos_base < 0 || a->q_pos_base >= a->n)
+    return 0;
+  return screen_layout(a).total;
+}
 
 int launch_select(const sta_select_args* a, cudaStream_t stream) {
   if (!a || !a->q_hi || !a->q_lo || !a->k_hi || !a->k_lo || !a->tau)
@@ -552,23 +813,57 @@ int launch_select(const sta_select_args* a, cudaStream_t stream) {
     return fail(STA_ERR_UNSUPPORTED, "sta_select: block_max needs tile 32 and block_max_bn 32 or 64");
   if (p.dca_L > 0 && (p.dca_L % BN)) return fail(STA_ERR_UNSUPPORTED, "sta_select: DCA chunk_len must be a multiple of 256");
 
+  // Screened scoring needs the caller's scratch and plain (unweighted) votes: weighted votes
+  // use the score of every kept key, which the exact three-product kernel provides.
+  const bool scr = a->screen_ws != nullptr && p.wmode == 0;
+  CUtensorMap m_q16, m_k16;
+  if (scr) {
+    const ScreenLayout SL = screen_layout(a);
+    uint8_t* ws = static_cast<uint8_t*>(a->screen_ws);
+    if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0)
+      return fail(STA_ERR_ARG, "sta_select: screen_ws must be 256-byte aligned");
+    __half* q16 = reinterpret_cast<__half*>(ws + SL.q16);
+    __half* k16 = reinterpret_cast<__half*>(ws + SL.k16);
+    p.qh = static_cast<const __nv_bfloat16*>(a->q_hi);
+    p.ql = static_cast<const __nv_bfloat16*>(a->q_lo);
+    p.kh = static_cast<const __nv_bfloat16*>(a->k_hi);
+    p.kl = static_cast<const __nv_bfloat16*>(a->k_lo);
+    p.qnorm = reinterpret_cast<const float2*>(ws + SL.qn);
+    p.knorm = reinterpret_cast<const float2*>(ws + SL.kn);
+    p.nkc = (a->n + 31) / 32;
+    if (!make_tmap_bf16_3d(&m_q16, q16, a->d, nq, qplanes * BH, 64, BM) ||
+        !make_tmap_bf16_3d(&m_k16, k16, a->d, a->n, BHk, 64, BN))
+      return fail(STA_ERR_CUDA, "sta_select: cuTensorMapEncodeTiled failed");
+    const int64_t warps = BH * nq + BHk * p.nkc;
+    cudaMemsetAsync(ws + SL.kn, 0, (size_t)BHk * 8, stream);
+    const int64_t blocks = (warps + 7) / 8;
+    if (a->d == 128)
+      select_prep_kernel<128><<<(unsigned)blocks, 256, 0, stream>>>(
+          p.qh, p.ql, BH * nq, (int)qplanes, p.kh, p.kl, BHk, a->n, p.nkc, q16, k16,
+          reinterpret_cast<float2*>(ws + SL.qn), reinterpret_cast<float2*>(ws + SL.kn));
+    else
+      select_prep_kernel<64><<<(unsigned)blocks, 256, 0, stream>>>(
+          p.qh, p.ql, BH * nq, (int)qplanes, p.kh, p.kl, BHk, a->n, p.nkc, q16, k16,
+          reinterpret_cast<float2*>(ws + SL.qn), reinterpret_cast<float2*>(ws + SL.kn));
+    p.npass = a->max_only ? 2 : 3;
+  }
+
   int dev = 0, nsm = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   const int64_t total = BH * p.nqb;
   const int grid = (int)(total < nsm ? total : nsm);
   cudaError_t e;
-  if (a->d == 128) {
-    e = cudaFuncSetAttribute(select_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg<128>::SMEM);
-    if (e == cudaSuccess)
-      select_kernel<128><<<grid, kThreads, Cfg<128>::SMEM, stream>>>(m_qhi, m_qlo, m_khi, m_klo, p);
-  } else {
-    e = cudaFuncSetAttribute(select_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg<64>::SMEM);
-    if (e == cudaSuccess)
-      select_kernel<64><<<grid, kThreads, Cfg<64>::SMEM, stream>>>(m_qhi, m_qlo, m_khi, m_klo, p);
-  }
+  auto run = [&](auto kern, int smem) {
+    cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (r == cudaSuccess) {
+      if (scr) kern<<<grid, kThreads, smem, stream>>>(m_q16, m_qlo, m_k16, m_klo, p);
+      else kern<<<grid, kThreads, smem, stream>>>(m_qhi, m_qlo, m_khi, m_klo, p);
+    }
+    return r;
+  };
+  if (a->d == 128) e = scr ? run(select_kernel<128, true>, Cfg<128>::SMEM) : run(select_kernel<128, false>, Cfg<128>::SMEM);
+  else e = scr ? run(select_kernel<64, true>, Cfg<64>::SMEM) : run(select_kernel<64, false>, Cfg<64>::SMEM);
   if (e != cudaSuccess) return fail(STA_ERR_CUDA, cudaGetErrorString(e));
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(STA_ERR_CUDA, cudaGetErrorString(e));

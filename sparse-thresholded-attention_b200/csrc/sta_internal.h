@@ -27,6 +27,7 @@ int launch_rope_split(const void* x, int dtype, int64_t heads, int64_t N, int D,
                       int64_t tab_len = 0);
 
 int launch_select(const sta_select_args* a, cudaStream_t stream);
+size_t select_screen_bytes(const sta_select_args* a);
 int launch_rope_table(const float* inv_freq, int D, float rope_scale, float R, int64_t len,
                       void* out, cudaStream_t stream);
 int launch_build_sets(const sta_build_args* a, cudaStream_t stream);

@@ -30,7 +30,8 @@ class SelectArgs(ctypes.Structure):
                 ("tau", c_vp), ("max_only", c_i32), ("votes", c_vp), ("wvotes", c_vp),
                 ("bits", c_vp), ("row_max", c_vp), ("row_count", c_vp),
                 ("dca_chunk_len", c_i32), ("q_pos_base", c_i64),
-                ("block_max", c_vp), ("block_max_bn", c_i32), ("wait_limit_ns", ctypes.c_uint64)]
+                ("block_max", c_vp), ("block_max_bn", c_i32), ("wait_limit_ns", ctypes.c_uint64),
+                ("screen_ws", c_vp)]
 
 
 class BuildArgs(ctypes.Structure):
@@ -147,7 +148,7 @@ EXPORTED = ["sta_last_error", "sta_version", "sta_tri_head_stride", "sta_rope_sp
             "sta_shared_forward_static", "sta_build_sets_chunk", "sta_chunk_workspace_bytes",
             "sta_chunk_forward", "sta_rope_split_dca", "sta_rope_table", "sta_tri_head_stride_q",
             "sta_decode_workspace_bytes", "sta_decode_forward", "sta_dca_workspace_bytes",
-            "sta_dca_forward"]
+            "sta_dca_forward", "sta_select_screen_bytes"]
 
 _lib = None
 
@@ -197,6 +198,8 @@ def lib():
     L.sta_dca_workspace_bytes.argtypes = [ctypes.POINTER(DcaArgs)]
     L.sta_dca_forward.restype = ctypes.c_int
     L.sta_dca_forward.argtypes = [ctypes.POINTER(DcaArgs), c_vp, ctypes.c_size_t, c_vp]
+    L.sta_select_screen_bytes.restype = ctypes.c_size_t
+    L.sta_select_screen_bytes.argtypes = [ctypes.POINTER(SelectArgs)]
     L.sta_shared_forward_static.restype = ctypes.c_int
     L.sta_shared_forward_static.argtypes = [ctypes.POINTER(ForwardArgs), c_vp]
     L.sta_device_error.restype = ctypes.c_int

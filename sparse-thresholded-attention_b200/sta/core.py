@@ -448,11 +448,14 @@ def rope_split_dca(x: torch.Tensor, g: Geometry, role: int, out_hi=None, out_lo=
 
 
 def select(q: torch.Tensor, k: torch.Tensor, tau, g: Geometry, *, tile, sm_scale=None,
-           wmode=0, bits=False, max_only=False, wait_limit_ns=0):
+           wmode=0, bits=False, max_only=False, wait_limit_ns=0, screen=False):
     """Kernel A on raw (H,N,D) q and (Hkv,N,D) k.  Returns dict of compact votes / wvotes /
     bits, row_max (H,N) and row_count (H,N).  `wait_limit_ns` bounds every device-side wait
     (0: the library default); an expired wait shows in device_error(), not here.  With
-    ``g.dca`` the selection geometry is Dual Chunk Attention (three rotated query planes)."""
+    ``g.dca`` the selection geometry is Dual Chunk Attention (three rotated query planes).
+    ``screen`` (unweighted modes) scores with one fp16 product per pair and exact rescoring of
+    the pairs a proven bound leaves undecided (the forward entry points do so under
+    ``STA_SELECT_SCREEN=1``); the default scores every pair with three bf16 products."""
     H, N, D = q.shape
     Hk = k.shape[0]
     if sm_scale is None:
@@ -493,7 +496,13 @@ def select(q: torch.Tensor, k: torch.Tensor, tau, g: Geometry, *, tile, sm_scale
     a.row_count = res["row_count"].data_ptr()
     a.dca_chunk_len = dca_len
     a.wait_limit_ns = int(wait_limit_ns)
+    scr = None
+    if screen and not wmode:
+        nb = int(L.lib().sta_select_screen_bytes(ctypes.byref(a)))
+        scr = torch.empty((nb,), dtype=torch.uint8, device=dev)
+        a.screen_ws = scr.data_ptr()
     L.check(L.lib().sta_select(ctypes.byref(a), _stream()), "sta_select")
+    del scr  # freed after the launch: torch's caching allocator keeps stream order
     return res
 
 
