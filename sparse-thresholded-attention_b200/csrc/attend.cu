@@ -54,6 +54,14 @@ struct AttendP {
 // tensor-core work.  Stage hand-off: named barriers FULL(s) (producers arrive, consumers wait)
 // and EMPTY(s) (consumers arrive, producers wait).
 constexpr int NPW = 4;
+
+// 16-byte asynchronous global -> shared copy; src_bytes 0 zero-fills the destination
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 constexpr int kBarFull = 1, kBarEmpty = 3, kBarProd = 5;
 
 template <int D, int T, bool F32>
@@ -126,29 +134,45 @@ gather_attend_kernel(const AttendP p) {
   if (warp >= NCW) {
     // ================================================================ producers
     const int ptid = tid - NCW * 32;
+    // slot metadata of the next block is fetched into registers while the current block's
+    // rows are gathered, so each block pays one global round trip instead of two
+    int nid = (int)N, nmk = -1;
+    float nnp = 0.f;
+    auto fetch = [&](int ib) {
+      const int slot = ib * BK + ptid;
+      nid = (int)N;
+      nnp = 0.f;
+      nmk = -1;
+      if (ptid < BK && slot < p.k_max) {
+        nid = idx_row[slot];
+        nnp = npk_row[slot];
+        if (use_mask) nmk = mask_row[slot];
+      }
+    };
+    fetch(0);
     for (int ib = 0; ib < nblocks; ++ib) {
       const int st = ib & 1;
       if (ib >= 2) named_bar_sync(kBarEmpty + st, NTH);
       int* mIdx = sIdx + st * BK;
       float* mNpk = sNpk + st * BK;
       int* mMask = sMask + st * BK;
-      for (int i = ptid; i < BK; i += NPW * 32) {
-        const int slot = ib * BK + i;
-        int id = (int)N;
-        float np = 0.f;
-        int mk = -1;
-        if (slot < p.k_max) {
-          id = idx_row[slot];
-          if (id < N) np = npk_row[slot];
-          if (use_mask) mk = mask_row[slot];
-        }
-        mIdx[i] = id;
-        mNpk[i] = np;
-        mMask[i] = mk;
+      if (ptid < BK) {
+        mIdx[ptid] = nid;
+        mNpk[ptid] = nid < N ? nnp : 0.f;
+        mMask[ptid] = nmk;
       }
       named_bar_sync(kBarProd, NPW * 32);
+      if (ib + 1 < nblocks) fetch(ib + 1);
       __nv_bfloat16* kdst = sK + st * C::KST;
       __nv_bfloat16* vdst = sV + st * C::VST;
+      if (!F32) {
+        // V rows need no transform: asynchronous copies overlap the K rotations below
+        for (int it = ptid; it < BK * (D / 8); it += NPW * 32) {
+          const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
+          const int id = mIdx[i];
+          cp_async16(vdst + i * LD + d0, vg + (int64_t)(id < N ? id : 0) * p.vsn + d0, id < N ? 16 : 0);
+        }
+      }
       for (int it = ptid; it < BK * C8; it += NPW * 32) {
         const int i = it / C8, f0 = (it % C8) * 8;
         const int id = mIdx[i];
@@ -161,15 +185,11 @@ gather_attend_kernel(const AttendP p) {
                             p.rope_scale, dst, BK * LD, p.rtab, table_index(pos, p.rtab_R, p.rtab_len));
         }
       }
-      for (int it = ptid; it < BK * (D / 8); it += NPW * 32) {
-        const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
-        const int id = mIdx[i];
-        __nv_bfloat16* dst = vdst + i * LD + d0;
-        if (!F32) {
-          uint4 u = make_uint4(0u, 0u, 0u, 0u);
-          if (id < N) u = *reinterpret_cast<const uint4*>(vg + (int64_t)id * p.vsn + d0);
-          *reinterpret_cast<uint4*>(dst) = u;
-        } else {
+      if (F32) {
+        for (int it = ptid; it < BK * (D / 8); it += NPW * 32) {
+          const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
+          const int id = mIdx[i];
+          __nv_bfloat16* dst = vdst + i * LD + d0;
           float x[8];
           if (id < N) {
             load8(vg + (int64_t)id * p.vsn + d0, x);
@@ -185,6 +205,8 @@ gather_attend_kernel(const AttendP p) {
             for (int j = 0; j < NV; ++j) dst[j * BK * LD + u] = a[j];
           }
         }
+      } else {
+        cp_async_wait_all();
       }
       named_bar_arrive(kBarFull + st, NTH);
     }

@@ -31,6 +31,9 @@ namespace {
 constexpr int BM = 128;       // query rows per item == TMEM lanes
 constexpr int BN = 256;       // keys per block == MMA N
 constexpr int NACC = 2;       // accumulator slots (2 x 256 fp32 columns = all 512 TMEM columns)
+#ifndef STA_SELECT_PREFETCH_PARTS
+#define STA_SELECT_PREFETCH_PARTS 2
+#endif
 #ifndef STA_SELECT_EPI_WARPS
 #define STA_SELECT_EPI_WARPS 16
 #endif
@@ -448,7 +451,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + slot * BN;
             // with 8 epilogue warps the next chunk's load is kept in flight (vn); with 16 the
             // other warps of the quadrant hide its latency and the registers go to occupancy
-            constexpr bool kPrefetch = kParts <= 2;
+            constexpr bool kPrefetch = kParts <= STA_SELECT_PREFETCH_PARTS;
             float v[32], vn[32];  // vn unused (eliminated) without prefetch
             tmem_ld32(taddr + part * (BN / kParts), v);
             tmem_wait_ld();
