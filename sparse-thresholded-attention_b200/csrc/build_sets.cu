@@ -156,10 +156,41 @@ __device__ void radix_kth_largest(const SetRow& r, int64_t N, bool weighted, int
     for (int i = threadIdx.x; i < 256; i += kBT) hist[i] = 0u;
     __syncthreads();
     const uint32_t prefix = s_prefix;
-    for (int64_t j = threadIdx.x; j < r.hi; j += kBT) {
-      if (cand_only && (r.v[j] == 0 || F.has(j))) continue;
+    auto count = [&](int64_t j) {
       const uint32_t key = __float_as_uint(rank_value(r, j, weighted));
       if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    };
+    if (cand_only && (reinterpret_cast<uintptr_t>(r.v) & 7u) == 0) {
+      // candidates have a nonzero vote: 8 votes per load, four loads in flight, all-zero
+      // words skipped (the union is sparse)
+      const int64_t nw = r.hi / 8;
+      const uint2* vw = reinterpret_cast<const uint2*>(r.v);
+      for (int64_t w0 = threadIdx.x; w0 < nw; w0 += 4 * kBT) {
+        uint2 u4[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int64_t w = w0 + (int64_t)q * kBT;
+          u4[q] = w < nw ? vw[w] : make_uint2(0u, 0u);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint2 u = u4[q];
+          if ((u.x | u.y) == 0u) continue;
+          const int64_t jb = (w0 + (int64_t)q * kBT) * 8;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int64_t j = jb + i;
+            if ((((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 255u) && !F.has(j)) count(j);
+          }
+        }
+      }
+      for (int64_t j = nw * 8 + threadIdx.x; j < r.hi; j += kBT)
+        if (r.v[j] != 0 && !F.has(j)) count(j);
+    } else {
+      for (int64_t j = threadIdx.x; j < r.hi; j += kBT) {
+        if (cand_only && (r.v[j] == 0 || F.has(j))) continue;
+        count(j);
+      }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -240,18 +271,28 @@ __global__ void __launch_bounds__(kBT) build_sets_kernel(const BuildP p) {
   int nz = 0;
   int64_t j_tail = 0;
   if ((reinterpret_cast<uintptr_t>(r.v) & 7u) == 0) {
-    // 8 votes per load; most keys have none, so all-zero words are skipped
+    // 8 votes per load, four loads in flight per thread; most keys have none, so all-zero
+    // words are skipped
     const int64_t nw = r.hi / 8;
     const uint2* vw = reinterpret_cast<const uint2*>(r.v);
-    for (int64_t w = tid; w < nw; w += kBT) {
-      const uint2 u = vw[w];
-      if ((u.x | u.y) == 0u) continue;
+    for (int64_t w0 = tid; w0 < nw; w0 += 4 * kBT) {
+      uint2 u4[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint32_t v = ((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 255u;
-        if (v) {
-          ++nz;
-          if (!weighted) atomicAdd(&hist[v], 1u);
+      for (int q = 0; q < 4; ++q) {
+        const int64_t w = w0 + (int64_t)q * kBT;
+        u4[q] = w < nw ? vw[w] : make_uint2(0u, 0u);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint2 u = u4[q];
+        if ((u.x | u.y) == 0u) continue;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t v = ((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 255u;
+          if (v) {
+            ++nz;
+            if (!weighted) atomicAdd(&hist[v], 1u);
+          }
         }
       }
     }
@@ -368,18 +409,28 @@ __global__ void __launch_bounds__(kBT) build_sets_kernel(const BuildP p) {
   // (Positions of keys that are not kept are only read for the tile's queries, which the local
   // window keeps whenever n_local >= 1.)
   const bool identity = p.pos_scale == 1.f && p.n_local >= 1;
+  // the thread's kItems consecutive votes packed in 8 bytes: one 8-byte load where aligned and
+  // in range; the next chunk's word is loaded while the current chunk is scanned
+  auto load_votes = [&](int64_t j0) -> uint2 {
+    if (j0 + kItems <= r.hi && ((reinterpret_cast<uintptr_t>(r.v + j0) & 7u) == 0))
+      return *reinterpret_cast<const uint2*>(r.v + j0);
+    uint32_t x = 0u, y = 0u;
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      const uint32_t b = j0 + i < r.hi ? (uint32_t)r.v[j0 + i] : 0u;
+      if (i < 4) x |= b << (8 * i);
+      else y |= b << (8 * (i - 4));
+    }
+    return make_uint2(x, y);
+  };
+  uint2 u_next = load_votes((int64_t)tid * kItems);
   for (int64_t c0 = 0; c0 < E; c0 += kChunk) {
     const int64_t j0 = c0 + (int64_t)tid * kItems;
-    // the thread's kItems consecutive votes, one 8-byte load where aligned and in range
+    const uint2 u = u_next;
+    if (c0 + kChunk < E) u_next = load_votes(j0 + kChunk);
     uint32_t vb[kItems];
-    if (j0 + kItems <= r.hi && ((reinterpret_cast<uintptr_t>(r.v + j0) & 7u) == 0)) {
-      const uint2 u = *reinterpret_cast<const uint2*>(r.v + j0);
 #pragma unroll
-      for (int i = 0; i < kItems; ++i) vb[i] = ((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 255u;
-    } else {
-#pragma unroll
-      for (int i = 0; i < kItems; ++i) vb[i] = j0 + i < r.hi ? r.v[j0 + i] : 0u;
-    }
+    for (int i = 0; i < kItems; ++i) vb[i] = ((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 255u;
     uint32_t flags = 0;
 #pragma unroll
     for (int i = 0; i < kItems; ++i) {
@@ -487,17 +538,28 @@ __global__ void __launch_bounds__(kBT) build_sets_pq_kernel(const BuildPQP p) {
 
   int nu = 0, nfu = 0;
   if ((reinterpret_cast<uintptr_t>(r.v) & 7u) == 0) {
-    // 8 votes per load; the union is sparse, so only nonzero words are looked at
+    // 8 votes per load, four loads in flight; the union is sparse, so only nonzero words are
+    // looked at
     const int64_t nw = r.hi / 8;
     const uint2* vw = reinterpret_cast<const uint2*>(r.v);
-    for (int64_t w = tid; w < nw; w += kBT) {
-      const uint2 u = vw[w];
-      if ((u.x | u.y) == 0u) continue;
+    for (int64_t w0 = tid; w0 < nw; w0 += 4 * kBT) {
+      uint2 u4[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 255u) {
-          ++nu;
-          if (F.has(w * 8 + i)) ++nfu;
+      for (int q = 0; q < 4; ++q) {
+        const int64_t w = w0 + (int64_t)q * kBT;
+        u4[q] = w < nw ? vw[w] : make_uint2(0u, 0u);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint2 u = u4[q];
+        if ((u.x | u.y) == 0u) continue;
+        const int64_t w = w0 + (int64_t)q * kBT;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 255u) {
+            ++nu;
+            if (F.has(w * 8 + i)) ++nfu;
+          }
         }
       }
     }
@@ -544,18 +606,28 @@ __global__ void __launch_bounds__(kBT) build_sets_pq_kernel(const BuildPQP p) {
   float* npq_row = p.newpos_q + nt_row * T;
   int32_t* mask_row = p.mask + nt_row * p.k_max;
   int64_t carry = 0, tie_carry = 0;
+  // the thread's kItems consecutive votes packed in 8 bytes (one 8-byte load where aligned and
+  // in range); the next chunk's word is loaded while the current chunk is processed
+  auto load_votes = [&](int64_t j0) -> uint2 {
+    if (j0 + kItems <= r.hi && ((reinterpret_cast<uintptr_t>(r.v + j0) & 7u) == 0))
+      return *reinterpret_cast<const uint2*>(r.v + j0);
+    uint32_t x = 0u, y = 0u;
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      const uint32_t b = j0 + i < r.hi ? (uint32_t)r.v[j0 + i] : 0u;
+      if (i < 4) x |= b << (8 * i);
+      else y |= b << (8 * (i - 4));
+    }
+    return make_uint2(x, y);
+  };
+  uint2 u_next = load_votes((int64_t)tid * kItems);
   for (int64_t c0 = 0; c0 < E; c0 += kChunk) {
     const int64_t j0 = c0 + (int64_t)tid * kItems;
-    // the thread's kItems consecutive votes, one 8-byte load where aligned and in range
+    const uint2 u = u_next;
+    if (c0 + kChunk < E) u_next = load_votes(j0 + kChunk);
     uint32_t vb8[kItems];
-    if (j0 + kItems <= r.hi && ((reinterpret_cast<uintptr_t>(r.v + j0) & 7u) == 0)) {
-      const uint2 u = *reinterpret_cast<const uint2*>(r.v + j0);
 #pragma unroll
-      for (int i = 0; i < kItems; ++i) vb8[i] = ((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 255u;
-    } else {
-#pragma unroll
-      for (int i = 0; i < kItems; ++i) vb8[i] = j0 + i < r.hi ? r.v[j0 + i] : 0u;
-    }
+    for (int i = 0; i < kItems; ++i) vb8[i] = ((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 255u;
     uint32_t flags = 0, tie = 0, sure = 0;
 #pragma unroll
     for (int i = 0; i < kItems; ++i) {
