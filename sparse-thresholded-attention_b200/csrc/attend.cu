@@ -92,8 +92,10 @@ gather_attend_kernel(const AttendP p) {
   float* sNpk = reinterpret_cast<float*>(sIdx + 2 * BK);          // [2][BK]
   int* sMask = reinterpret_cast<int*>(sNpk + 2 * BK);             // [2][BK]
 
-  const int t = blockIdx.x;
-  const int64_t bh = blockIdx.y;
+  // grid (heads, tiles) with the tile index reversed: the last tiles of every head, which hold
+  // the most kept slots, start first and the short early tiles fill the tail
+  const int t = (int)(p.nt - 1 - blockIdx.y);
+  const int64_t bh = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t N = p.N;
   const int64_t kvh = (bh / p.H) * p.Hkv + (bh % p.H) / (p.H / p.Hkv);
@@ -179,7 +181,13 @@ gather_attend_kernel(const AttendP p) {
         const float pos = mNpk[i];
         __nv_bfloat16* dst = kdst + i * LD;
         if (direct && id < N && pos == __fmul_rn((float)id, p.ps_sel)) {
-          copy_rotated<HALF>(p.kh + (kvh * N + id) * D, p.kl + (kvh * N + id) * D, f0, dst, BK * LD);
+          // the pre-rotated row is bit-identical: asynchronous copies of its hi / lo pieces
+          const __nv_bfloat16* h = p.kh + (kvh * N + id) * D;
+          const __nv_bfloat16* l = p.kl + (kvh * N + id) * D;
+          cp_async16(dst + f0, h + f0, 16);
+          cp_async16(dst + f0 + HALF, h + f0 + HALF, 16);
+          cp_async16(dst + BK * LD + f0, l + f0, 16);
+          cp_async16(dst + BK * LD + f0 + HALF, l + f0 + HALF, 16);
         } else {
           rotate8<NQ, HALF>(kg + (int64_t)(id < N ? id : 0) * p.ksn, id < N, f0, pos, p.inv_freq,
                             p.rope_scale, dst, BK * LD, p.rtab, table_index(pos, p.rtab_R, p.rtab_len));
@@ -368,7 +376,7 @@ int launch_one(const AttendP& p, cudaStream_t stream) {
   auto kern = gather_attend_kernel<D, T, F32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
   if (e != cudaSuccess) return fail(STA_ERR_CUDA, cudaGetErrorString(e));
-  dim3 grid((unsigned)p.nt, (unsigned)p.BH);
+  dim3 grid((unsigned)p.BH, (unsigned)p.nt);
   kern<<<grid, C::NTH, C::SMEM, stream>>>(p);
   e = cudaGetLastError();
   return e == cudaSuccess ? STA_OK : fail(STA_ERR_CUDA, cudaGetErrorString(e));
@@ -430,7 +438,7 @@ int launch_gather_attend(const sta_attend_args* a, cudaStream_t stream) {
   p.rtab = static_cast<const float2*>(a->rope_table);
   p.rtab_R = a->rope_table_R;
   p.rtab_len = a->rope_table ? a->rope_table_len : 0;
-  if (p.BH > 65535) return fail(STA_ERR_UNSUPPORTED, "sta_gather_attend: too many heads");
+  if (p.nt > 65535) return fail(STA_ERR_UNSUPPORTED, "sta_gather_attend: too many query tiles");
   const bool f32 = a->dtype == STA_DTYPE_F32;
   if (a->d == 128) {
     if (a->tile == 64) return f32 ? launch_one<128, 64, true>(p, stream) : launch_one<128, 64, false>(p, stream);

@@ -590,10 +590,13 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
             // warps of one tile's quadrants meet at their own barrier (ids 4, 5)
             const int g = quad / quads_per_tile;                 // == tile of the item
             named_bar_sync(4 + g, quads_per_tile * kParts * 32);
-            const int col = (part * quads_per_tile + quad % quads_per_tile) * 32 + lane;
             const int64_t tg = q0 / p.T + g;
-            const int64_t kj = (int64_t)kb * BN + col;
-            if (ok && col < BN && tg < nt && kj < min((tg + 1) * (int64_t)p.T, p.N)) {
+            // the tile's quads_per_tile * kParts warps cover the block's columns (one pass with
+            // 16 epilogue warps and 64-query tiles)
+            for (int col = (part * quads_per_tile + quad % quads_per_tile) * 32 + lane; col < BN;
+                 col += quads_per_tile * kParts * 32) {
+              const int64_t kj = (int64_t)kb * BN + col;
+              if (!(ok && tg < nt && kj < min((tg + 1) * (int64_t)p.T, p.N))) continue;
               uint32_t vs = 0;
               float wsum = 0.f;
               for (int qq = g * quads_per_tile; qq < (g + 1) * quads_per_tile; ++qq) {
