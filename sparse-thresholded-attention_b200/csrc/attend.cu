@@ -54,14 +54,6 @@ struct AttendP {
 // tensor-core work.  Stage hand-off: named barriers FULL(s) (producers arrive, consumers wait)
 // and EMPTY(s) (consumers arrive, producers wait).
 constexpr int NPW = 4;
-
-// 16-byte asynchronous global -> shared copy; src_bytes 0 zero-fills the destination
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src),
-               "r"(src_bytes)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 constexpr int kBarFull = 1, kBarEmpty = 3, kBarProd = 5;
 
 template <int D, int T, bool F32>

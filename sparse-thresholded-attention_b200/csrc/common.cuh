@@ -264,6 +264,14 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
          | ((uint32_t)(M >> 4) << 24);      // M / 16
 }
 
+// 16-byte asynchronous global -> shared copy (no register staging); src_bytes 0 zero-fills
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 // ------------------------------------------------------------------------------------------
 // misc
 // ------------------------------------------------------------------------------------------

@@ -245,6 +245,14 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
   // attend one batch of SB pending slots (fewer at the end: the rest are padding, masked):
   // every thread stages rotated K / V, then pair p scores slots [SP*p, SP*p + SP) for all rows
   auto attend_batch = [&](int nb) {
+    if (!F32) {
+      // V rows need no transform: asynchronous copies overlap the K rotations below
+      for (int it = tid; it < SB * (D / 8); it += NTH) {
+        const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
+        const int64_t j = i < nb ? s_sj[i] : 0;
+        cp_async16(sV + (i / SP) * VBUF + (i % SP) * LD + d0, vg + j * p.vsn + d0, i < nb ? 16 : 0);
+      }
+    }
     for (int it = tid; it < SB * (HALF / 8); it += NTH) {
       const int i = it / (HALF / 8), f0 = (it % (HALF / 8)) * 8;
       const int64_t j = i < nb ? s_sj[i] : 0;
@@ -253,15 +261,11 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
       rotate8<NQ, HALF>(kg + j * p.ksn, i < nb, f0, npk, p.inv_freq_c, 1.f, dst, SP * LD, p.rtab,
                         table_index(npk, p.rtab_R, p.rtab_len));
     }
-    for (int it = tid; it < SB * (D / 8); it += NTH) {
+    for (int it = tid; F32 && it < SB * (D / 8); it += NTH) {
       const int i = it / (D / 8), d0 = (it % (D / 8)) * 8;
       const int64_t j = i < nb ? s_sj[i] : 0;
       __nv_bfloat16* dst = sV + (i / SP) * VBUF + (i % SP) * LD + d0;
-      if (!F32) {
-        uint4 u = make_uint4(0u, 0u, 0u, 0u);
-        if (i < nb) u = *reinterpret_cast<const uint4*>(vg + j * p.vsn + d0);
-        *reinterpret_cast<uint4*>(dst) = u;
-      } else {
+      {
         float x[8];
         if (i < nb) {
           load8(vg + j * p.vsn + d0, x);
@@ -278,6 +282,7 @@ __global__ void __launch_bounds__(NTH) pqstream_kernel(const PQSP p) {
         }
       }
     }
+    if (!F32) cp_async_wait_all();
     __syncthreads();
     float s[SP / 8][4];
     score_tile<D, SP, NQ>(sQa, myK, s, rw);
