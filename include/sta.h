@@ -48,8 +48,8 @@ extern "C" {
  * Library
  * ------------------------------------------------------------------------------------- */
 const char* sta_last_error(void);
-/* ABI version: 4 (2: query slabs, PQ-Stream pass 2 on Kernel A keep bits, decode; 3: select wait
- * limit; 4: screened select scoring, sta_select_args.screen_ws) */
+/* ABI version: 5 (2: query slabs, PQ-Stream pass 2 on Kernel A keep bits, decode; 3: select wait
+ * limit; 4: screened select scoring, sta_select_args.screen_ws; 5: vote histograms) */
 int sta_version(void);
 /* Number of elements of one head of a compact selection array. */
 int64_t sta_tri_head_stride(int64_t n, int32_t tile);
@@ -137,6 +137,10 @@ typedef struct sta_select_args {
    * the pace, and screening adds a third epilogue pass); the forward entry points use
    * screening only when STA_SELECT_SCREEN=1 is set in the environment. */
   void* screen_ws;
+  /* optional (tile 64 or 128, votes): per (head, local tile) the histogram of the tile's
+   * nonzero vote values, (batch*n_heads, nt, tile + 1) uint32, bin v = number of keys with
+   * vote v (bin 0 is left 0).  sta_build_args.vote_hist consumes it. */
+  uint32_t* vote_hist;
 } sta_select_args;
 
 int sta_select(const sta_select_args* a, void* stream);
@@ -172,6 +176,10 @@ typedef struct sta_build_args {
   uint8_t* overflow20;     /* (heads, nt) still over k_max at the floor percentage */
   int64_t q_pos_base;      /* first query position (the reference's q_pos_base, shared_selection_triton_exact_2.py:291);
                             * nt = ceil((n - q_pos_base) / tile) local tiles */
+  /* optional (select_score FREQ): the vote histograms sta_select wrote (vote_hist); the union
+   * size and the frequency order statistic then come from them instead of a pass over the
+   * votes.  NULL: computed from the votes. */
+  const uint32_t* vote_hist;
 } sta_build_args;
 
 int sta_build_sets(const sta_build_args* a, void* stream);

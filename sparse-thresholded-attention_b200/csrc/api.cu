@@ -95,6 +95,7 @@ struct Layout {
   int64_t c;          // kv heads per group
   size_t qh, ql, kh, kl, votes, wvotes, bits, idx, npk, npq, mask, rowcnt, bmax, rtab, stab, total;
   size_t scr, scr_len;  // screened-select scratch (0 length: exact three-product scoring)
+  size_t vhist;         // per-tile vote histograms (shared path, frequency ranking) or 0
   float rtab_R, stab_R;
   int64_t rtab_len, stab_len;
   bool stab_shared;  // the selection table is the attend table
@@ -147,6 +148,8 @@ Layout layout_for(const sta_forward_args* a, Variant v, int64_t c) {
     L.npk = take(qh * nt * (int64_t)a->k_max * 4);
     L.npq = take(qh * nt * T * 4);
     if (v == kPQUnion) L.mask = take(qh * nt * (int64_t)a->k_max * 4);
+    if (v == kShared && a->select_score == STA_SCORE_FREQ && T != 32)
+      L.vhist = take(qh * nt * (T + 1) * 4);
   }
   // cos/sin table of the attend geometry: integer dense ranks (PQ-Union, chunk) or PI positions
   // at a power-of-two fraction (shared path with pos_scale_c in {1, 1/2, 1/4})
@@ -383,6 +386,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
       s.votes = w + L.votes;
       s.wvotes = a->select_score != STA_SCORE_FREQ ? reinterpret_cast<float*>(w + L.wvotes) : nullptr;
       s.bits = v == kPQUnion ? reinterpret_cast<uint32_t*>(w + L.bits) : nullptr;
+      s.vote_hist = L.vhist ? reinterpret_cast<uint32_t*>(w + L.vhist) : nullptr;
       STA_TRY(launch_select(&s, st));
       mark(2);
       int32_t* idx = a->idx_out ? a->idx_out + h0 * nt * kmax : reinterpret_cast<int32_t*>(w + L.idx);
@@ -393,6 +397,7 @@ int run_forward(const sta_forward_args* a, Variant v, void* ws, size_t ws_len, c
         sta_build_args ba{};
         ba.votes = w + L.votes;
         ba.wvotes = s.wvotes;
+        ba.vote_hist = s.vote_hist;
         ba.heads = qn;
         ba.n = N;
         ba.tile = T;
@@ -511,7 +516,7 @@ extern "C" {
 
 const char* sta_last_error(void) { return g_last_error; }
 
-int sta_version(void) { return 4; }
+int sta_version(void) { return 5; }
 
 int64_t sta_tri_head_stride(int64_t n, int32_t tile) { return tri_head_stride(n, tile); }
 

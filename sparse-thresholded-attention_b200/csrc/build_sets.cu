@@ -239,6 +239,7 @@ struct BuildP {
   uint8_t* overflow;
   int32_t* kpct_meas;
   uint8_t* overflow20;
+  const uint32_t* vote_hist;
 };
 
 __global__ void __launch_bounds__(kBT) build_sets_kernel(const BuildP p) {
@@ -265,12 +266,17 @@ __global__ void __launch_bounds__(kBT) build_sets_kernel(const BuildP p) {
   __shared__ uint32_t s_cut;
   __shared__ int64_t s_ge;
 
-  // ---- union size and (frequency ranking) vote histogram over bins 0..T
-  for (int i = tid; i < 256; i += kBT) hist[i] = 0u;
+  // ---- union size and (frequency ranking) vote histogram over bins 0..T: from the select
+  // kernel's histograms when given, else one pass over the votes
+  const uint32_t* vh = (!weighted && p.vote_hist) ? p.vote_hist + (bh * p.nt + t) * (T + 1) : nullptr;
+  for (int i = tid; i < 256; i += kBT) hist[i] = (vh && i >= 1 && i <= T) ? vh[i] : 0u;
   __syncthreads();
   int nz = 0;
-  int64_t j_tail = 0;
-  if ((reinterpret_cast<uintptr_t>(r.v) & 7u) == 0) {
+  int64_t j_tail = vh ? r.hi : 0;
+  if (vh) {
+    for (int i = tid; i <= T; i += kBT)
+      if (i >= 1) nz += (int)hist[i];
+  } else if ((reinterpret_cast<uintptr_t>(r.v) & 7u) == 0) {
     // 8 votes per load, four loads in flight per thread; most keys have none, so all-zero
     // words are skipped
     const int64_t nw = r.hi / 8;
@@ -968,6 +974,7 @@ int launch_build_sets(const sta_build_args* a, cudaStream_t stream) {
   p.chosen = a->chosen;
   p.overflow = a->overflow;
   p.kpct_meas = a->kpct_meas;
+  p.vote_hist = a->vote_hist;
   p.overflow20 = a->overflow20;
   if (p.nt > 0x7fffffff || p.BH > 65535) return fail(STA_ERR_UNSUPPORTED, "sta_build_sets: grid");
   dim3 grid((unsigned)p.nt, (unsigned)p.BH);

@@ -52,7 +52,9 @@ struct Cfg {
   static constexpr int STAGE_BYTES = NC * kKTileBytes;
   static constexpr int NSTAGE = (D == 64) ? 4 : 2;
   static constexpr int RED_WORDS = 2 * 4 * BN;   // [buffer][quadrant][column]
-  static constexpr int SMEM = 1024 + Q_BYTES + NSTAGE * STAGE_BYTES + 2 * RED_WORDS * 4 + 2 * kEpi * 4 + 512;
+  static constexpr int HIST_WORDS = 2 * 65;     // per-tile vote histograms of an item (T 64 / 128)
+  static constexpr int SMEM = 1024 + Q_BYTES + NSTAGE * STAGE_BYTES + 2 * RED_WORDS * 4 + 2 * kEpi * 4 +
+                              HIST_WORDS * 4 + 512;
 };
 
 struct Params {
@@ -80,6 +82,7 @@ struct Params {
   int bmax_bn;
   int64_t bmax_head_stride;
   uint64_t limit_ns;    // bound of every mbarrier wait
+  uint32_t* vote_hist;  // (BH, nt local, T + 1) nonzero-vote histograms (T 64 / 128) or null
   // screened scoring (SCR kernels): canonical bf16 pieces for exact recomputation, per-row
   // query norms and per-32-key-chunk key norm maxima of the fp16 screening operands
   const __nv_bfloat16 *qh, *ql, *kh, *kl;
@@ -230,7 +233,8 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
   float* s_w = reinterpret_cast<float*>(s_vote + C::RED_WORDS);
   float* s_rowx = s_w + C::RED_WORDS;                                  // [kParts][128 rows]
   int* s_rowc = reinterpret_cast<int*>(s_rowx + kEpi);                  // [kParts][128 rows]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_rowc + kEpi);
+  uint32_t* s_hist = reinterpret_cast<uint32_t*>(s_rowc + kEpi);       // [BM / T][T + 1]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_hist + C::HIST_WORDS);
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 1;
   uint64_t* k_full = bars + 2;
@@ -434,6 +438,13 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
       int cnt = 0;
       for (int pass = 0; pass < p.npass; ++pass) {
         if (pass == kVotePass) {
+          if (p.vote_hist && p.T != 32) {
+            // this thread's bin of its tile's histogram (ordered before the first atomics by the
+            // tile's combine barrier)
+            const int g = quad / quads_per_tile;
+            const int ti = (part * quads_per_tile + quad % quads_per_tile) * 32 + lane;
+            if (ti <= p.T) s_hist[g * (p.T + 1) + ti] = 0u;
+          }
           thr = __fsub_rn(m, tau_h);
           thr_raw = row_ok ? raw_threshold(thr, p.sm_scale) : INFINITY;
           // covers the rounding of thr_raw +- Bc
@@ -608,6 +619,7 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
                   bh * p.head_stride + tri_tile_offset(tg - p.qbase / p.T, p.T, p.qbase) + kj;
               if (p.votes) p.votes[off] = (uint8_t)vs;
               if (p.wmode != 0 && p.wvotes) p.wvotes[off] = wsum;
+              if (p.vote_hist && vs) atomicAdd(&s_hist[g * (p.T + 1) + vs], 1u);
             }
             rb ^= 1;
           }
@@ -643,6 +655,15 @@ select_kernel(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant_
       if (ok && part == 0 && row_ok) {
         if (p.row_max) p.row_max[bh * p.Nq + (qp - p.qbase)] = m;
         if (p.row_count && p.npass > kVotePass) p.row_count[bh * p.Nq + (qp - p.qbase)] = cnt;
+      }
+      if (p.vote_hist && p.T != 32 && p.npass > kVotePass) {
+        // the same thread that zeroed a bin flushes it (the barrier above ordered the atomics)
+        const int g = quad / quads_per_tile;
+        const int ti = (part * quads_per_tile + quad % quads_per_tile) * 32 + lane;
+        const int64_t tg = q0 / p.T + g;
+        if (ok && ti <= p.T && tg < nt)
+          p.vote_hist[(bh * ((p.Nq + p.T - 1) / p.T) + (tg - p.qbase / p.T)) * (p.T + 1) + ti] =
+              s_hist[g * (p.T + 1) + ti];
       }
     }
   }
@@ -815,6 +836,7 @@ int launch_select(const sta_select_args* a, cudaStream_t stream) {
   p.bmax_bn = a->block_max_bn;
   p.bmax_head_stride = tri_head_stride((a->n + 31) / 32, 1, a->q_pos_base / 32);
   p.limit_ns = a->wait_limit_ns > 0 ? a->wait_limit_ns : 4000000000ull;
+  p.vote_hist = (a->max_only || !a->votes || a->tile == 32) ? nullptr : a->vote_hist;
   if (p.block_max && (a->tile != 32 || (p.bmax_bn != 32 && p.bmax_bn != 64)))
     return fail(STA_ERR_UNSUPPORTED, "sta_select: block_max needs tile 32 and block_max_bn 32 or 64");
   if (p.dca_L > 0 && (p.dca_L % BN)) return fail(STA_ERR_UNSUPPORTED, "sta_select: DCA chunk_len must be a multiple of 256");

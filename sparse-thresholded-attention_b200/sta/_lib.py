@@ -31,7 +31,7 @@ class SelectArgs(ctypes.Structure):
                 ("bits", c_vp), ("row_max", c_vp), ("row_count", c_vp),
                 ("dca_chunk_len", c_i32), ("q_pos_base", c_i64),
                 ("block_max", c_vp), ("block_max_bn", c_i32), ("wait_limit_ns", ctypes.c_uint64),
-                ("screen_ws", c_vp)]
+                ("screen_ws", c_vp), ("vote_hist", c_vp)]
 
 
 class BuildArgs(ctypes.Structure):
@@ -41,7 +41,7 @@ class BuildArgs(ctypes.Structure):
                 ("measure", c_i32), ("idx", c_vp), ("newpos_k", c_vp), ("newpos_q", c_vp),
                 ("shared_size", c_vp), ("kept_size", c_vp), ("chosen", c_vp),
                 ("overflow", c_vp), ("kpct_meas", c_vp), ("overflow20", c_vp),
-                ("q_pos_base", c_i64)]
+                ("q_pos_base", c_i64), ("vote_hist", c_vp)]
 
 
 class BuildPQArgs(ctypes.Structure):

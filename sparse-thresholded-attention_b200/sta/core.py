@@ -448,14 +448,16 @@ def rope_split_dca(x: torch.Tensor, g: Geometry, role: int, out_hi=None, out_lo=
 
 
 def select(q: torch.Tensor, k: torch.Tensor, tau, g: Geometry, *, tile, sm_scale=None,
-           wmode=0, bits=False, max_only=False, wait_limit_ns=0, screen=False):
+           wmode=0, bits=False, max_only=False, wait_limit_ns=0, screen=False,
+           vote_hist=False):
     """Kernel A on raw (H,N,D) q and (Hkv,N,D) k.  Returns dict of compact votes / wvotes /
     bits, row_max (H,N) and row_count (H,N).  `wait_limit_ns` bounds every device-side wait
     (0: the library default); an expired wait shows in device_error(), not here.  With
     ``g.dca`` the selection geometry is Dual Chunk Attention (three rotated query planes).
     ``screen`` (unweighted modes) scores with one fp16 product per pair and exact rescoring of
     the pairs a proven bound leaves undecided (the forward entry points do so under
-    ``STA_SELECT_SCREEN=1``); the default scores every pair with three bf16 products."""
+    ``STA_SELECT_SCREEN=1``); the default scores every pair with three bf16 products.
+    ``vote_hist`` (tile 64 / 128) also returns each tile's histogram of nonzero votes."""
     H, N, D = q.shape
     Hk = k.shape[0]
     if sm_scale is None:
@@ -496,6 +498,10 @@ def select(q: torch.Tensor, k: torch.Tensor, tau, g: Geometry, *, tile, sm_scale
     a.row_count = res["row_count"].data_ptr()
     a.dca_chunk_len = dca_len
     a.wait_limit_ns = int(wait_limit_ns)
+    if vote_hist and not max_only and tile != 32:
+        res["vote_hist"] = torch.zeros((H, (N + tile - 1) // tile, tile + 1), dtype=torch.int32,
+                                       device=dev)
+        a.vote_hist = res["vote_hist"].data_ptr()
     scr = None
     if screen and not wmode:
         nb = int(L.lib().sta_select_screen_bytes(ctypes.byref(a)))

@@ -133,7 +133,7 @@ def test_synth_is_deterministic():
 
 
 def test_abi_version():
-    assert L.lib().sta_version() == 4
+    assert L.lib().sta_version() == 5
 
 
 def _static_args():

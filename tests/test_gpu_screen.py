@@ -94,3 +94,23 @@ def test_screened_dca_planes():
     np.testing.assert_allclose(a["row_max"].cpu().numpy(), b["row_max"].cpu().numpy(),
                                rtol=1e-5, atol=1e-5)
     assert int(np.abs(_votes(a, H, N, 64) - _votes(b, H, N, 64)).sum()) <= 2
+
+
+@pytest.mark.parametrize("T,screen", [(64, False), (128, False), (64, True)])
+def test_vote_histograms_match_votes(T, screen):
+    """Kernel A's per-tile histograms of nonzero votes (consumed by the shared-path selection in
+    place of a pass over the votes) equal a bincount of the votes it wrote."""
+    H, Hk, N, D = 4, 2, 1800, 128
+    q, k, _ = make_inputs(SynthSpec(n_heads=H, n_kv_heads=Hk, seq_len=N, head_dim=D, n_planted=8,
+                                    seed=21, dtype=torch.bfloat16))
+    res = core.select(cu(q[0]), cu(k[0]), torch.full((H,), 5.0), Geometry(rope_inv_freq(D, 1e4)),
+                      tile=T, vote_hist=True, screen=screen)
+    torch.cuda.synchronize()
+    v = _votes(res, H, N, T)
+    hist = res["vote_hist"].cpu().numpy()
+    nt = (N + T - 1) // T
+    for h in range(H):
+        for t in range(nt):
+            want = np.bincount(v[h, t][v[h, t] > 0], minlength=T + 1)
+            want[0] = 0
+            assert (hist[h, t] == want).all(), (h, t)
